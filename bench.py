@@ -1,0 +1,461 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 grammar-conditioned LM head.
+
+Headline workload (one GPU): batch-1 row-sparse (direct-bitmask) projection at
+V=248,320, H=2,048, fp16, W ~ N(0, 0.02), h ~ N(0, 1), 1% of the vocabulary
+legal (uniform), a fresh seeded mask every step. One step = one call of the
+hot path: full -inf-filled logits [V] plus the fused greedy top-1.
+
+  value      legal-row GB/s = legal W bytes (k * H * 2) per step / device time
+             per step, summed over ranks' work, timed with CUDA events;
+  e2e        the same metric through the C-ABI call with host buffers: the
+             step's mask and hidden state copied from pinned host memory, the
+             top-1 copied back, all inside the timed region;
+  roofline   the row-sparse kernel's achieved legal-row bandwidth against the
+             measured HBM copy bandwidth;
+  sweep      every density of the GEMV workload, uniform and clustered;
+  cpu_baseline  the oracle's CPU restatement of the same step on host cores.
+
+L2 is flushed (a 256 MiB write) before every timed step; the flush is outside
+the per-step events. With --gpus N (torchrun, one process per GPU) the head is
+vocabulary-parallel: each rank streams the legal rows of its V/N shard and the
+ranks merge the per-request top-1 with one NCCL integer-MAX all-reduce.
+
+`--impl reference` times the reference's CPU algorithm for the same step (the
+oracle port, all host threads) and prints its own line.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "grammar-sparse-projection_b200"))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "LM-head µs/step & legal-row HBM GB/s at V=248320 H=2048 fp16, batch 1-32"
+UNIT = "GB/s"
+VOCAB, HIDDEN = 248320, 2048
+DENSITIES = (0.0005, 0.005, 0.01, 0.10, 0.50, 1.0)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--density", type=float, default=0.01)
+    ap.add_argument("--pattern", choices=("uniform", "clustered"), default="uniform")
+    ap.add_argument("--masks", type=int, default=64, help="distinct seeded masks cycled through")
+    ap.add_argument("--sweep-steps", type=int, default=100)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def make_masks(n: int, density: float, pattern: str, seed: int) -> np.ndarray:
+    from oracle import gsp_oracle as O  # seeded generators only
+    rng = np.random.default_rng(seed)
+    k = int(round(density * VOCAB))
+    return np.concatenate([O.make_batch_mask(rng, 1, VOCAB, [k], clustered=(pattern == "clustered"),
+                                             max_runs=64) for _ in range(n)])
+
+
+def legal_counts(masks: np.ndarray) -> np.ndarray:
+    from oracle import gsp_oracle as O
+    return O.unpack_bitmask(masks, VOCAB).sum(axis=1)
+
+
+def read_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            peaks = json.load(f)
+        return float(peaks["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def read_profile_traffic(kernel: str):
+    """Per-launch DRAM traffic recorded from an ncu capture in profiles/."""
+    path = os.path.join(REPO, "profiles", f"{kernel}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML polling thread; read-only)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._handle = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._handle = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for name, bit in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                break
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._handle is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0, "source": "nvml unavailable"}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples),
+                "source": "nvml"}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: baseline and reference arm
+# ---------------------------------------------------------------------------
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        info = [i for i in threadpool_info() if i.get("user_api") == "blas"]
+        if info:
+            return int(max(i["num_threads"] for i in info))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def time_cpu_steps(weight_cpu: np.ndarray, hidden_cpu: np.ndarray, masks: np.ndarray, steps: int | None,
+                   seconds: float | None):
+    """Times oracle.cpu_row_sparse_step over cycling masks; returns (GB/s, µs/step, steps)."""
+    from oracle import gsp_oracle as O
+    counts = legal_counts(masks)
+    done, legal_bytes, t0 = 0, 0, time.perf_counter()
+    while True:
+        m = masks[done % len(masks)][None]
+        O.cpu_row_sparse_step(hidden_cpu, weight_cpu, m, VOCAB)
+        legal_bytes += int(counts[done % len(masks)]) * HIDDEN * 2
+        done += 1
+        el = time.perf_counter() - t0
+        if steps is not None and done >= steps:
+            break
+        if seconds is not None and el >= seconds and done >= 3:
+            break
+    el = time.perf_counter() - t0
+    return legal_bytes / el / 1e9, el / done * 1e6, done
+
+
+def host_weight(seed: int) -> tuple[np.ndarray, np.ndarray]:
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn(VOCAB, HIDDEN, generator=g) * 0.02).half().numpy()
+    h = torch.randn(1, HIDDEN, generator=g).half().numpy()
+    return w, h
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    masks = make_masks(args.masks, args.density, args.pattern, seed=100)
+    w, h = host_weight(1234)
+    time_cpu_steps(w, h, masks, steps=max(args.warmup, 1), seconds=None)
+    gbs, us, n = time_cpu_steps(w, h, masks, steps=args.steps, seconds=None)
+    sample = (f"{n} steps of the batch-1 row-sparse step (mask decode, legal-row gather, fp32 dots, "
+              f"-inf fill, argmax) at V={VOCAB}, H={HIDDEN}, {args.density:.2%} {args.pattern}")
+    line = {
+        "metric": METRIC, "value": gbs, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3, "us_per_step": us,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": gbs, "unit": UNIT, "cores": cpu_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": gbs, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args):
+    return {"workload": "batch-1 row-sparse direct-bitmask LM-head GEMV", "vocab": VOCAB, "hidden": HIDDEN,
+            "batch": 1, "density": args.density, "mask": f"{args.pattern}, fresh seeded mask per step",
+            "weight": "fp16 N(0,0.02) row-major [V,H]", "outputs": "full logits [V] + fused top-1",
+            "l2": "flushed before every step (256 MiB write), flush outside the step events",
+            "parallelism": f"vocab-parallel x{args.gpus}" if args.gpus > 1 else "single GPU"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    from gsp import _native
+    from gsp import vocab_parallel as vp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    lo, hi = vp.shard_bounds(VOCAB, world, rank)
+
+    # weight shard, hidden state and seeded masks (identical on every rank)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    weight = (torch.randn(hi - lo, HIDDEN, device=dev, generator=g) * 0.02).half()
+    hidden = torch.randn(1, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(99)).half()
+    masks_np = make_masks(args.masks, args.density, args.pattern, seed=100)
+    counts = legal_counts(masks_np)
+    masks = torch.from_numpy(masks_np).to(dev)
+    local_masks = masks[:, lo // 32:(hi + 31) // 32]
+    local_counts = legal_counts_local(masks_np, lo, hi)
+
+    logits = torch.empty(1, hi - lo, device=dev, dtype=torch.float16)
+    top_value = torch.empty(1, device=dev, dtype=torch.float32)
+    top_index = torch.empty(1, device=dev, dtype=torch.int64)
+    top_key = torch.empty(1, device=dev, dtype=torch.int64)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step(i, mask_rows=local_masks):
+        m = mask_rows[i % args.masks][None]
+        if world == 1:
+            _native.row_sparse(hidden, weight, m, logits=logits, top_value=top_value, top_index=top_index)
+        else:
+            _native.row_sparse(hidden, weight, m, logits=logits, top_key=top_key, vocab_offset=lo)
+            vp.merge_top1_keys(top_key, group)
+            _native.top1_from_keys(top_key, top_value, top_index)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def timed(n, fn, offset):
+        ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for i in range(n):
+            flush.zero_()
+            ev0[i].record()
+            fn(offset + i)
+            ev1[i].record()
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) * 1e3 for a, b in zip(ev0, ev1)]  # µs
+
+    # warm-up (untimed)
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    barrier()
+    sampler = ClockSampler(local_rank)
+    with sampler:
+        t_wall = time.perf_counter()
+        per_step = timed(args.steps, step, 0)
+        barrier()
+        t_wall = time.perf_counter() - t_wall
+    total_us = sum(per_step)
+    total_us = max_over_ranks(total_us, world)
+    steps_idx = [i % args.masks for i in range(args.steps)]
+    legal_bytes = float(sum(int(counts[j]) for j in steps_idx)) * HIDDEN * 2
+    value = legal_bytes / (total_us * 1e-6) / 1e9
+    us_per_step = total_us / args.steps
+
+    # e2e through the C ABI with host buffers
+    pinned_masks = torch.from_numpy(np.ascontiguousarray(masks_np[:, lo // 32:(hi + 31) // 32])).pin_memory()
+    pinned_hidden = hidden.cpu().pin_memory()
+    host_top = torch.empty(2, dtype=torch.int64).pin_memory()
+    dev_mask = torch.empty(1, pinned_masks.shape[1], dtype=torch.int32, device=dev)
+    dev_hidden = torch.empty_like(hidden)
+
+    def e2e_step(i):
+        dev_mask.copy_(pinned_masks[i % args.masks][None], non_blocking=True)
+        dev_hidden.copy_(pinned_hidden, non_blocking=True)
+        if world == 1:
+            _native.row_sparse(dev_hidden, weight, dev_mask, logits=logits, top_value=top_value,
+                               top_index=top_index)
+        else:
+            _native.row_sparse(dev_hidden, weight, dev_mask, logits=logits, top_key=top_key, vocab_offset=lo)
+            vp.merge_top1_keys(top_key, group)
+            _native.top1_from_keys(top_key, top_value, top_index)
+        host_top[0:1].copy_(top_index, non_blocking=True)
+        host_top[1:2].view(torch.float32)[:1].copy_(top_value, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    barrier()
+    e2e_steps = timed(args.steps, e2e_step, 0)
+    barrier()
+    e2e_total = max_over_ranks(sum(e2e_steps), world)
+    e2e_value = legal_bytes / (e2e_total * 1e-6) / 1e9
+    h2d = int(pinned_masks[0].numel() * 4 + pinned_hidden.numel() * 2)
+    d2h = int(top_index.numel() * 8 + top_value.numel() * 4)
+
+    # roofline of the row-sparse kernel (rank 0's shard at N > 1)
+    local_bytes = float(sum(int(local_counts[j]) for j in steps_idx)) * HIDDEN * 2
+    kernel_us = statistics.mean(per_step) if world == 1 else None
+    peak, peak_src = read_peaks()
+    algo_per_launch = local_bytes / args.steps
+    if world == 1:
+        achieved = algo_per_launch / (kernel_us * 1e-6) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": read_profile_traffic("row_sparse_gemv"),
+                    "kernel": "row_sparse_kernel", "algorithmic_bytes_per_launch": algo_per_launch,
+                    "peak_source": peak_src, "avg_launch_us": kernel_us,
+                    "all_bytes_per_launch": algo_per_launch + (VOCAB // 32) * 4 + HIDDEN * 2 + VOCAB * 2}
+    else:
+        roofline = None
+
+    sweep = None
+    same_gpu_dense = None
+    cpu_base = None
+    if world == 1 and not args.no_sweep:
+        sweep = []
+        for pattern in ("uniform", "clustered"):
+            for d in DENSITIES:
+                mk_np = make_masks(16, d, pattern, seed=200)
+                mk = torch.from_numpy(mk_np).to(dev)
+                cnt = legal_counts(mk_np)
+                n = args.sweep_steps
+                for i in range(3):
+                    step(i, mk)
+                ts = timed(n, lambda i: step(i, mk), 0)
+                lb = float(sum(int(cnt[i % 16]) for i in range(n))) * HIDDEN * 2
+                sweep.append({"density": d, "pattern": pattern, "us_per_step": statistics.mean(ts),
+                              "us_p50": statistics.median(ts), "legal_gbs": lb / (sum(ts) * 1e-6) / 1e9,
+                              "frac_of_hbm": lb / (sum(ts) * 1e-6) / 1e9 / peak})
+        same_gpu_dense = time_dense_baseline(dev, weight, hidden, masks, args)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        w_cpu = weight.cpu().numpy()
+        h_cpu = hidden.cpu().numpy()
+        gbs, us, n = time_cpu_steps(w_cpu, h_cpu, masks_np, steps=None, seconds=args.cpu_seconds)
+        cpu_base = {"value": gbs, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                    "sample": f"{n} CPU steps ({us:.0f} us/step) of the same batch-1 1% workload, "
+                              f"bounded to {args.cpu_seconds:.0f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": us_per_step / 1e3, "us_per_step": us_per_step,
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": workload_config(args),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "us_per_step": e2e_total / args.steps},
+            "gpu_launches": args.steps * (1 if world == 1 else 2),
+            "roofline": roofline,
+            "cpu_baseline": cpu_base,
+            "clocks": sampler.summary(),
+            "timed_region_wall_s": t_wall,
+            "sweep": sweep,
+            "same_gpu_dense_mask": same_gpu_dense,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def legal_counts_local(masks_np: np.ndarray, lo: int, hi: int) -> np.ndarray:
+    from oracle import gsp_oracle as O
+    return O.unpack_bitmask(masks_np, VOCAB)[:, lo:hi].sum(axis=1)
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_dense_baseline(dev, weight, hidden, masks, args):
+    """Same-GPU dense LM head + mask as the reference's dense route runs it:
+    cuBLAS (F.linear) then xgrammar's Triton mask kernel."""
+    try:
+        import xgrammar as xgr
+        import torch.nn.functional as F
+    except Exception as exc:  # pragma: no cover - optional comparison
+        return {"unavailable": str(exc)}
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def dense(i):
+        lg = F.linear(hidden, weight)
+        xgr.apply_token_bitmask_inplace(lg, masks[i % masks.shape[0]][None], vocab_size=VOCAB, backend="triton")
+        return lg
+
+    try:
+        for i in range(3):
+            dense(i)
+        torch.cuda.synchronize()
+        ts = []
+        for i in range(50):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            dense(i)
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return {"us_per_step": statistics.median(ts), "what": "F.linear (cuBLAS) + xgrammar triton mask, batch 1"}
+    except Exception as exc:  # pragma: no cover
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,330 @@
+// extern "C" entry points declared in include/gsp_b200.h: argument validation,
+// workspace carving and dispatch to the kernel launchers. No exception, abort
+// or host synchronisation happens here.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/gsp_b200.h"
+#include "gsp_internal.h"
+
+namespace gsp {
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int32_t fail(int32_t code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int32_t cuda_status(cudaError_t err, const char* where) {
+  if (err == cudaSuccess) return GSP_OK;
+  return fail(GSP_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorName(err), cudaGetErrorString(err));
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+constexpr int kBuilderTiles = 256;  // tiles per active-tile builder block
+
+}  // namespace
+
+int tile_builder_blocks(int vocab) {
+  const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
+  return (ntiles + kBuilderTiles - 1) / kBuilderTiles;
+}
+
+size_t workspace_bytes(int batch, int vocab) {
+  const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
+  return align256(sizeof(unsigned long long) * (size_t)batch + 8) +
+         align256(sizeof(int32_t) * (size_t)ntiles) +
+         align256(sizeof(int32_t) * (size_t)tile_builder_blocks(vocab));
+}
+
+Workspace carve_workspace(void* base, int batch, int vocab) {
+  const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
+  char* p = static_cast<char*>(base);
+  Workspace w;
+  w.keys = reinterpret_cast<unsigned long long*>(p);
+  w.ticket = reinterpret_cast<unsigned int*>(p + sizeof(unsigned long long) * (size_t)batch);
+  p += align256(sizeof(unsigned long long) * (size_t)batch + 8);
+  w.tile_list = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * (size_t)ntiles);
+  w.tile_counts = reinterpret_cast<int32_t*>(p);
+  return w;
+}
+
+int num_sms(int device) {
+  static int cache[128] = {0};
+  if (device < 0 || device >= 128) return 148;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+namespace {
+
+// Checks shared by every projection entry point.
+int32_t validate_projection(const char* fn, const void* hidden, int64_t hidden_row_stride,
+                            const void* weight, int64_t weight_row_stride, const int32_t* bitmask,
+                            int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                            int32_t hidden_dim, int32_t dtype, const void* logits,
+                            int64_t logits_row_stride) {
+  if (!hidden || !weight) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: hidden and weight must be non-null", fn);
+  if (batch < 1 || vocab < 1 || hidden_dim < 1)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: batch, vocab and hidden_dim must be positive", fn);
+  if (dtype != GSP_DTYPE_F16 && dtype != GSP_DTYPE_BF16)
+    return fail(GSP_ERR_UNSUPPORTED, "%s: dtype must be GSP_DTYPE_F16 or GSP_DTYPE_BF16", fn);
+  if (batch > 1 && hidden_row_stride < hidden_dim)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: hidden_row_stride < hidden_dim", fn);
+  if (vocab > 1 && weight_row_stride < hidden_dim)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: weight_row_stride < hidden_dim", fn);
+  const int64_t nw = (vocab + 31) / 32;
+  if (bitmask && batch > 1 && bitmask_row_stride != 0 && bitmask_row_stride < nw)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask_row_stride must be 0 or >= ceil(vocab/32)", fn);
+  if (bitmask_row_stride < 0) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: negative bitmask_row_stride", fn);
+  if (logits && batch > 1 && logits_row_stride < vocab)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: logits_row_stride < vocab", fn);
+  if ((uint64_t)batch * (uint64_t)nw * 32ull > 0xffffffffull)
+    return fail(GSP_ERR_UNSUPPORTED, "%s: batch * vocab too large (limit 2^32 tokens)", fn);
+  return GSP_OK;
+}
+
+int32_t check_workspace(const char* fn, bool needed, void* workspace, size_t bytes, int32_t batch,
+                        int32_t vocab) {
+  if (!needed) return GSP_OK;
+  if (!workspace) return fail(GSP_ERR_WORKSPACE, "%s: workspace is required for this call", fn);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(GSP_ERR_WORKSPACE, "%s: workspace must be 256-byte aligned", fn);
+  const size_t need = workspace_bytes(batch, vocab);
+  if (bytes < need)
+    return fail(GSP_ERR_WORKSPACE, "%s: workspace has %zu bytes, needs %zu", fn, bytes, need);
+  return GSP_OK;
+}
+
+RowSparseParams make_row_sparse(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                                int64_t weight_row_stride, const int32_t* bitmask,
+                                int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                                int32_t hidden_dim, int64_t vocab_offset) {
+  RowSparseParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.hidden = hidden;
+  p.hidden_stride = batch > 1 ? hidden_row_stride : hidden_dim;
+  p.weight = weight;
+  p.weight_stride = vocab > 1 ? weight_row_stride : hidden_dim;
+  p.mask = reinterpret_cast<const uint32_t*>(bitmask);
+  p.mask_stride = batch > 1 ? bitmask_row_stride : 0;
+  p.batch = batch;
+  p.vocab = vocab;
+  p.hidden_dim = hidden_dim;
+  p.nw = (vocab + 31) / 32;
+  p.vocab_offset = vocab_offset;
+  return p;
+}
+
+int32_t projection_common(const char* fn, bool tensor_core, int dense, const void* hidden,
+                          int64_t hidden_row_stride, const void* weight, int64_t weight_row_stride,
+                          const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch,
+                          int32_t vocab, int32_t hidden_dim, int32_t dtype, int64_t vocab_offset,
+                          void* logits, int64_t logits_row_stride, float* top_value,
+                          int64_t* top_index, int64_t* top_key, void* workspace,
+                          size_t workspace_bytes_, void* stream) {
+  int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                   bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits,
+                                   logits_row_stride);
+  if (st != GSP_OK) return st;
+  const bool want_top = top_value || top_index || top_key;
+  st = check_workspace(fn, want_top || tensor_core, workspace, workspace_bytes_, batch, vocab);
+  if (st != GSP_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!tensor_core) {
+    RowSparseParams p = make_row_sparse(hidden, hidden_row_stride, weight, weight_row_stride,
+                                        bitmask, bitmask_row_stride, batch, vocab, hidden_dim,
+                                        vocab_offset);
+    p.logits = logits;
+    p.logits_stride = batch > 1 ? logits_row_stride : vocab;
+    p.top_value = top_value;
+    p.top_index = top_index;
+    p.top_key = top_key;
+    if (want_top) {
+      Workspace w = carve_workspace(workspace, batch, vocab);
+      p.keys = w.keys;
+      p.ticket = w.ticket;
+    }
+    return cuda_status(launch_row_sparse(p, dtype, s), fn);
+  }
+  BlockGemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.hidden = hidden;
+  p.hidden_stride = batch > 1 ? hidden_row_stride : hidden_dim;
+  p.weight = weight;
+  p.weight_stride = vocab > 1 ? weight_row_stride : hidden_dim;
+  p.mask = reinterpret_cast<const uint32_t*>(bitmask);
+  p.mask_stride = batch > 1 ? bitmask_row_stride : 0;
+  p.batch = batch;
+  p.vocab = vocab;
+  p.hidden_dim = hidden_dim;
+  p.nw = (vocab + 31) / 32;
+  p.vocab_offset = vocab_offset;
+  p.logits = logits;
+  p.logits_stride = batch > 1 ? logits_row_stride : vocab;
+  p.top_value = top_value;
+  p.top_index = top_index;
+  p.top_key = top_key;
+  Workspace w = carve_workspace(workspace, batch, vocab);
+  p.keys = w.keys;
+  p.ticket = w.ticket;
+  p.tile_list = w.tile_list;
+  p.tile_counts = w.tile_counts;
+  p.dense = dense || bitmask == nullptr;
+  return cuda_status(launch_block_gemm(p, dtype, s), fn);
+}
+
+}  // namespace
+}  // namespace gsp
+
+using namespace gsp;
+
+extern "C" {
+
+int32_t gsp_abi_version(void) { return GSP_ABI_VERSION; }
+
+const char* gsp_status_string(int32_t status) {
+  switch (status) {
+    case GSP_OK: return "GSP_OK";
+    case GSP_ERR_INVALID_ARGUMENT: return "GSP_ERR_INVALID_ARGUMENT";
+    case GSP_ERR_UNSUPPORTED: return "GSP_ERR_UNSUPPORTED";
+    case GSP_ERR_WORKSPACE: return "GSP_ERR_WORKSPACE";
+    case GSP_ERR_CUDA: return "GSP_ERR_CUDA";
+    default: return "GSP_ERR_UNKNOWN";
+  }
+}
+
+const char* gsp_last_error(void) { return g_last_error; }
+
+size_t gsp_workspace_bytes(int32_t batch, int32_t vocab) {
+  if (batch < 1 || vocab < 1) return 0;
+  return workspace_bytes(batch, vocab);
+}
+
+int32_t gsp_row_sparse_logits(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                              int64_t weight_row_stride, const int32_t* bitmask,
+                              int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                              int32_t hidden_dim, int32_t dtype, int64_t vocab_offset, void* logits,
+                              int64_t logits_row_stride, float* top_value, int64_t* top_index,
+                              int64_t* top_key, void* workspace, size_t workspace_bytes_,
+                              void* stream) {
+  return projection_common("gsp_row_sparse_logits", false, 0, hidden, hidden_row_stride, weight,
+                           weight_row_stride, bitmask, bitmask_row_stride, batch, vocab, hidden_dim,
+                           dtype, vocab_offset, logits, logits_row_stride, top_value, top_index,
+                           top_key, workspace, workspace_bytes_, stream);
+}
+
+int32_t gsp_row_sparse_compact(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                               int64_t weight_row_stride, const int32_t* bitmask,
+                               int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                               int32_t hidden_dim, int32_t dtype, int64_t vocab_offset,
+                               void* compact_logits, int64_t* compact_ids, int64_t capacity,
+                               int64_t* request_offsets, float* top_value, int64_t* top_index,
+                               int64_t* top_key, void* workspace, size_t workspace_bytes_,
+                               void* stream) {
+  const char* fn = "gsp_row_sparse_compact";
+  int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                   bitmask_row_stride, batch, vocab, hidden_dim, dtype, nullptr, 0);
+  if (st != GSP_OK) return st;
+  if (capacity < 0) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: negative capacity", fn);
+  if (capacity > 0 && (!compact_logits || !compact_ids))
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: compact_logits and compact_ids are required", fn);
+  if (!request_offsets) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: request_offsets is required", fn);
+  const bool want_top = top_value || top_index || top_key;
+  st = check_workspace(fn, want_top, workspace, workspace_bytes_, batch, vocab);
+  if (st != GSP_OK) return st;
+  RowSparseParams p = make_row_sparse(hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                      bitmask_row_stride, batch, vocab, hidden_dim, vocab_offset);
+  p.compact = capacity > 0 ? compact_logits : nullptr;
+  p.compact_ids = compact_ids;
+  p.capacity = capacity;
+  p.offsets = request_offsets;
+  p.top_value = top_value;
+  p.top_index = top_index;
+  p.top_key = top_key;
+  if (want_top) {
+    Workspace w = carve_workspace(workspace, batch, vocab);
+    p.keys = w.keys;
+    p.ticket = w.ticket;
+  }
+  return cuda_status(launch_row_sparse(p, dtype, static_cast<cudaStream_t>(stream)), fn);
+}
+
+int32_t gsp_ids_to_bitmask(const int64_t* ids, int64_t count, int32_t vocab, int32_t* bitmask,
+                           int64_t* stats, void* stream) {
+  const char* fn = "gsp_ids_to_bitmask";
+  if (vocab < 1) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: vocab must be positive", fn);
+  if (count < 0 || (count > 0 && !ids)) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bad ids", fn);
+  if (!bitmask || !stats) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask and stats are required", fn);
+  return cuda_status(launch_ids_to_bitmask(ids, count, vocab, reinterpret_cast<uint32_t*>(bitmask),
+                                           reinterpret_cast<unsigned long long*>(stats),
+                                           static_cast<cudaStream_t>(stream)),
+                     fn);
+}
+
+int32_t gsp_mask_stats(const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch,
+                       int32_t vocab, int32_t* legal_counts, int32_t* full_words,
+                       int32_t* active_tiles, void* stream) {
+  const char* fn = "gsp_mask_stats";
+  if (!bitmask) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask is required", fn);
+  if (batch < 1 || vocab < 1) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: batch and vocab must be positive", fn);
+  const int64_t nw = (vocab + 31) / 32;
+  if (batch > 1 && bitmask_row_stride != 0 && bitmask_row_stride < nw)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask_row_stride must be 0 or >= ceil(vocab/32)", fn);
+  if (bitmask_row_stride < 0) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: negative bitmask_row_stride", fn);
+  return cuda_status(launch_mask_stats(reinterpret_cast<const uint32_t*>(bitmask),
+                                       batch > 1 ? bitmask_row_stride : 0, batch, vocab,
+                                       legal_counts, full_words, active_tiles,
+                                       static_cast<cudaStream_t>(stream)),
+                     fn);
+}
+
+int32_t gsp_block_gemm_logits(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                              int64_t weight_row_stride, const int32_t* bitmask,
+                              int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                              int32_t hidden_dim, int32_t dtype, int64_t vocab_offset, void* logits,
+                              int64_t logits_row_stride, float* top_value, int64_t* top_index,
+                              int64_t* top_key, void* workspace, size_t workspace_bytes_,
+                              void* stream) {
+  return projection_common("gsp_block_gemm_logits", true, 0, hidden, hidden_row_stride, weight,
+                           weight_row_stride, bitmask, bitmask_row_stride, batch, vocab, hidden_dim,
+                           dtype, vocab_offset, logits, logits_row_stride, top_value, top_index,
+                           top_key, workspace, workspace_bytes_, stream);
+}
+
+int32_t gsp_dense_masked_logits(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                                int64_t weight_row_stride, const int32_t* bitmask,
+                                int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                                int32_t hidden_dim, int32_t dtype, int64_t vocab_offset,
+                                void* logits, int64_t logits_row_stride, float* top_value,
+                                int64_t* top_index, int64_t* top_key, void* workspace,
+                                size_t workspace_bytes_, void* stream) {
+  return projection_common("gsp_dense_masked_logits", true, 1, hidden, hidden_row_stride, weight,
+                           weight_row_stride, bitmask, bitmask_row_stride, batch, vocab, hidden_dim,
+                           dtype, vocab_offset, logits, logits_row_stride, top_value, top_index,
+                           top_key, workspace, workspace_bytes_, stream);
+}
+
+int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value, int64_t* top_index,
+                           void* stream) {
+  const char* fn = "gsp_top1_from_keys";
+  if (!keys || batch < 1) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: keys and batch are required", fn);
+  return cuda_status(
+      launch_top1_from_keys(keys, batch, top_value, top_index, static_cast<cudaStream_t>(stream)),
+      fn);
+}
+
+}  // extern "C"

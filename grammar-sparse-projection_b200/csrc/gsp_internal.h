@@ -1,0 +1,91 @@
+// Internal launch interfaces shared by the kernel translation units and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gsp {
+
+// Parameters of the row-sparse kernel (one launch covers every request).
+struct RowSparseParams {
+  const void* hidden;
+  int64_t hidden_stride;
+  const void* weight;
+  int64_t weight_stride;
+  const uint32_t* mask;  // nullptr: every token legal
+  int64_t mask_stride;   // words; 0 broadcasts row 0
+  int batch;
+  int vocab;
+  int hidden_dim;
+  int nw;  // ceil(vocab / 32)
+  int64_t vocab_offset;
+  // full logits [batch, vocab] (optional)
+  void* logits;
+  int64_t logits_stride;
+  // compact output (optional)
+  void* compact;
+  int64_t* compact_ids;
+  int64_t capacity;
+  int64_t* offsets;  // [batch + 1]
+  // top-1 (optional; all three may be null)
+  float* top_value;
+  int64_t* top_index;
+  int64_t* top_key;
+  // workspace: per-request keys + arrival ticket (zero on entry and exit)
+  unsigned long long* keys;
+  unsigned int* ticket;
+};
+
+// Parameters of the tensor-core block / dense projection.
+struct BlockGemmParams {
+  const void* hidden;
+  int64_t hidden_stride;
+  const void* weight;
+  int64_t weight_stride;
+  const uint32_t* mask;  // nullptr: every token legal
+  int64_t mask_stride;
+  int batch;
+  int vocab;
+  int hidden_dim;
+  int nw;
+  int64_t vocab_offset;
+  void* logits;
+  int64_t logits_stride;
+  float* top_value;
+  int64_t* top_index;
+  int64_t* top_key;
+  unsigned long long* keys;
+  unsigned int* ticket;
+  int32_t* tile_list;     // workspace: compacted active tile ids
+  int32_t* tile_counts;   // workspace: per-builder-block active tile counts
+  int dense;              // 1: every tile is projected (dense_masked_logits)
+};
+
+struct Workspace {
+  unsigned long long* keys;
+  unsigned int* ticket;
+  int32_t* tile_list;
+  int32_t* tile_counts;
+};
+
+size_t workspace_bytes(int batch, int vocab);
+Workspace carve_workspace(void* base, int batch, int vocab);
+
+int num_sms(int device);
+
+// Each launcher returns a cudaError_t value (cudaSuccess == 0).
+cudaError_t launch_row_sparse(const RowSparseParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_ids_to_bitmask(const int64_t* ids, int64_t count, int vocab, uint32_t* mask,
+                                  unsigned long long* stats, cudaStream_t stream);
+cudaError_t launch_mask_stats(const uint32_t* mask, int64_t stride, int batch, int vocab,
+                              int32_t* legal_counts, int32_t* full_words, int32_t* active_tiles,
+                              cudaStream_t stream);
+cudaError_t launch_top1_from_keys(const int64_t* keys, int batch, float* top_value,
+                                  int64_t* top_index, cudaStream_t stream);
+cudaError_t launch_block_gemm(const BlockGemmParams& p, int dtype, cudaStream_t stream);
+
+// Number of builder blocks used by the active-tile builder for `vocab`.
+int tile_builder_blocks(int vocab);
+
+}  // namespace gsp

@@ -1,0 +1,152 @@
+// Bitmask utilities: token-id list -> bitmask, per-request density statistics,
+// and top-1 key decoding.
+#include "gsp_common.cuh"
+#include "gsp_internal.h"
+
+namespace gsp {
+namespace {
+
+// ids -> packed LSB-first bitmask (gsp/runtime.py:35-43: range check, dedup and
+// sort are all implied by setting bits). stats[0] counts ids whose bit was
+// newly set (distinct ids), stats[1] ids outside [0, vocab).
+__global__ void ids_to_bitmask_kernel(const int64_t* __restrict__ ids, int64_t count, int vocab,
+                                      uint32_t* __restrict__ mask,
+                                      unsigned long long* __restrict__ stats) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  unsigned fresh = 0, bad = 0;
+  if (i < count) {
+    const int64_t id = ids[i];
+    if (id < 0 || id >= vocab) {
+      bad = 1;
+    } else {
+      const uint32_t bit = 1u << (uint32_t)(id & 31);
+      const uint32_t old = atomicOr(mask + (id >> 5), bit);
+      fresh = (old & bit) ? 0u : 1u;
+    }
+  }
+  const unsigned nf = __reduce_add_sync(FULL_MASK, fresh);
+  const unsigned nb = __reduce_add_sync(FULL_MASK, bad);
+  if ((threadIdx.x & 31) == 0) {
+    if (nf) atomicAdd(stats + 0, (unsigned long long)nf);
+    if (nb) atomicAdd(stats + 1, (unsigned long long)nb);
+  }
+}
+
+constexpr int kStatThreads = 256;
+constexpr int kWordsPerThread = 4;
+
+// Per request: legal tokens (popcount, bits >= vocab ignored) and full words
+// (word == -1, the signal of gsp/triton_runtime.py:319).
+__global__ void request_stats_kernel(const uint32_t* __restrict__ mask, int64_t stride, int vocab,
+                                     int nw, int32_t* legal_counts, int32_t* full_words) {
+  const int b = blockIdx.y;
+  const int w0 = (blockIdx.x * kStatThreads + threadIdx.x) * kWordsPerThread;
+  int legal = 0, full = 0;
+#pragma unroll
+  for (int j = 0; j < kWordsPerThread; ++j) {
+    const int w = w0 + j;
+    if (w < nw) {
+      const uint32_t word = __ldg(mask + (int64_t)b * stride + w);
+      legal += __popc(tail_clip(word, w, vocab));
+      full += (word == 0xffffffffu);
+    }
+  }
+  legal = __reduce_add_sync(FULL_MASK, legal);
+  full = __reduce_add_sync(FULL_MASK, full);
+  __shared__ int s_legal[kStatThreads / 32], s_full[kStatThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { s_legal[warp] = legal; s_full[warp] = full; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int a = 0, f = 0;
+    for (int i = 0; i < kStatThreads / 32; ++i) { a += s_legal[i]; f += s_full[i]; }
+    if (legal_counts && a) atomicAdd(legal_counts + b, a);
+    if (full_words && f) atomicAdd(full_words + b, f);
+  }
+}
+
+// Tiles of 128 rows (4 words) with any legal token in any request.
+__global__ void active_tile_count_kernel(const uint32_t* __restrict__ mask, int64_t stride,
+                                         int batch, int vocab, int nw, int ntiles,
+                                         int32_t* active_tiles) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  int active = 0;
+  if (t < ntiles) {
+    uint32_t any = 0;
+    for (int b = 0; b < batch && !any; ++b) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int w = t * 4 + j;
+        if (w < nw) any |= tail_clip(__ldg(mask + (int64_t)b * stride + w), w, vocab);
+      }
+    }
+    active = any != 0;
+  }
+  active = __reduce_add_sync(FULL_MASK, active);
+  if ((threadIdx.x & 31) == 0 && active) atomicAdd(active_tiles, active);
+}
+
+__global__ void top1_from_keys_kernel(const int64_t* __restrict__ keys, int batch,
+                                      float* top_value, int64_t* top_index) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const unsigned long long k = key_from_signed(keys[b]);
+  if (top_value) top_value[b] = key_value(k);
+  if (top_index) top_index[b] = key_index(k);
+}
+
+}  // namespace
+
+cudaError_t launch_ids_to_bitmask(const int64_t* ids, int64_t count, int vocab, uint32_t* mask,
+                                  unsigned long long* stats, cudaStream_t stream) {
+  const int nw = (vocab + 31) / 32;
+  cudaError_t err = cudaMemsetAsync(mask, 0, sizeof(uint32_t) * (size_t)nw, stream);
+  if (err != cudaSuccess) return err;
+  err = cudaMemsetAsync(stats, 0, 2 * sizeof(unsigned long long), stream);
+  if (err != cudaSuccess) return err;
+  if (count == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks = (count + threads - 1) / threads;
+  ids_to_bitmask_kernel<<<(unsigned)blocks, threads, 0, stream>>>(ids, count, vocab, mask, stats);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mask_stats(const uint32_t* mask, int64_t stride, int batch, int vocab,
+                              int32_t* legal_counts, int32_t* full_words, int32_t* active_tiles,
+                              cudaStream_t stream) {
+  const int nw = (vocab + 31) / 32;
+  cudaError_t err;
+  if (legal_counts) {
+    err = cudaMemsetAsync(legal_counts, 0, sizeof(int32_t) * batch, stream);
+    if (err != cudaSuccess) return err;
+  }
+  if (full_words) {
+    err = cudaMemsetAsync(full_words, 0, sizeof(int32_t) * batch, stream);
+    if (err != cudaSuccess) return err;
+  }
+  if (legal_counts || full_words) {
+    dim3 grid((nw + kStatThreads * kWordsPerThread - 1) / (kStatThreads * kWordsPerThread), batch);
+    request_stats_kernel<<<grid, kStatThreads, 0, stream>>>(mask, stride, vocab, nw, legal_counts,
+                                                            full_words);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+  }
+  if (active_tiles) {
+    err = cudaMemsetAsync(active_tiles, 0, sizeof(int32_t), stream);
+    if (err != cudaSuccess) return err;
+    const int ntiles = (vocab + 127) / 128;
+    active_tile_count_kernel<<<(ntiles + 255) / 256, 256, 0, stream>>>(mask, stride, batch, vocab,
+                                                                       nw, ntiles, active_tiles);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_top1_from_keys(const int64_t* keys, int batch, float* top_value,
+                                  int64_t* top_index, cudaStream_t stream) {
+  top1_from_keys_kernel<<<(batch + 127) / 128, 128, 0, stream>>>(keys, batch, top_value, top_index);
+  return cudaGetLastError();
+}
+
+}  // namespace gsp

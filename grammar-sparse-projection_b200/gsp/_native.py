@@ -1,0 +1,211 @@
+"""ctypes binding of libgsp_b200.so, the C ABI declared in include/gsp_b200.h.
+
+This is the only route from Python to the device: there is no Triton, no
+PyTorch compute fallback and no CPU path. If the library is missing, or a
+tensor is not on a CUDA device, calls raise instead of computing elsewhere.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libgsp_b200.so")
+
+GSP_OK = 0
+GSP_ERR_INVALID_ARGUMENT = -1
+GSP_ERR_UNSUPPORTED = -2
+GSP_ERR_WORKSPACE = -3
+GSP_ERR_CUDA = -4
+TILE_ROWS = 128
+
+DTYPE_CODES = {torch.float16: 0, torch.bfloat16: 1}
+
+
+class GSPNativeError(RuntimeError):
+    """A C-ABI call returned an error status."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_sz = ctypes.c_size_t
+
+_PROJECTION_ARGS = [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
+                    _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]
+
+SIGNATURES = {
+    "gsp_abi_version": ([], _i32),
+    "gsp_status_string": ([_i32], ctypes.c_char_p),
+    "gsp_last_error": ([], ctypes.c_char_p),
+    "gsp_workspace_bytes": ([_i32, _i32], _sz),
+    "gsp_row_sparse_logits": (_PROJECTION_ARGS, _i32),
+    "gsp_row_sparse_compact": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
+                                _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp], _i32),
+    "gsp_ids_to_bitmask": ([_vp, _i64, _i32, _vp, _vp, _vp], _i32),
+    "gsp_mask_stats": ([_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp], _i32),
+    "gsp_block_gemm_logits": (_PROJECTION_ARGS, _i32),
+    "gsp_dense_masked_logits": (_PROJECTION_ARGS, _i32),
+    "gsp_top1_from_keys": ([_vp, _i32, _vp, _vp, _vp], _i32),
+}
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise loudly if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"libgsp_b200.so is not built (expected at {LIB_PATH}); run "
+                    "`python grammar-sparse-projection_b200/build.py` or __graft_entry__.build()")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (args, res) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = lib
+    return _lib
+
+
+def _check(status: int, fn: str) -> None:
+    if status != GSP_OK:
+        lib = load()
+        msg = lib.gsp_last_error().decode(errors="replace")
+        name = lib.gsp_status_string(status).decode()
+        raise GSPNativeError(status, f"{fn} failed with {name}: {msg}")
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dtype}: the B200 kernels take float16 or bfloat16") from None
+
+
+# ---------------------------------------------------------------------------
+# workspace: one zero-initialised buffer per (device, stream); every kernel
+# leaves it zeroed again, so stream order makes reuse safe.
+# ---------------------------------------------------------------------------
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_ws_lock = threading.Lock()
+
+
+def workspace(device: torch.device, batch: int, vocab: int) -> torch.Tensor:
+    need = int(load().gsp_workspace_bytes(batch, vocab))
+    dev_index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (dev_index, torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < need:
+            size = max(need, 64 * 1024, 0 if ws is None else 2 * ws.numel())
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise ValueError("GSP B200 kernels take CUDA tensors only (no CPU path)")
+
+
+# ---------------------------------------------------------------------------
+# thin wrappers over the entry points (no validation beyond what the C ABI does)
+# ---------------------------------------------------------------------------
+def _projection(entry: str, hidden: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor | None,
+                logits: torch.Tensor | None, top_value: torch.Tensor | None,
+                top_index: torch.Tensor | None, top_key: torch.Tensor | None,
+                vocab_offset: int = 0) -> None:
+    _require_cuda(hidden, weight, mask, logits)
+    lib = load()
+    batch, hdim = hidden.shape
+    vocab = weight.shape[0]
+    ws = workspace(hidden.device, batch, vocab)
+    status = getattr(lib, entry)(
+        _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+        _ptr(mask), 0 if mask is None else mask.stride(0),
+        batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+        _ptr(logits), 0 if logits is None else logits.stride(0),
+        _ptr(top_value), _ptr(top_index), _ptr(top_key),
+        _ptr(ws), ws.numel(), _stream(hidden.device))
+    _check(status, entry)
+
+
+def row_sparse(hidden, weight, mask, logits=None, top_value=None, top_index=None, top_key=None,
+               vocab_offset: int = 0) -> None:
+    _projection("gsp_row_sparse_logits", hidden, weight, mask, logits, top_value, top_index,
+                top_key, vocab_offset)
+
+
+def block_gemm(hidden, weight, mask, logits=None, top_value=None, top_index=None, top_key=None,
+               vocab_offset: int = 0) -> None:
+    _projection("gsp_block_gemm_logits", hidden, weight, mask, logits, top_value, top_index,
+                top_key, vocab_offset)
+
+
+def dense_masked(hidden, weight, mask, logits=None, top_value=None, top_index=None, top_key=None,
+                 vocab_offset: int = 0) -> None:
+    _projection("gsp_dense_masked_logits", hidden, weight, mask, logits, top_value, top_index,
+                top_key, vocab_offset)
+
+
+def row_sparse_compact(hidden, weight, mask, compact_logits, compact_ids, offsets,
+                       top_value=None, top_index=None, top_key=None, vocab_offset: int = 0) -> None:
+    _require_cuda(hidden, weight, mask, compact_logits, compact_ids, offsets)
+    lib = load()
+    batch, hdim = hidden.shape
+    vocab = weight.shape[0]
+    ws = workspace(hidden.device, batch, vocab)
+    cap = 0 if compact_logits is None else compact_logits.numel()
+    status = lib.gsp_row_sparse_compact(
+        _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+        _ptr(mask), 0 if mask is None else mask.stride(0),
+        batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+        _ptr(compact_logits), _ptr(compact_ids), cap, _ptr(offsets),
+        _ptr(top_value), _ptr(top_index), _ptr(top_key),
+        _ptr(ws), ws.numel(), _stream(hidden.device))
+    _check(status, "gsp_row_sparse_compact")
+
+
+def ids_to_bitmask(ids: torch.Tensor, vocab: int, bitmask: torch.Tensor, stats: torch.Tensor) -> None:
+    _require_cuda(ids, bitmask, stats)
+    status = load().gsp_ids_to_bitmask(_ptr(ids), ids.numel(), vocab, _ptr(bitmask), _ptr(stats),
+                                       _stream(ids.device))
+    _check(status, "gsp_ids_to_bitmask")
+
+
+def mask_stats(mask: torch.Tensor, vocab: int, legal_counts=None, full_words=None,
+               active_tiles=None) -> None:
+    _require_cuda(mask)
+    batch = mask.shape[0]
+    status = load().gsp_mask_stats(_ptr(mask), mask.stride(0), batch, vocab, _ptr(legal_counts),
+                                   _ptr(full_words), _ptr(active_tiles), _stream(mask.device))
+    _check(status, "gsp_mask_stats")
+
+
+def top1_from_keys(keys: torch.Tensor, top_value=None, top_index=None) -> None:
+    _require_cuda(keys)
+    status = load().gsp_top1_from_keys(_ptr(keys), keys.numel(), _ptr(top_value), _ptr(top_index),
+                                       _stream(keys.device))
+    _check(status, "gsp_top1_from_keys")

@@ -1,0 +1,152 @@
+"""Vocabulary-parallel grammar-conditioned LM head (one process per GPU).
+
+The reference is single-GPU. A large-vocabulary head shards naturally by
+vocabulary rows: rank r owns the contiguous rows [start_r, stop_r) of W and
+the matching words of every request's bitmask (shard boundaries are multiples
+of 32 tokens, so a shard owns whole mask words), runs the same kernels on its
+slice with vocab_offset = start_r, and the ranks exchange only
+
+  * one signed-orderable int64 top-1 key per request (an integer MAX
+    all-reduce: the larger rounded logit wins, ties go to the lower global
+    token id), decoded on the device by gsp_top1_from_keys; and
+  * when full logits are requested, the -inf-filled [B, V/R] logit slices
+    (an all-gather).
+
+All collectives go through torch.distributed (NCCL between GPUs; gloo works
+for the host-side logic on CPU ranks).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _native
+
+KEY_SIGN = -(1 << 63)  # XOR with this flips the top bit of an int64
+
+
+def shard_bounds(vocab: int, world_size: int, rank: int, align: int = 32) -> tuple[int, int]:
+    """Contiguous row range of `rank`: boundaries are multiples of `align`
+    (whole mask words), sizes differ by at most one `align` block, the last
+    shard takes the ragged tail."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError("bad rank / world size")
+    blocks = (vocab + align - 1) // align
+    lo_blk = blocks * rank // world_size
+    hi_blk = blocks * (rank + 1) // world_size
+    return min(lo_blk * align, vocab), min(hi_blk * align, vocab)
+
+
+# ---------------------------------------------------------------------------
+# top-1 keys (host mirror of the device packing in csrc/gsp_common.cuh)
+# ---------------------------------------------------------------------------
+def _ordered_bits(values: torch.Tensor) -> torch.Tensor:
+    v = values.to(torch.float32).clone()
+    v[v == 0] = 0.0  # +0 and -0 compare equal
+    u = v.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    neg = (u & 0x80000000) != 0
+    return torch.where(neg, (~u) & 0xFFFFFFFF, u | 0x80000000)
+
+
+def encode_keys(rounded_values: torch.Tensor, global_index: torch.Tensor, valid: torch.Tensor | None = None) -> torch.Tensor:
+    """Signed-orderable int64 keys of (rounded logit, global token id); rows
+    with no legal token (valid False) get the empty key."""
+    hi = _ordered_bits(rounded_values)
+    lo = 0xFFFFFFFF - (global_index.to(torch.int64) & 0xFFFFFFFF)
+    unsigned = (hi << 32) | lo  # wraps into the sign bit exactly like uint64
+    keys = unsigned ^ KEY_SIGN
+    if valid is not None:
+        keys = torch.where(valid, keys, torch.full_like(keys, KEY_SIGN))
+    return keys
+
+
+def decode_keys(keys: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """int64 keys -> (float32 value, int64 token id); the empty key decodes to
+    (-inf, 0), as torch.argmax of an all -inf row."""
+    unsigned = keys.to(torch.int64) ^ KEY_SIGN
+    empty = unsigned == 0
+    hi = (unsigned >> 32) & 0xFFFFFFFF
+    lo = unsigned & 0xFFFFFFFF
+    bits = torch.where((hi & 0x80000000) != 0, hi & 0x7FFFFFFF, (~hi) & 0xFFFFFFFF)
+    vals = bits.to(torch.int32).view(torch.float32) if bits.numel() else bits.to(torch.float32)
+    vals = torch.where(empty, torch.full_like(vals, float("-inf")), vals)
+    idx = torch.where(empty, torch.zeros_like(lo), 0xFFFFFFFF - lo)
+    return vals, idx
+
+
+def merge_top1_keys(keys: torch.Tensor, group=None) -> torch.Tensor:
+    """In-place integer MAX all-reduce of per-request keys across the ranks."""
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
+    return keys
+
+
+def gather_logits(local: torch.Tensor, vocab: int, group=None) -> torch.Tensor:
+    """All-gather [B, V_r] logit slices into [B, V] (ranks in order). Slices
+    are padded to the largest shard for the collective."""
+    if not (dist.is_initialized() and dist.get_world_size(group) > 1):
+        return local
+    world = dist.get_world_size(group)
+    bounds = [shard_bounds(vocab, world, r) for r in range(world)]
+    width = max(hi - lo for lo, hi in bounds)
+    batch = local.shape[0]
+    padded = torch.full((batch, width), float("-inf"), dtype=local.dtype, device=local.device)
+    padded[:, : local.shape[1]] = local
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded.contiguous(), group=group)
+    return torch.cat([p[:, : hi - lo] for p, (lo, hi) in zip(parts, bounds)], dim=1)
+
+
+class VocabParallelHead:
+    """This rank's shard of a vocabulary-parallel LM head.
+
+    forward(hidden [B, H], bitmask_gpu [B, >= ceil(V/32)] full-vocabulary
+    mask) -> (top_value [B] float32, top_index [B] int64 global ids,
+    logits [B, V] or None). Every rank must call forward with the same
+    arguments in the same order (the collectives are matched by order).
+    """
+
+    def __init__(self, weight_shard: torch.Tensor, vocab: int, start: int, group=None):
+        if weight_shard.device.type != "cuda":
+            raise ValueError("weight_shard must be a CUDA tensor")
+        if start % 32:
+            raise ValueError("shard start must be a multiple of 32")
+        self.weight = weight_shard.contiguous()
+        self.vocab = vocab
+        self.start = start
+        self.stop = start + weight_shard.shape[0]
+        self.group = group
+
+    @classmethod
+    def from_full_weight(cls, weight: torch.Tensor, group=None) -> "VocabParallelHead":
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        lo, hi = shard_bounds(weight.shape[0], world, rank)
+        return cls(weight[lo:hi], weight.shape[0], lo, group)
+
+    def local_mask(self, bitmask_gpu: torch.Tensor) -> torch.Tensor:
+        w0 = self.start // 32
+        w1 = (self.stop + 31) // 32
+        return bitmask_gpu[:, w0:w1]
+
+    def forward(self, hidden: torch.Tensor, bitmask_gpu: torch.Tensor | None, *,
+                route: str = "row-sparse", full_logits: bool = False):
+        hidden_2d = hidden.reshape(1, -1) if hidden.ndim == 1 else hidden
+        batch = hidden_2d.shape[0]
+        dev = hidden.device
+        mask = None if bitmask_gpu is None else self.local_mask(bitmask_gpu.reshape(batch, -1))
+        local_logits = (torch.empty((batch, self.stop - self.start), device=dev, dtype=hidden.dtype)
+                        if full_logits else None)
+        keys = torch.empty(batch, device=dev, dtype=torch.int64)
+        fn = {"row-sparse": _native.row_sparse, "block-sparse": _native.block_gemm,
+              "dense-mask": _native.dense_masked}[route]
+        if self.stop > self.start:
+            fn(hidden_2d, self.weight, mask, logits=local_logits, top_key=keys, vocab_offset=self.start)
+        else:
+            keys.fill_(KEY_SIGN)
+        merge_top1_keys(keys, self.group)
+        top_value = torch.empty(batch, device=dev, dtype=torch.float32)
+        top_index = torch.empty(batch, device=dev, dtype=torch.int64)
+        _native.top1_from_keys(keys, top_value, top_index)
+        logits = gather_logits(local_logits, self.vocab, self.group) if full_logits else None
+        return top_value, top_index, logits

@@ -1,0 +1,164 @@
+/*
+ * gsp_b200.h -- C ABI of the B200 (sm_100a) grammar-conditioned LM-head library.
+ *
+ * Drop-in device layer for the GSP decode-time LM head: inputs are decode
+ * hidden states [B, H], the LM-head weight W [V, H] (row-major) and a packed
+ * int32 grammar bitmask [B, >= ceil(V/32)] (LSB-first: token v is legal iff bit
+ * v%32 of word v/32 is set). Outputs are vocab-shaped logits with -inf on
+ * illegal tokens, or compact legal logits with their token ids, plus a fused
+ * greedy top-1 per request (ties to the lowest vocabulary index).
+ *
+ * Conventions for every entry point:
+ *   - All tensor pointers are device pointers (cudaMalloc / torch CUDA memory).
+ *   - Strides are in ELEMENTS of the pointed-to type and refer to the row
+ *     (outer) dimension; the inner dimension is contiguous.
+ *   - `stream` is a cudaStream_t handle passed as void* (NULL = legacy default
+ *     stream). Every call is asynchronous on that stream: no host sync.
+ *   - `dtype`: GSP_DTYPE_F16 or GSP_DTYPE_BF16; hidden, weight and the logits
+ *     share it. Accumulation is fp32, rounded once to `dtype`.
+ *   - `vocab_offset` shifts the token ids reported in top_index / compact ids,
+ *     for a weight that is one contiguous row shard of a larger vocabulary.
+ *   - Optional outputs may be NULL.
+ *   - `workspace` must be at least gsp_workspace_bytes(batch, vocab) bytes,
+ *     zero-filled once before first use; every call leaves it zero-filled
+ *     again. Calls that run concurrently must not share one workspace.
+ *   - Returns GSP_OK or a negative GSP_ERR_* code; no exception or abort
+ *     crosses the ABI. gsp_last_error() describes the last failure on the
+ *     calling host thread.
+ *
+ * Top-1 keys (top_key outputs) are signed-orderable int64 values: a larger key
+ * is a larger rounded logit, or the same logit at a lower token id. A plain
+ * integer MAX reduction over keys from vocabulary shards therefore yields the
+ * global greedy token; gsp_top1_from_keys decodes a key.
+ */
+#ifndef GSP_B200_H_
+#define GSP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GSP_ABI_VERSION 1
+
+#define GSP_OK 0
+#define GSP_ERR_INVALID_ARGUMENT (-1)
+#define GSP_ERR_UNSUPPORTED (-2)
+#define GSP_ERR_WORKSPACE (-3)
+#define GSP_ERR_CUDA (-4)
+
+#define GSP_DTYPE_F16 0
+#define GSP_DTYPE_BF16 1
+
+/* Rows of one vocabulary tile for the block and dense GEMM paths and for the
+ * active-tile statistics. */
+#define GSP_TILE_ROWS 128
+
+int32_t gsp_abi_version(void);
+const char* gsp_status_string(int32_t status);
+const char* gsp_last_error(void);
+
+/* Bytes of workspace any entry point below needs for (batch, vocab). */
+size_t gsp_workspace_bytes(int32_t batch, int32_t vocab);
+
+/*
+ * Row-sparse (direct-bitmask) projection: only legal rows of W are read.
+ * Replaces gsp/triton_runtime.py:61-125 (bitmask_sparse_logits) and its kernel
+ * gsp/triton_runtime.py:15-58 (_bitmask_sparse_lm_head_kernel).
+ * bitmask == NULL means every token is legal. bitmask_row_stride may be 0 to
+ * share one mask row across the batch. logits [batch, vocab] may be NULL when
+ * only the top-1 outputs are wanted.
+ */
+int32_t gsp_row_sparse_logits(const void* hidden, int64_t hidden_row_stride,
+                              const void* weight, int64_t weight_row_stride,
+                              const int32_t* bitmask, int64_t bitmask_row_stride,
+                              int32_t batch, int32_t vocab, int32_t hidden_dim,
+                              int32_t dtype, int64_t vocab_offset, void* logits,
+                              int64_t logits_row_stride, float* top_value,
+                              int64_t* top_index, int64_t* top_key, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/*
+ * Compact legal logits: request b's legal tokens, in increasing token order,
+ * occupy positions [request_offsets[b], request_offsets[b+1]) of
+ * compact_logits / compact_ids. request_offsets ([batch+1]) is always written;
+ * entries past `capacity` are not. Replaces gsp/runtime.py:9-51
+ * (constrained_projection / ProjectionResult, mode "sparse-gather" and
+ * "dense-selected") for bitmask-described legal sets.
+ */
+int32_t gsp_row_sparse_compact(const void* hidden, int64_t hidden_row_stride,
+                               const void* weight, int64_t weight_row_stride,
+                               const int32_t* bitmask, int64_t bitmask_row_stride,
+                               int32_t batch, int32_t vocab, int32_t hidden_dim,
+                               int32_t dtype, int64_t vocab_offset, void* compact_logits,
+                               int64_t* compact_ids, int64_t capacity,
+                               int64_t* request_offsets, float* top_value,
+                               int64_t* top_index, int64_t* top_key, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
+ * Token-id list -> packed bitmask [ceil(vocab/32)] (duplicates collapse, the
+ * ids come out sorted). stats[0] = number of distinct in-range ids,
+ * stats[1] = number of ids outside [0, vocab). Both outputs are cleared by the
+ * call. Replaces the id handling of gsp/runtime.py:35-43.
+ */
+int32_t gsp_ids_to_bitmask(const int64_t* ids, int64_t count, int32_t vocab,
+                           int32_t* bitmask, int64_t* stats, void* stream);
+
+/*
+ * Per-request density statistics computed on the device: legal token counts,
+ * full (-1) word counts (the signal of gsp/triton_runtime.py:310-321) and the
+ * number of GSP_TILE_ROWS-row tiles holding any legal token of any request.
+ * Outputs may be NULL; active_tiles is a single int32.
+ */
+int32_t gsp_mask_stats(const int32_t* bitmask, int64_t bitmask_row_stride,
+                       int32_t batch, int32_t vocab, int32_t* legal_counts,
+                       int32_t* full_words, int32_t* active_tiles, void* stream);
+
+/*
+ * Grammar-aware block GEMM: tensor-core (tcgen05) projection of only the
+ * GSP_TILE_ROWS-row vocabulary tiles that hold a legal token of any request in
+ * the batch, with the -inf mask and top-1 fused into the epilogue.
+ * Replaces gsp/triton_runtime.py:212-258 (bitmask_block_gemm_logits) and its
+ * kernel gsp/triton_runtime.py:147-209.
+ */
+int32_t gsp_block_gemm_logits(const void* hidden, int64_t hidden_row_stride,
+                              const void* weight, int64_t weight_row_stride,
+                              const int32_t* bitmask, int64_t bitmask_row_stride,
+                              int32_t batch, int32_t vocab, int32_t hidden_dim,
+                              int32_t dtype, int64_t vocab_offset, void* logits,
+                              int64_t logits_row_stride, float* top_value,
+                              int64_t* top_index, int64_t* top_key, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/*
+ * Dense tensor-core projection of every vocabulary tile with the grammar mask
+ * and top-1 fused into the epilogue (bitmask may be NULL: no mask).
+ * Replaces gsp/triton_runtime.py:285-308 (dense_masked_logits: F.linear
+ * followed by xgrammar's apply_token_bitmask_inplace).
+ */
+int32_t gsp_dense_masked_logits(const void* hidden, int64_t hidden_row_stride,
+                                const void* weight, int64_t weight_row_stride,
+                                const int32_t* bitmask, int64_t bitmask_row_stride,
+                                int32_t batch, int32_t vocab, int32_t hidden_dim,
+                                int32_t dtype, int64_t vocab_offset, void* logits,
+                                int64_t logits_row_stride, float* top_value,
+                                int64_t* top_index, int64_t* top_key, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/*
+ * Decode top-1 keys (e.g. after an integer MAX all-reduce across vocabulary
+ * shards) into the rounded logit value and the token id. No reference
+ * counterpart: the reference is single-GPU and takes logits.argmax(-1)
+ * (benchmarks/qwen35_adaptive_paired.py:94).
+ */
+int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
+                           int64_t* top_index, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSP_B200_H_ */

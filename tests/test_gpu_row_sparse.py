@@ -1,0 +1,259 @@
+"""GPU parity of the row-sparse path (gsp_row_sparse_logits / _compact), the
+mask utilities and constrained_projection against the CPU oracle and the
+reference's golden outputs.
+
+Tolerance (oracle.value_bound): legal support bit-exact; each legal logit
+within atol 2e-3 + max(rtol 2e-3 * |exact|, half an output ulp) of the exact
+float64 value; greedy top-1 identical to the exact argmax except inside the
+near-tie window atol + max(rtol * |max|, one output ulp); fused top-1 equal to
+torch.argmax over the kernel's own logits, bit for bit.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_npz
+from gsp import _native
+from gsp import runtime as rt
+from gsp import triton_runtime as tr
+from oracle import gsp_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(exact, got, dtype, label=""):
+    rep = O.compare_logits(exact, got.cpu(), dtype=dtype)
+    assert rep["support"], ("support", label, rep)
+    assert rep["values"], ("values", label, rep)
+    _, idx = O.top1(got.cpu())
+    assert O.top1_agrees(exact, idx, dtype=dtype), ("top1", label)
+
+
+def _fused(h2, w, mask, logits=None):
+    b = h2.shape[0]
+    tv = torch.empty(b, device=h2.device, dtype=torch.float32)
+    ti = torch.empty(b, device=h2.device, dtype=torch.int64)
+    tk = torch.empty(b, device=h2.device, dtype=torch.int64)
+    _native.row_sparse(h2, w, mask, logits=logits, top_value=tv, top_index=ti, top_key=tk)
+    return tv, ti, tk
+
+
+@pytest.mark.parametrize("fixture", ["row_sparse_ref.npz", "dense_mask_ref.npz"])
+def test_golden_fixtures(cuda_device, fixture):
+    data, meta = load_npz(fixture)
+    for c in meta:
+        w, h, mask = O.kernel_case_inputs(c["vocab"], c["hidden"], c["batch"], c["dtype"], c["seed"],
+                                          c["recipe"], c["extra_words"])
+        ref = O.bits16_to_tensor(data[c["name"] + "/out"], c["dtype"])
+        got = tr.bitmask_sparse_logits(h.to(cuda_device), w.to(cuda_device), torch.from_numpy(mask).to(cuda_device))
+        got = got.reshape(c["batch"], -1).cpu()
+        assert torch.equal(torch.isfinite(got), torch.isfinite(ref)), c["name"]
+        _check(O.masked_logits_exact(h, w, mask), got, O.TORCH_DTYPES[c["dtype"]], c["name"])
+
+
+def test_reference_sparse_test_shapes(cuda_device):
+    """tests/test_triton_sparse.py of the reference: V=151,936, H=1,024, fp16,
+    batch 1, k in {1, 13, 428, 4096, 32768, 120000}, W and h ~ N(0, 1)."""
+    rng = np.random.default_rng(17)
+    vocab, hidden = 151936, 1024
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half()
+    h = torch.from_numpy(rng.standard_normal((1, hidden), dtype=np.float32)).half()
+    wd, hd = w.to(cuda_device), h.to(cuda_device)
+    for k in (1, 13, 428, 4096, 32768, 120000):
+        ids = rng.permutation(vocab)[:k]
+        mask = O.ids_to_bitmask(ids, vocab)
+        got = tr.bitmask_sparse_logits(hd, wd, torch.from_numpy(mask).to(cuda_device))
+        assert got.shape == (vocab,)
+        _check(O.masked_logits_exact(h, w, mask)[0], got, torch.float16, f"k={k}")
+
+
+def test_fused_top1_is_argmax_of_logits(cuda_device):
+    rng = np.random.default_rng(3)
+    for vocab, hidden, batch, dtype in ((5000, 256, 1, torch.float16), (4099, 512, 3, torch.bfloat16),
+                                        (248320, 64, 2, torch.float16)):
+        w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).to(dtype).to(cuda_device)
+        h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).to(dtype).to(cuda_device)
+        mask = torch.from_numpy(O.make_batch_mask(rng, batch, vocab, [vocab // 50] * batch)).to(cuda_device)
+        logits = torch.empty(batch, vocab, device=cuda_device, dtype=dtype)
+        tv, ti, tk = _fused(h, w, mask, logits)
+        assert torch.equal(ti, logits.argmax(-1))
+        assert torch.equal(tv, logits.float().gather(1, ti[:, None])[:, 0])
+        tv2, ti2, _ = _fused(h, w, mask, None)  # top-1 without materialising logits
+        assert torch.equal(ti2, ti) and torch.equal(tv2, tv)
+
+
+def test_ties_go_to_lowest_index(cuda_device):
+    vocab, hidden = 4096, 128
+    w = torch.zeros(vocab, hidden, dtype=torch.float16)
+    w[:, 0] = 1.0
+    h = torch.zeros(1, hidden, dtype=torch.float16)
+    h[0, 0] = 2.0
+    mask = O.ids_to_bitmask([4000, 17, 900, 3000], vocab)
+    logits = torch.empty(1, vocab, device=cuda_device, dtype=torch.float16)
+    tv, ti, _ = _fused(h.to(cuda_device), w.to(cuda_device), torch.from_numpy(mask).to(cuda_device), logits)
+    assert ti.item() == 17 and tv.item() == 2.0
+    assert ti.item() == logits.argmax(-1).item()
+
+
+def test_empty_mask_and_repeated_calls(cuda_device):
+    vocab, hidden = 3000, 64
+    rng = np.random.default_rng(9)
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half().to(cuda_device)
+    h = torch.from_numpy(rng.standard_normal((2, hidden), dtype=np.float32)).half().to(cuda_device)
+    mask = torch.from_numpy(O.make_batch_mask(rng, 2, vocab, [0, 40])).to(cuda_device)
+    logits = torch.empty(2, vocab, device=cuda_device, dtype=torch.float16)
+    results = [tuple(t.clone() for t in _fused(h, w, mask, logits)) for _ in range(3)]
+    for r in results[1:]:
+        assert all(torch.equal(a, b) for a, b in zip(r, results[0]))
+    tv, ti, _ = results[0]
+    assert ti[0].item() == 0 and tv[0].item() == float("-inf")  # torch.argmax of all -inf is 0
+    assert not torch.isfinite(logits[0]).any()
+    assert ti[1].item() == logits[1].argmax().item()
+
+
+@pytest.mark.parametrize("vocab,hidden,batch", [(1, 8, 1), (33, 16, 2), (1000, 1000, 2), (4100, 12, 3),
+                                                (777, 96, 5)])
+def test_edge_shapes(cuda_device, vocab, hidden, batch):
+    """V not a multiple of 32, H not a multiple of 8 (scalar path), tiny V."""
+    rng = np.random.default_rng(vocab + hidden)
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half()
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).half()
+    mask = O.recipe_mask("random+full+zero", rng, batch, vocab)
+    got = tr.bitmask_sparse_logits(h.to(cuda_device), w.to(cuda_device), torch.from_numpy(mask).to(cuda_device))
+    _check(O.masked_logits_exact(h, w, mask).reshape(batch, vocab), got.reshape(batch, vocab), torch.float16)
+
+
+def test_misaligned_strided_and_broadcast_inputs(cuda_device):
+    rng = np.random.default_rng(21)
+    vocab, hidden, batch = 2048, 256, 3
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half()
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).half()
+    mask = O.recipe_mask("u100", rng, 1, vocab, extra_words=3)
+    exact = O.masked_logits_exact(h, w, np.repeat(mask, batch, axis=0))
+    # hidden starting one element off a 16-byte boundary (vector path disabled)
+    hbuf = torch.empty(batch * hidden + 1, dtype=torch.float16, device=cuda_device)
+    hbuf[1:] = h.reshape(-1).to(cuda_device)
+    h_mis = hbuf[1:].view(batch, hidden)
+    # one mask row shared by every request: row stride 0; wider than ceil(V/32)
+    m = torch.from_numpy(mask).to(cuda_device).expand(batch, -1)
+    logits = torch.empty(batch, vocab + 5, device=cuda_device, dtype=torch.float16)[:, :vocab]
+    _native.row_sparse(h_mis, w.to(cuda_device), m, logits=logits)
+    _check(exact, logits, torch.float16, "misaligned/broadcast/strided-out")
+
+
+def test_wide_mask_uses_real_row_stride(cuda_device):
+    """A [B, words + extra] mask: every request reads its own row (the reference
+    kernels assume stride ceil(V/32); its dense route uses the real stride)."""
+    rng = np.random.default_rng(5)
+    vocab, hidden, batch = 1000, 64, 3
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half()
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).half()
+    mask = O.recipe_mask("u10+u300+random", rng, batch, vocab, extra_words=7)
+    got = tr.bitmask_sparse_logits(h.to(cuda_device), w.to(cuda_device), torch.from_numpy(mask).to(cuda_device))
+    _check(O.masked_logits_exact(h, w, mask), got, torch.float16)
+
+
+def test_compact_logits(cuda_device):
+    rng = np.random.default_rng(8)
+    vocab, hidden, batch = 9000, 128, 3
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).bfloat16()
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).bfloat16()
+    mask = O.make_batch_mask(rng, batch, vocab, [5, 0, 700], clustered=True, max_runs=8)
+    md = torch.from_numpy(mask).to(cuda_device)
+    ids, lg, off = tr.bitmask_compact_logits(h.to(cuda_device), w.to(cuda_device), md)
+    legal = O.unpack_bitmask(mask, vocab)
+    assert off.tolist() == [0, 5, 5, 705]
+    exact = O.masked_logits_exact(h, w, mask)
+    for b in range(batch):
+        s, e = off[b].item(), off[b + 1].item()
+        assert np.array_equal(ids[s:e].cpu().numpy(), np.flatnonzero(legal[b]))
+        rep = O.compare_logits(exact[b, np.flatnonzero(legal[b])], lg[s:e].cpu(), dtype=torch.bfloat16)
+        assert rep["support"] and rep["values"]
+
+
+def test_ids_to_bitmask_and_mask_stats(cuda_device):
+    rng = np.random.default_rng(12)
+    vocab = 248320
+    ids = rng.integers(0, vocab, size=5000)
+    bm = torch.empty(1, (vocab + 31) // 32, dtype=torch.int32, device=cuda_device)
+    stats = torch.empty(2, dtype=torch.int64, device=cuda_device)
+    _native.ids_to_bitmask(torch.from_numpy(ids).to(cuda_device), vocab, bm, stats)
+    assert np.array_equal(bm.cpu().numpy(), O.ids_to_bitmask(ids, vocab))
+    assert stats.tolist() == [len(np.unique(ids)), 0]
+    bad = torch.tensor([3, -1, vocab, 5, 5], device=cuda_device)
+    _native.ids_to_bitmask(bad, vocab, bm, stats)
+    assert stats.tolist() == [2, 2]
+    batch = 5
+    mask = O.make_batch_mask(rng, batch, vocab, [1242] * batch, clustered=True, max_runs=16)
+    mask[2, 10:20] = -1
+    st = tr.mask_stats(torch.from_numpy(mask).to(cuda_device), vocab)
+    legal = O.unpack_bitmask(mask, vocab)
+    assert st["legal_counts"] == legal.sum(1).tolist()
+    assert st["full_words"] == [int((mask[b] == -1).sum()) for b in range(batch)]
+    assert st["active_tiles"] == O.active_tiles(mask, vocab)
+
+
+def test_constrained_projection_golden(cuda_device):
+    data, _ = load_npz("projection_ref.npz")
+    import json
+    meta = json.loads(str(data["meta"]))
+    for c in meta:
+        if c["name"].startswith("config0"):
+            continue  # fp32: checked below in fp16
+        w, h = O.projection_case_inputs(c["dtype"], c["seed"])
+        if c["hidden_1d"]:
+            h = h[0]
+        ids = None if c["ids_is_none"] else torch.from_numpy(data[c["name"] + "/ids"])
+        res = rt.constrained_projection(h.to(cuda_device), w.to(cuda_device),
+                                        None if ids is None else ids.to(cuda_device),
+                                        dense_threshold=c["threshold"])
+        assert res.mode == c["mode"], c["name"]
+        assert np.array_equal(res.token_ids.cpu().numpy(), data[c["name"] + "/token_ids"]), c["name"]
+        exact = O.constrained_projection(h, w, ids, dense_threshold=c["threshold"])
+        ex = (h.reshape(-1, h.shape[-1]).double() @ w[exact.token_ids].double().T)
+        ex = ex[0] if h.ndim == 1 else ex
+        rep = O.compare_logits(ex, res.logits.cpu(), dtype=w.dtype)
+        assert rep["support"] and rep["values"], (c["name"], rep)
+
+
+def test_constrained_projection_errors_and_config0(cuda_device):
+    w = torch.zeros((100, 8), dtype=torch.float16, device=cuda_device)
+    h = torch.zeros((1, 8), dtype=torch.float16, device=cuda_device)
+    with pytest.raises(ValueError, match="grammar produced an empty legal-token set"):
+        rt.constrained_projection(h, w, torch.zeros(0, dtype=torch.long))
+    with pytest.raises(ValueError, match="out-of-range"):
+        rt.constrained_projection(h, w, torch.tensor([5, 100]))
+    with pytest.raises(ValueError, match="one-dimensional"):
+        rt.constrained_projection(h, w, torch.tensor([[1, 2]]))
+    with pytest.raises(ValueError, match="float16 or bfloat16"):
+        rt.constrained_projection(h.float(), w.float(), torch.tensor([1]))
+    # 32,768 x 1,024, batch 1, 1% uniform (seed 0), in fp16
+    w32, h32, ids = O.config0_inputs(seed=0)
+    w16, h16 = w32.half(), h32.half()
+    res = rt.constrained_projection(h16.to(cuda_device), w16.to(cuda_device), torch.from_numpy(ids).to(cuda_device))
+    assert res.mode == "sparse-gather" and res.logits.shape == (1, 327)
+    assert np.array_equal(res.token_ids.cpu().numpy(), ids)
+    exact = h16.double() @ w16[torch.from_numpy(ids)].double().T
+    rep = O.compare_logits(exact, res.logits.cpu(), dtype=torch.float16)
+    assert rep["values"], rep
+
+
+@pytest.mark.parametrize("clustered", [False, True])
+def test_full_size_density_sweep(cuda_device, clustered):
+    """V=248,320, H=2,048 fp16, W ~ N(0, 0.02), h ~ N(0, 1), batch 1: every
+    density of the GEMV workload, uniform or clustered in 1-64 runs."""
+    vocab, hidden = 248320, 2048
+    g = torch.Generator(device=cuda_device).manual_seed(1234)
+    wd = (torch.randn(vocab, hidden, device=cuda_device, generator=g) * 0.02).half()
+    hd = torch.randn(1, hidden, device=cuda_device, generator=g).half()
+    w, h = wd.cpu(), hd.cpu()
+    rng = np.random.default_rng(77 + clustered)
+    for density in (0.0005, 0.005, 0.01, 0.10, 0.50, 1.0):
+        k = int(round(density * vocab))
+        mask = O.make_batch_mask(rng, 1, vocab, [k], clustered=clustered, max_runs=64)
+        logits = torch.empty(1, vocab, device=cuda_device, dtype=torch.float16)
+        tv, ti, _ = _fused(hd, wd, torch.from_numpy(mask).to(cuda_device), logits)
+        exact = O.masked_logits_exact(h, w, mask)
+        _check(exact, logits, torch.float16, f"density={density}")
+        assert int(torch.isfinite(logits).sum()) == k
+        assert ti.item() == logits.argmax(-1).item()

@@ -1,0 +1,127 @@
+"""CPU-side checks of the C ABI library and of the drop-in Python API: the
+library loads and exports every symbol include/gsp_b200.h declares, C-level
+argument validation fails before any device work, and the Python entry points
+raise the reference's ValueErrors. No kernel is launched here."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from conftest import REPO, load_json
+from gsp import _native
+from gsp import runtime as rt
+from gsp import triton_runtime as tr
+
+HEADER = os.path.join(REPO, "include", "gsp_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int32_t|size_t|const char\s*\*)\s*(gsp_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    syms = declared_symbols()
+    assert len(syms) >= 11
+    lib = _native.load()
+    for s in syms:
+        assert hasattr(lib, s), s
+        assert s in _native.SIGNATURES, f"{s} has no ctypes signature"
+
+
+def test_abi_version_and_status_strings():
+    lib = _native.load()
+    assert lib.gsp_abi_version() == 1
+    assert lib.gsp_status_string(0) == b"GSP_OK"
+    assert lib.gsp_status_string(-4) == b"GSP_ERR_CUDA"
+
+
+def test_workspace_bytes():
+    lib = _native.load()
+    assert lib.gsp_workspace_bytes(0, 10) == 0
+    n = lib.gsp_workspace_bytes(32, 248320)
+    assert n % 256 == 0 and n >= 8 * 32 + 1940 * 4
+
+
+FAKE = ctypes.c_void_p(4096)  # never dereferenced: every call below fails validation first
+
+
+def _row_sparse(**kw):
+    args = dict(hidden=FAKE, hs=8, weight=FAKE, ws=8, mask=None, ms=0, batch=1, vocab=64, hdim=8,
+                dtype=0, off=0, logits=None, ls=64, tv=None, ti=None, tk=None, wsp=None, wsb=0)
+    args.update(kw)
+    lib = _native.load()
+    return lib.gsp_row_sparse_logits(args["hidden"], args["hs"], args["weight"], args["ws"], args["mask"],
+                                     args["ms"], args["batch"], args["vocab"], args["hdim"], args["dtype"],
+                                     args["off"], args["logits"], args["ls"], args["tv"], args["ti"],
+                                     args["tk"], args["wsp"], args["wsb"], None)
+
+
+def test_c_abi_validation_rejects_before_launch():
+    lib = _native.load()
+    assert _row_sparse(hidden=None) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert b"non-null" in lib.gsp_last_error()
+    assert _row_sparse(batch=0) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert _row_sparse(dtype=7) == _native.GSP_ERR_UNSUPPORTED
+    assert _row_sparse(batch=2, hs=4) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert _row_sparse(batch=2, mask=FAKE, ms=1) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert _row_sparse(tv=FAKE) == _native.GSP_ERR_WORKSPACE
+    assert _row_sparse(tv=FAKE, wsp=FAKE, wsb=1) == _native.GSP_ERR_WORKSPACE
+    assert lib.gsp_ids_to_bitmask(None, 3, 10, FAKE, FAKE, None) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert lib.gsp_mask_stats(None, 0, 1, 10, None, None, None, None) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert lib.gsp_top1_from_keys(None, 1, None, None, None) == _native.GSP_ERR_INVALID_ARGUMENT
+
+
+def test_python_api_rejects_cpu_tensors_like_the_reference():
+    h = torch.zeros(2, 8, dtype=torch.float16)
+    w = torch.zeros(64, 8, dtype=torch.float16)
+    m = torch.zeros(2, 2, dtype=torch.int32)
+    with pytest.raises(ValueError, match="hidden and weight must be CUDA tensors"):
+        tr.bitmask_sparse_logits(h, w, m)
+    with pytest.raises(ValueError, match="hidden and weight must be CUDA tensors"):
+        tr.bitmask_block_gemm_logits(h, w, m)
+    with pytest.raises(ValueError, match=r"block GEMM path expects hidden shape \[B,D\] with B >= 2"):
+        tr.bitmask_block_gemm_logits(h[:1], w, m[:1])
+    with pytest.raises(ValueError, match="hidden and weight must be CUDA tensors"):
+        tr.dense_masked_logits(h, w, m)
+    with pytest.raises(ValueError):
+        rt.constrained_projection(h, w, torch.tensor([1, 2]))
+
+
+def test_mask_staging_validation():
+    with pytest.raises(ValueError, match="bitmask_cpu must be CPU int32"):
+        tr.copy_bitmask_to_gpu(torch.zeros(1, 4, dtype=torch.int64))
+    with pytest.raises(ValueError, match="bitmask_cpu must be pinned"):
+        tr.copy_bitmask_to_gpu(torch.zeros(1, 4, dtype=torch.int32))
+
+
+def test_full_word_fraction_matches_reference():
+    for c in load_json("routes_ref.json")["full_word_fraction"]:
+        assert tr.full_word_fraction_cpu(torch.tensor(c["mask"], dtype=torch.int32)) == c["fwf"]
+
+
+def test_reference_policy_routes_match_reference():
+    routes = load_json("routes_ref.json")
+    for c in routes["dispatch_cases"]:
+        assert tr._reference_route(c["batch"], c["fwf"], 0.80) == c["route"]
+        assert tr._reference_route(c["batch"], None, 0.80) == c["route_without_fwf"]
+    for c in routes["grid"]:
+        assert tr._reference_route(c["batch"], c["fwf"], c["threshold"]) == c["route"]
+    with pytest.raises(ValueError, match="full_word_fraction length must equal batch"):
+        tr._reference_route(3, [0.1, 0.2], 0.8)
+
+
+def test_b200_cost_model_prefers_the_cheapest_bytes():
+    V, H, e = 248320, 2048, 2
+    assert tr.choose_route(1, V, H, e, [V], 1940) == "row-sparse"
+    # two requests with a few clustered tokens: row-sparse reads far fewer bytes
+    assert tr.choose_route(2, V, H, e, [1242, 1242], 40) == "row-sparse"
+    # 32 requests sharing one grammar state: the union of tiles is read once,
+    # row-sparse would read the same rows 32 times
+    assert tr.choose_route(32, V, H, e, [1242] * 32, 20) == "block-sparse"
+    # 32 requests with disjoint clustered sets: fewer bytes row by row
+    assert tr.choose_route(32, V, H, e, [1242] * 32, 700) == "row-sparse"
+    # everything legal: dense
+    assert tr.choose_route(8, V, H, e, [V] * 8, 1940) == "dense-mask"

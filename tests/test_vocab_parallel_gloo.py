@@ -1,0 +1,103 @@
+"""Host-side logic of the vocabulary-parallel head on CPU ranks (gloo, world 2):
+shard bounds, top-1 key packing, the integer-MAX merge and the logit
+all-gather, checked against the single-process oracle."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gsp import vocab_parallel as vp
+from oracle import gsp_oracle as O
+
+
+def test_shard_bounds_cover_vocab():
+    for vocab in (1, 31, 32, 1000, 248320, 262144, 151936):
+        for world in (1, 2, 3, 4, 8):
+            bounds = [vp.shard_bounds(vocab, world, r) for r in range(world)]
+            assert bounds[0][0] == 0 and bounds[-1][1] == vocab
+            for (a, b), (c, d) in zip(bounds, bounds[1:]):
+                assert b == c and a % 32 == 0 and c % 32 == 0
+            sizes = [b - a for a, b in bounds]
+            assert max(sizes) - min(sizes) <= 32 or vocab % 32
+    assert vp.shard_bounds(248320, 8, 3) == (93120, 124160)
+
+
+def test_key_roundtrip_and_order():
+    vals = torch.tensor([1.5, -2.0, 0.0, -0.0, float("-inf"), 3.25, 3.25], dtype=torch.float16).float()
+    idx = torch.tensor([7, 3, 9, 2, 11, 40, 5])
+    keys = vp.encode_keys(vals, idx)
+    v, i = vp.decode_keys(keys)
+    assert torch.equal(i, torch.where(vals == 0, idx, idx)) and torch.equal(v[vals != 0], vals[vals != 0])
+    # larger value wins; equal values -> lower index wins; +0 == -0
+    assert keys[6] > keys[5]
+    assert keys[3] > keys[2]
+    assert keys[4] > vp.encode_keys(torch.tensor([0.0]), torch.tensor([0]), torch.tensor([False]))[0]
+    empty = vp.encode_keys(torch.zeros(1), torch.zeros(1, dtype=torch.long), torch.tensor([False]))
+    ev, ei = vp.decode_keys(empty)
+    assert ev.item() == float("-inf") and ei.item() == 0
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, case, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        vocab, hidden, batch, seed = case
+        rng = np.random.default_rng(seed)
+        w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half()
+        h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).half()
+        mask = O.make_batch_mask(rng, batch, vocab, [0, 1, 37, vocab // 3][:batch], clustered=True, max_runs=4)
+        # a tie across the shard boundary: request 0 gets two identical rows
+        lo, hi = vp.shard_bounds(vocab, world, rank)
+        full = O.masked_logits(h, w, mask)
+        local = full[:, lo:hi]
+        fin = torch.isfinite(local)
+        vals = torch.where(fin, local.float(), torch.full_like(local.float(), float("-inf")))
+        loc_idx = vals.argmax(1)
+        loc_val = vals.gather(1, loc_idx[:, None])[:, 0]
+        keys = vp.encode_keys(loc_val, loc_idx + lo, fin.any(1))
+        vp.merge_top1_keys(keys)
+        gv, gi = vp.decode_keys(keys)
+        ref_v, ref_i = O.top1(full)
+        gathered = vp.gather_logits(local, vocab)
+        q.put((rank, bool(torch.equal(gi, ref_i)), bool(torch.equal(gv, ref_v)),
+               bool(torch.equal(gathered, full))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [(1000, 64, 4, 5), (4096, 32, 3, 6)])
+def test_vocab_parallel_merge_gloo(case):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, idx_ok, val_ok, gather_ok in results:
+        assert idx_ok and val_ok and gather_ok, (rank, idx_ok, val_ok, gather_ok)
+
+
+def test_tie_across_shards_prefers_lowest_global_index():
+    keys_r0 = vp.encode_keys(torch.tensor([2.5]), torch.tensor([100]))
+    keys_r1 = vp.encode_keys(torch.tensor([2.5]), torch.tensor([900]))
+    merged = torch.maximum(keys_r0, keys_r1)
+    _, idx = vp.decode_keys(merged)
+    assert idx.item() == 100

@@ -16,8 +16,12 @@ hot path: full -inf-filled logits [V] plus the fused greedy top-1.
   sweep      every density of the GEMV workload, uniform and clustered;
   cpu_baseline  the oracle's CPU restatement of the same step on host cores.
 
-L2 is flushed (a 256 MiB write) before every timed step; the flush is outside
-the per-step events. With --gpus N (torchrun, one process per GPU) the head is
+Timing (one GPU): the K timed steps are captured in one CUDA graph and timed
+with CUDA events around its replay, so host launch overhead and per-step event
+overhead are excluded. Inputs are larger than L2: step i reads weight copy
+i % 32 (32 copies of the 1 GB head) and mask i % 64, so no step finds its legal
+rows in L2. A second, conservative figure ("cold") times every step eagerly
+with its own events after a 256 MiB L2-flushing write. With --gpus N (torchrun, one process per GPU) the head is
 vocabulary-parallel: each rank streams the legal rows of its V/N shard and the
 ranks merge the per-request top-1 with one NCCL integer-MAX all-reduce.
 
@@ -58,6 +62,7 @@ def parse_args():
     ap.add_argument("--density", type=float, default=0.01)
     ap.add_argument("--pattern", choices=("uniform", "clustered"), default="uniform")
     ap.add_argument("--masks", type=int, default=64, help="distinct seeded masks cycled through")
+    ap.add_argument("--copies", type=int, default=32, help="weight copies cycled through (one GPU)")
     ap.add_argument("--sweep-steps", type=int, default=100)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -229,7 +234,8 @@ def workload_config(args):
     return {"workload": "batch-1 row-sparse direct-bitmask LM-head GEMV", "vocab": VOCAB, "hidden": HIDDEN,
             "batch": 1, "density": args.density, "mask": f"{args.pattern}, fresh seeded mask per step",
             "weight": "fp16 N(0,0.02) row-major [V,H]", "outputs": "full logits [V] + fused top-1",
-            "l2": "flushed before every step (256 MiB write), flush outside the step events",
+            "l2": ("inputs larger than L2: step i reads weight copy i % copies (1 GB each) and mask i % masks"
+                   if args.gpus == 1 else "flushed before every step (256 MiB write), flush outside the step events"),
             "parallelism": f"vocab-parallel x{args.gpus}" if args.gpus > 1 else "single GPU"}
 
 
@@ -257,9 +263,11 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     lo, hi = vp.shard_bounds(VOCAB, world, rank)
 
-    # weight shard, hidden state and seeded masks (identical on every rank)
+    # weight shard(s), hidden state and seeded masks (identical on every rank)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    weight = (torch.randn(hi - lo, HIDDEN, device=dev, generator=g) * 0.02).half()
+    copies = args.copies if world == 1 else 1
+    weights = [(torch.randn(hi - lo, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(copies)]
+    weight = weights[0]
     hidden = torch.randn(1, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(99)).half()
     masks_np = make_masks(args.masks, args.density, args.pattern, seed=100)
     counts = legal_counts(masks_np)
@@ -274,11 +282,12 @@ def main():
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
     def step(i, mask_rows=local_masks):
-        m = mask_rows[i % args.masks][None]
+        m = mask_rows[i % mask_rows.shape[0]][None]
+        w = weights[i % len(weights)]
         if world == 1:
-            _native.row_sparse(hidden, weight, m, logits=logits, top_value=top_value, top_index=top_index)
+            _native.row_sparse(hidden, w, m, logits=logits, top_value=top_value, top_index=top_index)
         else:
-            _native.row_sparse(hidden, weight, m, logits=logits, top_key=top_key, vocab_offset=lo)
+            _native.row_sparse(hidden, w, m, logits=logits, top_key=top_key, vocab_offset=lo)
             vp.merge_top1_keys(top_key, group)
             _native.top1_from_keys(top_key, top_value, top_index)
 
@@ -288,6 +297,7 @@ def main():
         torch.cuda.synchronize()
 
     def timed(n, fn, offset):
+        """Eager steps, each after an L2-flushing write, each with its own events (µs)."""
         ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         for i in range(n):
@@ -296,7 +306,30 @@ def main():
             fn(offset + i)
             ev1[i].record()
         torch.cuda.synchronize()
-        return [a.elapsed_time(b) * 1e3 for a, b in zip(ev0, ev1)]  # µs
+        return [a.elapsed_time(b) * 1e3 for a, b in zip(ev0, ev1)]
+
+    def graph_total_us(n, fn):
+        """n steps captured in one CUDA graph; events around one replay (µs)."""
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for i in range(3):
+                fn(i)  # creates this stream's workspace before capture
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(n):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        del graph
+        return a.elapsed_time(b) * 1e3
 
     # warm-up (untimed)
     for i in range(max(args.warmup, 3)):
@@ -305,15 +338,24 @@ def main():
     sampler = ClockSampler(local_rank)
     with sampler:
         t_wall = time.perf_counter()
-        per_step = timed(args.steps, step, 0)
+        if world == 1:
+            total_us = graph_total_us(args.steps, step)
+            per_step = None
+        else:
+            per_step = timed(args.steps, step, 0)
+            total_us = sum(per_step)
         barrier()
         t_wall = time.perf_counter() - t_wall
-    total_us = sum(per_step)
     total_us = max_over_ranks(total_us, world)
     steps_idx = [i % args.masks for i in range(args.steps)]
     legal_bytes = float(sum(int(counts[j]) for j in steps_idx)) * HIDDEN * 2
     value = legal_bytes / (total_us * 1e-6) / 1e9
     us_per_step = total_us / args.steps
+    cold = None
+    if world == 1:
+        cold_steps = timed(min(args.steps, 200), step, 0)
+        cold = {"us_per_step": statistics.mean(cold_steps), "us_p50": statistics.median(cold_steps),
+                "what": "eager steps, 256 MiB L2-flushing write before each, events around each step"}
 
     # e2e through the C ABI with host buffers
     pinned_masks = torch.from_numpy(np.ascontiguousarray(masks_np[:, lo // 32:(hi + 31) // 32])).pin_memory()
@@ -347,7 +389,7 @@ def main():
 
     # roofline of the row-sparse kernel (rank 0's shard at N > 1)
     local_bytes = float(sum(int(local_counts[j]) for j in steps_idx)) * HIDDEN * 2
-    kernel_us = statistics.mean(per_step) if world == 1 else None
+    kernel_us = us_per_step if world == 1 else None
     peak, peak_src = read_peaks()
     algo_per_launch = local_bytes / args.steps
     if world == 1:
@@ -371,13 +413,13 @@ def main():
                 mk = torch.from_numpy(mk_np).to(dev)
                 cnt = legal_counts(mk_np)
                 n = args.sweep_steps
-                for i in range(3):
-                    step(i, mk)
-                ts = timed(n, lambda i: step(i, mk), 0)
+                t_us = graph_total_us(n, lambda i: step(i, mk))
+                ts = timed(min(n, 50), lambda i: step(i, mk), 0)
                 lb = float(sum(int(cnt[i % 16]) for i in range(n))) * HIDDEN * 2
-                sweep.append({"density": d, "pattern": pattern, "us_per_step": statistics.mean(ts),
-                              "us_p50": statistics.median(ts), "legal_gbs": lb / (sum(ts) * 1e-6) / 1e9,
-                              "frac_of_hbm": lb / (sum(ts) * 1e-6) / 1e9 / peak})
+                sweep.append({"density": d, "pattern": pattern, "us_per_step": t_us / n,
+                              "legal_gbs": lb / (t_us * 1e-6) / 1e9,
+                              "frac_of_hbm": lb / (t_us * 1e-6) / 1e9 / peak,
+                              "cold_us_per_step": statistics.mean(ts)})
         same_gpu_dense = time_dense_baseline(dev, weight, hidden, masks, args)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         w_cpu = weight.cpu().numpy()
@@ -400,6 +442,7 @@ def main():
             "roofline": roofline,
             "cpu_baseline": cpu_base,
             "clocks": sampler.summary(),
+            "cold": cold,
             "timed_region_wall_s": t_wall,
             "sweep": sweep,
             "same_gpu_dense_mask": same_gpu_dense,

@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/gsp_b200.h"
 #include "gsp_internal.h"
@@ -39,7 +40,7 @@ int tile_builder_blocks(int vocab) {
 
 size_t workspace_bytes(int batch, int vocab) {
   const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
-  return align256(sizeof(unsigned long long) * (size_t)batch + 8) +
+  return align256(16 + sizeof(unsigned long long) * (size_t)batch) +
          align256(sizeof(int32_t) * (size_t)ntiles) +
          align256(sizeof(int32_t) * (size_t)tile_builder_blocks(vocab));
 }
@@ -48,9 +49,10 @@ Workspace carve_workspace(void* base, int batch, int vocab) {
   const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
   char* p = static_cast<char*>(base);
   Workspace w;
-  w.keys = reinterpret_cast<unsigned long long*>(p);
-  w.ticket = reinterpret_cast<unsigned int*>(p + sizeof(unsigned long long) * (size_t)batch);
-  p += align256(sizeof(unsigned long long) * (size_t)batch + 8);
+  w.ticket = reinterpret_cast<unsigned int*>(p);
+  w.error = reinterpret_cast<int*>(p + 4);
+  w.keys = reinterpret_cast<unsigned long long*>(p + 16);
+  p += align256(16 + sizeof(unsigned long long) * (size_t)batch);
   w.tile_list = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * (size_t)ntiles);
   w.tile_counts = reinterpret_cast<int32_t*>(p);
@@ -67,6 +69,29 @@ int num_sms(int device) {
     cache[device] = n;
   }
   return cache[device];
+}
+
+cudaError_t raise_smem_limit(const void* func, size_t bytes, int device) {
+  struct Entry {
+    const void* func;
+    int device;
+    int bytes;
+  };
+  static std::mutex mu;
+  static Entry table[256];
+  static int used = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i) {
+    if (table[i].func == func && table[i].device == device) {
+      if ((int)bytes <= table[i].bytes) return cudaSuccess;
+      cudaError_t err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+      if (err == cudaSuccess) table[i].bytes = (int)bytes;
+      return err;
+    }
+  }
+  cudaError_t err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (err == cudaSuccess && used < 256) table[used++] = Entry{func, device, (int)bytes};
+  return err;
 }
 
 namespace {
@@ -153,10 +178,11 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
     p.top_value = top_value;
     p.top_index = top_index;
     p.top_key = top_key;
-    if (want_top) {
+    if (workspace) {
       Workspace w = carve_workspace(workspace, batch, vocab);
       p.keys = w.keys;
       p.ticket = w.ticket;
+      p.error = w.error;
     }
     return cuda_status(launch_row_sparse(p, dtype, s), fn);
   }
@@ -181,6 +207,7 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
   Workspace w = carve_workspace(workspace, batch, vocab);
   p.keys = w.keys;
   p.ticket = w.ticket;
+  p.error = w.error;
   p.tile_list = w.tile_list;
   p.tile_counts = w.tile_counts;
   p.dense = dense || bitmask == nullptr;
@@ -255,10 +282,11 @@ int32_t gsp_row_sparse_compact(const void* hidden, int64_t hidden_row_stride, co
   p.top_value = top_value;
   p.top_index = top_index;
   p.top_key = top_key;
-  if (want_top) {
+  if (workspace) {
     Workspace w = carve_workspace(workspace, batch, vocab);
     p.keys = w.keys;
     p.ticket = w.ticket;
+    p.error = w.error;
   }
   return cuda_status(launch_row_sparse(p, dtype, static_cast<cudaStream_t>(stream)), fn);
 }

@@ -35,6 +35,7 @@ struct RowSparseParams {
   // workspace: per-request keys + arrival ticket (zero on entry and exit)
   unsigned long long* keys;
   unsigned int* ticket;
+  int* error;  // set non-zero when a bounded wait gave up (never cleared by kernels)
 };
 
 // Parameters of the tensor-core block / dense projection.
@@ -57,14 +58,19 @@ struct BlockGemmParams {
   int64_t* top_key;
   unsigned long long* keys;
   unsigned int* ticket;
+  int* error;
   int32_t* tile_list;     // workspace: compacted active tile ids
   int32_t* tile_counts;   // workspace: per-builder-block active tile counts
   int dense;              // 1: every tile is projected (dense_masked_logits)
 };
 
+// Workspace layout (fixed offsets first, so calls with different batch sizes
+// can share one buffer): [0] arrival ticket, [4] error word, [16] per-request
+// top-1 keys, then the tile lists of the block / dense path.
 struct Workspace {
   unsigned long long* keys;
   unsigned int* ticket;
+  int* error;
   int32_t* tile_list;
   int32_t* tile_counts;
 };
@@ -73,6 +79,10 @@ size_t workspace_bytes(int batch, int vocab);
 Workspace carve_workspace(void* base, int batch, int vocab);
 
 int num_sms(int device);
+
+// Raises cudaFuncAttributeMaxDynamicSharedMemorySize of `func` on `device` to at
+// least `bytes` (thread-safe; a no-op when the current setting suffices).
+cudaError_t raise_smem_limit(const void* func, size_t bytes, int device);
 
 // Each launcher returns a cudaError_t value (cudaSuccess == 0).
 cudaError_t launch_row_sparse(const RowSparseParams& p, int dtype, cudaStream_t stream);

@@ -124,6 +124,16 @@ def workspace(device: torch.device, batch: int, vocab: int) -> torch.Tensor:
         return ws
 
 
+def workspace_error(device: torch.device) -> int:
+    """Error word of the current stream's workspace: non-zero after a kernel
+    gave up a bounded wait (reads the device, so it synchronises)."""
+    dev_index = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get((dev_index, torch.cuda.current_stream(device).cuda_stream))
+    if ws is None:
+        return 0
+    return int(ws[4:8].view(torch.int32).item())
+
+
 def _require_cuda(*tensors: torch.Tensor) -> None:
     for t in tensors:
         if t is not None and t.device.type != "cuda":

@@ -257,3 +257,8 @@ def test_full_size_density_sweep(cuda_device, clustered):
         _check(exact, logits, torch.float16, f"density={density}")
         assert int(torch.isfinite(logits).sum()) == k
         assert ti.item() == logits.argmax(-1).item()
+
+
+def test_no_bounded_wait_gave_up(cuda_device):
+    """Every kernel above completed without giving up a bounded wait."""
+    assert _native.workspace_error(cuda_device) == 0

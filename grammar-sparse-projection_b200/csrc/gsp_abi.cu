@@ -71,6 +71,14 @@ int num_sms(int device) {
   return cache[device];
 }
 
+int32_t record_error(int32_t code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 cudaError_t raise_smem_limit(const void* func, size_t bytes, int device) {
   struct Entry {
     const void* func;

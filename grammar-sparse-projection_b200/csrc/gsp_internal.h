@@ -80,6 +80,10 @@ Workspace carve_workspace(void* base, int batch, int vocab);
 
 int num_sms(int device);
 
+// Records `code` with a printf-style message as the calling thread's
+// gsp_last_error() and returns `code`.
+int32_t record_error(int32_t code, const char* fmt, ...);
+
 // Raises cudaFuncAttributeMaxDynamicSharedMemorySize of `func` on `device` to at
 // least `bytes` (thread-safe; a no-op when the current setting suffices).
 cudaError_t raise_smem_limit(const void* func, size_t bytes, int device);

@@ -57,6 +57,8 @@ SIGNATURES = {
     "gsp_block_gemm_logits": (_PROJECTION_ARGS, _i32),
     "gsp_dense_masked_logits": (_PROJECTION_ARGS, _i32),
     "gsp_top1_from_keys": ([_vp, _i32, _vp, _vp, _vp], _i32),
+    "gsp_row_sparse_logits_static": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
+                                      _vp, _i64, _vp, _vp, _vp, _vp], _i32),
 }
 
 

@@ -149,6 +149,33 @@ int32_t gsp_dense_masked_logits(const void* hidden, int64_t hidden_row_stride,
                                 size_t workspace_bytes, void* stream);
 
 /*
+ * Allocation-free variant of gsp_row_sparse_logits, for callers that cannot
+ * allocate device memory at all (a plugin inside a serving engine that owns
+ * every byte of device memory through its own pool, or an FFI binding that is
+ * handed only the input and output buffers). It takes the same arguments minus
+ * the workspace: the top-1 scratch lives in a fixed array inside the library,
+ * kept on every GPU that loads it until exit, so batch must be
+ * <= GSP_STATIC_MAX_BATCH and vocab <= GSP_STATIC_MAX_VOCAB (larger sizes fail
+ * with GSP_ERR_INVALID_ARGUMENT and a message in gsp_last_error()).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture. Each call clears the scratch it needs on `stream` and
+ * allocates nothing. All calls share the one array: calls that may run at the
+ * same time on the GPU (other streams, other host threads) race on it and
+ * must be serialised by the caller.
+ * No counterpart in the reference.
+ */
+#define GSP_STATIC_MAX_BATCH 1024
+#define GSP_STATIC_MAX_VOCAB 1048576
+int32_t gsp_row_sparse_logits_static(const void* hidden, int64_t hidden_row_stride,
+                                     const void* weight, int64_t weight_row_stride,
+                                     const int32_t* bitmask, int64_t bitmask_row_stride,
+                                     int32_t batch, int32_t vocab, int32_t hidden_dim,
+                                     int32_t dtype, int64_t vocab_offset, void* logits,
+                                     int64_t logits_row_stride, float* top_value,
+                                     int64_t* top_index, int64_t* top_key, void* stream);
+
+/*
  * Decode top-1 keys (e.g. after an integer MAX all-reduce across vocabulary
  * shards) into the rounded logit value and the token id. No reference
  * counterpart: the reference is single-GPU and takes logits.argmax(-1)

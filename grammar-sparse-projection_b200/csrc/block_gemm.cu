@@ -1,5 +1,564 @@
-// placeholder until the tcgen05 kernel lands
+// Grammar-aware block GEMM and dense masked GEMM on sm_100a tensor cores.
+//
+// Behaviour follows gsp/triton_runtime.py:147-209 (_bitmask_block_gemm_kernel):
+// logits[b, v] = sum_k W[v, k] h[b, k] (fp32 accumulate, rounded to the input
+// dtype) where token v is legal for request b, -inf elsewhere; only vocabulary
+// tiles holding a legal token of some request are multiplied. The dense route
+// (gsp/triton_runtime.py:285-308, F.linear + xgrammar mask) is the same kernel
+// over every tile.
+//
+// Two launches:
+//  * tile_builder_kernel: for every 128-row vocabulary tile, OR of the batch's
+//    mask words (4 words per request); active tile ids are compacted per
+//    builder block of kBuilderTiles tiles, and -inf is written over every
+//    request's outputs in inactive tiles. Skipped in dense mode.
+//  * tc_projection_kernel: one persistent CTA per SM, 6 warps.
+//      warp 0      one lane issues TMA loads of the W tile (128 rows x 64 K,
+//                  128-byte swizzle) and of h (Npad rows x 64 K) into a ring of
+//                  shared-memory stages;
+//      warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128 vocabulary
+//                  rows, N = batch padded to a multiple of 32, K = 16 per
+//                  instruction) into one of two TMEM accumulators, committing
+//                  each stage back to the producer and each tile to the epilogue;
+//      warps 2-5   epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
+//                  vocabulary row per thread), mask bit, rounding, -inf, logits
+//                  stores coalesced along the vocabulary, and 64-bit top-1 keys
+//                  reduced across the warp's 32 rows with a transpose-reduce.
+//    Tiles are taken from the compacted list round-robin by CTA. The cross-CTA
+//    top-1 merge is the same last-arrival scheme as the row-sparse kernel.
+//
+// "Swap-AB": the vocabulary is the MMA's M dimension and the (small) batch its N
+// dimension, so a batch of 2..256 requests fills a 128 x N tile.
+//
+// Every wait is bounded; a timed-out wait sets the workspace error word and the
+// kernel drains its copies and tensor-core work before returning.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+#include "gsp_async.cuh"
+#include "gsp_common.cuh"
 #include "gsp_internal.h"
+#include "gsp_tcgen05.cuh"
+
 namespace gsp {
-cudaError_t launch_block_gemm(const BlockGemmParams&, int, cudaStream_t) { return cudaErrorNotSupported; }
+namespace {
+
+constexpr int kTileRows = 128;
+constexpr int kTileK = 64;  // K elements per stage: one 128-byte swizzle row
+constexpr int kGemmThreads = 192;
+constexpr int kMaxNpad = 256;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kABytes = kTileRows * kTileK * 2;  // 16 KB
+
+struct GemmConfig {
+  int npad;      // batch padded to a multiple of 32 (<= 256)
+  int stages;
+  int kblocks;   // ceil(H / 64)
+  int ntiles;    // ceil(V / 128)
+  int nbuild;    // builder blocks (block mode)
+  uint32_t tmem_cols;
+  uint32_t idesc;
+};
+
+struct GemmLayout {
+  size_t a, b, bars, tmem, keys, pref, misc, total;
+};
+
+__host__ __device__ inline size_t align_to(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+__host__ __device__ inline GemmLayout gemm_layout(int npad, int stages, int nbuild) {
+  GemmLayout l;
+  size_t off = 0;
+  l.a = off;
+  off += (size_t)stages * kABytes;
+  l.b = align_to(off, 1024);
+  off = l.b + (size_t)stages * npad * kTileK * 2;
+  l.bars = align_to(off, 16);
+  off = l.bars + 8 * (2 * (size_t)stages + 4);
+  l.tmem = align_to(off, 16);
+  off = l.tmem + 16;
+  l.keys = align_to(off, 16);
+  off = l.keys + 8 * (size_t)kMaxNpad;
+  l.pref = align_to(off, 16);
+  off = l.pref + 4 * ((size_t)nbuild + 1);
+  l.misc = align_to(off, 16);
+  off = l.misc + 16;
+  l.total = align_to(off, 1024);
+  return l;
 }
+
+__device__ __forceinline__ int tile_at(const BlockGemmParams& p, const GemmConfig& c, const int* s_pref, int pos) {
+  if (p.dense) return pos;
+  int lo = 0, hi = c.nbuild;  // find j with s_pref[j] <= pos < s_pref[j + 1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (s_pref[mid] <= pos) lo = mid; else hi = mid;
+  }
+  return p.tile_list[lo * kBuilderTiles + (pos - s_pref[lo])];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tc_projection_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_h,
+                         const BlockGemmParams p, const GemmConfig c) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 128-byte-swizzled TMA tiles need 1024-byte alignment; the launch reserves
+  // 1 KB of slack for this round-up.
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const GemmLayout L = gemm_layout(c.npad, c.stages, c.nbuild);
+  unsigned char* s_a = smem + L.a;
+  unsigned char* s_b = smem + L.b;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + c.stages;
+  uint64_t* tfull = empty + c.stages;  // [2]
+  uint64_t* tempty = tfull + 2;        // [2]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.tmem);
+  unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
+  int* s_pref = reinterpret_cast<int*>(smem + L.pref);
+  int* s_misc = reinterpret_cast<int*>(smem + L.misc);  // [0] abort, [1] last-CTA flag
+  volatile int* abort_flag = s_misc;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int B = p.batch, V = p.vocab;
+  const bool want_top = (p.top_value != nullptr) | (p.top_index != nullptr) | (p.top_key != nullptr);
+
+  // ---- set-up -------------------------------------------------------------
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_h);
+    for (int s = 0; s < c.stages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, 4);  // one arrival per epilogue warp
+    }
+    fence_mbar_init();
+    s_misc[0] = 0;
+    s_misc[1] = 0;
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, c.tmem_cols);
+    tmem_relinquish();
+  }
+  for (int i = tid; i < kMaxNpad; i += kGemmThreads) s_keys[i] = 0ull;
+  if (!p.dense && warp == 2) {
+    // exclusive prefix of the builder blocks' active-tile counts
+    int carry = 0;
+    for (int j0 = 0; j0 < c.nbuild; j0 += 32) {
+      const int j = j0 + lane;
+      const int v = j < c.nbuild ? p.tile_counts[j] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(FULL_MASK, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (j < c.nbuild) s_pref[j] = carry + incl - v;
+      carry += __shfl_sync(FULL_MASK, incl, 31);
+    }
+    if (lane == 0) s_pref[c.nbuild] = carry;
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *s_tmem;
+  const int total = p.dense ? c.ntiles : s_pref[c.nbuild];
+
+  if (warp == 0) {
+    // ---- TMA producer -------------------------------------------------------
+    if (lane == 0) {
+      uint32_t g = 0;
+      for (int pos = cta; pos < total && !*abort_flag; pos += G) {
+        const int tile = tile_at(p, c, s_pref, pos);
+        for (int kb = 0; kb < c.kblocks; ++kb, ++g) {
+          const int s = (int)(g % (uint32_t)c.stages);
+          const uint32_t use = g / (uint32_t)c.stages;
+          if (use > 0 && !mbar_wait(empty + s, (use - 1) & 1u, abort_flag)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(full + s, kABytes + (uint32_t)c.npad * kTileK * 2u);
+          tma_load_2d(s_a + (size_t)s * kABytes, &tmap_w, kb * kTileK, tile * kTileRows, full + s);
+          tma_load_2d(s_b + (size_t)s * c.npad * kTileK * 2, &tmap_h, kb * kTileK, 0, full + s);
+        }
+      }
+      // Let every issued copy land before the CTA can exit: the stage ring is
+      // fully consumed on the normal path; after an abort, wait for each
+      // stage's last phase (bounded).
+      if (*abort_flag) {
+        const uint32_t issued = g;
+        for (uint32_t k = issued > (uint32_t)c.stages ? issued - c.stages : 0; k < issued; ++k)
+          mbar_wait(full + (k % (uint32_t)c.stages), (k / (uint32_t)c.stages) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ---------------------------------------------------------
+    if (lane == 0) {
+      uint32_t g = 0;
+      int last_stage = -1;
+      uint32_t last_use = 0;
+      int i = 0;
+      for (int pos = cta; pos < total && !*abort_flag; pos += G, ++i) {
+        const int acc = i & 1;
+        const uint32_t ause = (uint32_t)(i >> 1);
+        if (ause > 0 && !mbar_wait(tempty + acc, (ause - 1) & 1u, abort_flag)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t d = tmem_base + (uint32_t)(acc * c.npad);
+        bool ok = true;
+        for (int kb = 0; kb < c.kblocks; ++kb, ++g) {
+          const int s = (int)(g % (uint32_t)c.stages);
+          const uint32_t use = g / (uint32_t)c.stages;
+          if (!mbar_wait(full + s, use & 1u, abort_flag)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint64_t ad = tc_desc_sw128(s_a + (size_t)s * kABytes);
+          const uint64_t bd = tc_desc_sw128(s_b + (size_t)s * c.npad * kTileK * 2);
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k)
+            tc_mma_f16(d, ad + 2ull * k, bd + 2ull * k, c.idesc, (kb | k) != 0);
+          tc_commit(empty + s);  // stage s is free once these MMAs complete
+          last_stage = s;
+          last_use = use;
+        }
+        if (!ok) break;
+        tc_commit(tfull + acc);  // accumulator `acc` is complete
+      }
+      // all tensor-core work of this CTA has finished once the last stage
+      // commit has arrived
+      if (last_stage >= 0) mbar_wait(empty + last_stage, last_use & 1u, nullptr);
+    }
+  } else {
+    // ---- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4) -----------
+    const int q = warp & 3;
+    const int nchunks = c.npad / 32;
+    const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
+    unsigned long long running[kMaxNpad / 32];
+#pragma unroll
+    for (int j = 0; j < kMaxNpad / 32; ++j) running[j] = 0ull;
+    int i = 0;
+    for (int pos = cta; pos < total; pos += G, ++i) {
+      const int acc = i & 1;
+      const uint32_t ause = (uint32_t)(i >> 1);
+      const bool ok = mbar_wait(tfull + acc, ause & 1u, abort_flag);
+      __syncwarp();
+      if (!ok) {
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      tc_fence_after_sync();
+      const int tile = tile_at(p, c, s_pref, pos);
+      const int row = tile * kTileRows + q * 32 + lane;
+      const int word_idx = tile * 4 + q;  // mask word holding this warp's 32 rows
+#pragma unroll
+      for (int ch = 0; ch < kMaxNpad / 32; ++ch) {
+        if (ch < nchunks) {
+          uint32_t v[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * c.npad + ch * 32), v);
+          tmem_ld_wait();
+          const int b0 = ch * 32;
+          uint32_t my_word = 0u;
+          if (b0 + lane < B) {
+            if (!p.mask) my_word = 0xffffffffu;
+            else if (word_idx < p.nw) my_word = __ldg(p.mask + (int64_t)(b0 + lane) * p.mask_stride + word_idx);
+          }
+          unsigned long long key[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int b = b0 + jj;
+            const uint32_t word = __shfl_sync(FULL_MASK, my_word, jj);
+            const bool in = (b < B) && (row < V);
+            const bool legal = in && ((word >> lane) & 1u);
+            const uint16_t bits = legal ? DTypeTraits<T>::round_bits(__uint_as_float(v[jj])) : ninf;
+            if (in && p.logits) static_cast<uint16_t*>(p.logits)[(int64_t)b * p.logits_stride + row] = bits;
+            key[jj] = legal ? top1_key(DTypeTraits<T>::bits_to_float(bits), (uint64_t)(p.vocab_offset + row)) : 0ull;
+          }
+          // transpose-reduce: lane l ends with the max over the warp's 32 rows
+          // of request b0 + l
+#pragma unroll
+          for (int half = 16; half >= 1; half >>= 1) {
+            const bool upper = (lane & half) != 0;
+#pragma unroll
+            for (int j = 0; j < half; ++j) {
+              const unsigned long long send = upper ? key[j] : key[j + half];
+              const unsigned long long keep = upper ? key[j + half] : key[j];
+              const unsigned long long recv = shfl_xor_u64(send, half);
+              key[j] = keep > recv ? keep : recv;
+            }
+          }
+          running[ch] = key[0] > running[ch] ? key[0] : running[ch];
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + acc);
+    }
+    if (want_top) {
+#pragma unroll
+      for (int ch = 0; ch < kMaxNpad / 32; ++ch) {
+        const int b = ch * 32 + lane;
+        if (ch < nchunks && b < B && running[ch] != 0ull) atomicMax(&s_keys[b], running[ch]);
+      }
+    }
+  }
+
+  // ---- teardown: TMEM free, error report, top-1 merge ---------------------
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, c.tmem_cols);
+  }
+  if (*abort_flag) {
+    if (tid == 0 && p.error) atomicExch(p.error, 1);
+    return;
+  }
+  if (!want_top) return;
+  bool did = false;
+  for (int b = tid; b < B; b += kGemmThreads) {
+    const unsigned long long k = s_keys[b];
+    if (k != 0ull) {
+      atomicMax(p.keys + b, k);
+      did = true;
+    }
+  }
+  if (did) __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned int t = atomicAdd(p.ticket, 1u);
+    s_misc[1] = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (s_misc[1]) {
+    __threadfence();
+    for (int b = tid; b < B; b += kGemmThreads) {
+      const unsigned long long k = atomicExch(p.keys + b, 0ull);
+      if (p.top_value) p.top_value[b] = key_value(k);
+      if (p.top_index) p.top_index[b] = key_index(k);
+      if (p.top_key) p.top_key[b] = key_to_signed(k);
+    }
+    if (tid == 0) atomicExch(p.ticket, 0u);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// active-tile builder
+// ---------------------------------------------------------------------------
+constexpr int kBuilderThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kBuilderThreads) tile_builder_kernel(const BlockGemmParams p, int ntiles) {
+  __shared__ uint32_t s_act[kBuilderTiles];
+  __shared__ int s_inactive[kBuilderTiles];
+  __shared__ int s_ninactive;
+  const int tid = threadIdx.x;
+  const int t0 = blockIdx.x * kBuilderTiles;
+  const int V = p.vocab, nw = p.nw, B = p.batch;
+  if (tid < kBuilderTiles) s_act[tid] = 0u;
+  __syncthreads();
+
+  // thread (tile = tid % 32, group = tid / 32) ORs the 4 words of requests
+  // group, group + 8, ... for its tile: loads are independent, one round trip.
+  {
+    const int lt = tid % kBuilderTiles, grp = tid / kBuilderTiles;
+    const int groups = kBuilderThreads / kBuilderTiles;
+    const int t = t0 + lt;
+    uint32_t any = 0u;
+    if (t < ntiles) {
+#pragma unroll 4
+      for (int b = grp; b < B; b += groups) {
+        const uint32_t* row = p.mask + (int64_t)b * p.mask_stride;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int w = t * 4 + j;
+          if (w < nw) any |= tail_clip(__ldg(row + w), w, V);
+        }
+      }
+    }
+    if (any) atomicOr(&s_act[lt], 1u);
+  }
+  __syncthreads();
+  if (tid < 32) {
+    const int t = t0 + tid;
+    const bool valid = t < ntiles;
+    const bool act = valid && s_act[tid] != 0u;
+    const unsigned am = __ballot_sync(FULL_MASK, act);
+    const unsigned im = __ballot_sync(FULL_MASK, valid && !act);
+    const unsigned below = (1u << tid) - 1u;
+    if (act) p.tile_list[t0 + __popc(am & below)] = t;
+    if (valid && !act) s_inactive[__popc(im & below)] = t;
+    if (tid == 0) {
+      p.tile_counts[blockIdx.x] = __popc(am);
+      s_ninactive = __popc(im);
+    }
+  }
+  __syncthreads();
+
+  // -inf over every request's outputs in the inactive tiles of this block
+  if (p.logits) {
+    const int lane = tid & 31, warp = tid >> 5, nwarps = kBuilderThreads / 32;
+    const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 7) == 0) && (p.logits_stride % 4 == 0);
+    const int items = s_ninactive * B;
+    for (int it = warp; it < items; it += nwarps) {
+      const int t = s_inactive[it / B], b = it % B;
+      const int r0 = t * kTileRows;
+      uint16_t* dst = static_cast<uint16_t*>(p.logits) + (int64_t)b * p.logits_stride + r0;
+      if (vec_ok && r0 + kTileRows <= V) {
+        const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
+        reinterpret_cast<uint2*>(dst)[lane] = make_uint2(x, x);
+      } else {
+        for (int r = lane; r < kTileRows && r0 + r < V; r += 32) dst[r] = ninf;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D K-major tensor map [rows, H] with a (64 x box_rows) box and 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, int bf16, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,
+              uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_stride_elems * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kTileK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int smem_optin(int dev) {
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
+    v = 227 * 1024;
+  return v;
+}
+
+template <typename T>
+cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream) {
+  GemmConfig c;
+  c.npad = ((p.batch + 31) / 32) * 32;
+  c.kblocks = (p.hidden_dim + kTileK - 1) / kTileK;
+  c.ntiles = (p.vocab + kTileRows - 1) / kTileRows;
+  c.nbuild = (c.ntiles + kBuilderTiles - 1) / kBuilderTiles;
+  uint32_t cols = 32;
+  while (cols < 2u * (uint32_t)c.npad) cols <<= 1;
+  c.tmem_cols = cols;
+  c.idesc = tc_idesc_f16((uint32_t)c.npad, sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value);
+  const size_t stage_bytes = kABytes + (size_t)c.npad * kTileK * 2;
+  const size_t fixed = gemm_layout(c.npad, 0, c.nbuild).total + 1024 + 2048;
+  c.stages = (int)std::min<size_t>(kMaxStages, ((size_t)smem_optin(dev) - fixed) / stage_bytes);
+  if (c.stages < 2) return cudaErrorInvalidConfiguration;
+  const GemmLayout L = gemm_layout(c.npad, c.stages, c.nbuild);
+
+  const int bf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  CUtensorMap tw, th;
+  if (!make_map(&tw, p.weight, bf16, (uint64_t)p.vocab, (uint64_t)p.hidden_dim, (uint64_t)p.weight_stride, kTileRows) ||
+      !make_map(&th, p.hidden, bf16, (uint64_t)p.batch, (uint64_t)p.hidden_dim, (uint64_t)p.hidden_stride,
+                (uint32_t)c.npad))
+    return cudaErrorInvalidValue;
+
+  cudaError_t err;
+  if (!p.dense) {
+    tile_builder_kernel<T><<<c.nbuild, kBuilderThreads, 0, stream>>>(p, c.ntiles);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  }
+  auto k = tc_projection_kernel<T>;
+  const size_t smem_bytes = L.total + 1024;
+  if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), smem_bytes, dev)) != cudaSuccess) return err;
+  k<<<num_sms(dev), kGemmThreads, smem_bytes, stream>>>(tw, th, p, c);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_typed(const BlockGemmParams& p0, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  // TMA needs 16-byte aligned bases and row pitches; otherwise the row-sparse
+  // kernel computes the same outputs (every legal row, -inf elsewhere).
+  const bool tma_ok = (p0.hidden_dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(p0.weight) & 15) == 0) &&
+                      (p0.weight_stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(p0.hidden) & 15) == 0) &&
+                      (p0.batch == 1 || p0.hidden_stride % 8 == 0);
+  if (!tma_ok) {
+    RowSparseParams r{};
+    r.hidden = p0.hidden;
+    r.hidden_stride = p0.hidden_stride;
+    r.weight = p0.weight;
+    r.weight_stride = p0.weight_stride;
+    r.mask = p0.mask;
+    r.mask_stride = p0.mask_stride;
+    r.batch = p0.batch;
+    r.vocab = p0.vocab;
+    r.hidden_dim = p0.hidden_dim;
+    r.nw = p0.nw;
+    r.vocab_offset = p0.vocab_offset;
+    r.logits = p0.logits;
+    r.logits_stride = p0.logits_stride;
+    r.top_value = p0.top_value;
+    r.top_index = p0.top_index;
+    r.top_key = p0.top_key;
+    r.keys = p0.keys;
+    r.ticket = p0.ticket;
+    r.error = p0.error;
+    return launch_row_sparse(r, std::is_same<T, __nv_bfloat16>::value ? 1 : 0, stream);
+  }
+  // Batches above kMaxNpad run as consecutive chunks of requests.
+  for (int b0 = 0; b0 < p0.batch; b0 += kMaxNpad) {
+    BlockGemmParams p = p0;
+    const int nb = std::min(kMaxNpad, p0.batch - b0);
+    p.batch = nb;
+    p.hidden = static_cast<const uint16_t*>(p0.hidden) + (int64_t)b0 * p0.hidden_stride;
+    if (p0.mask) p.mask = p0.mask + (int64_t)b0 * p0.mask_stride;
+    if (p0.logits) p.logits = static_cast<uint16_t*>(p0.logits) + (int64_t)b0 * p0.logits_stride;
+    if (p0.top_value) p.top_value = p0.top_value + b0;
+    if (p0.top_index) p.top_index = p0.top_index + b0;
+    if (p0.top_key) p.top_key = p0.top_key + b0;
+    p.keys = p0.keys + b0;
+    if ((err = launch_chunk<T>(p, dev, stream)) != cudaSuccess) return err;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t launch_block_gemm(const BlockGemmParams& p, int dtype, cudaStream_t stream) {
+  if (dtype == 1) return launch_typed<__nv_bfloat16>(p, stream);
+  return launch_typed<__half>(p, stream);
+}
+
+}  // namespace gsp

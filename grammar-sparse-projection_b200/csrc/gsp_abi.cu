@@ -29,8 +29,6 @@ int32_t cuda_status(cudaError_t err, const char* where) {
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
-constexpr int kBuilderTiles = 256;  // tiles per active-tile builder block
-
 }  // namespace
 
 int tile_builder_blocks(int vocab) {
@@ -38,12 +36,7 @@ int tile_builder_blocks(int vocab) {
   return (ntiles + kBuilderTiles - 1) / kBuilderTiles;
 }
 
-size_t workspace_bytes(int batch, int vocab) {
-  const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
-  return align256(16 + sizeof(unsigned long long) * (size_t)batch) +
-         align256(sizeof(int32_t) * (size_t)ntiles) +
-         align256(sizeof(int32_t) * (size_t)tile_builder_blocks(vocab));
-}
+size_t workspace_bytes(int batch, int vocab) { return workspace_bytes_for((size_t)batch, (size_t)vocab); }
 
 Workspace carve_workspace(void* base, int batch, int vocab) {
   const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;

@@ -75,6 +75,18 @@ struct Workspace {
   int32_t* tile_counts;
 };
 
+// Active-tile builder granularity: tiles per builder block (one count each).
+constexpr int kBuilderTiles = 32;
+
+constexpr size_t align256c(size_t x) { return (x + 255) / 256 * 256; }
+
+// Workspace bytes for (batch, vocab): ticket + error word + one 64-bit key per
+// request, the compacted active-tile list and the per-builder-block counts.
+constexpr size_t workspace_bytes_for(size_t batch, size_t vocab) {
+  return align256c(16 + 8 * batch) + align256c(4 * ((vocab + 127) / 128)) +
+         align256c(4 * (((vocab + 127) / 128 + kBuilderTiles - 1) / kBuilderTiles));
+}
+
 size_t workspace_bytes(int batch, int vocab);
 Workspace carve_workspace(void* base, int batch, int vocab);
 

@@ -1,0 +1,108 @@
+// Wrappers over the sm_100a 5th-generation tensor-core (tcgen05) and TMA PTX
+// used by the block / dense projection kernel.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+#include "gsp_async.cuh"
+
+namespace gsp {
+
+// ---- tensor memory --------------------------------------------------------
+// Warp-wide: allocates `ncols` TMEM columns (power of two >= 32) and writes the
+// base address to shared memory.
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// ---- MMA ------------------------------------------------------------------
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (A and B both fp16 or both bf16),
+// fp32 accumulation; issued by a single thread.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05 operation this thread issued so far
+// has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation, both operands
+// K-major, M = 128.
+__host__ __device__ constexpr uint32_t tc_idesc_f16(uint32_t n, bool bf16) {
+  return (1u << 4) |                      // D format: F32
+         ((bf16 ? 1u : 0u) << 7) |        // A format: F16 / BF16
+         ((bf16 ? 1u : 0u) << 10) |       // B format
+         ((n >> 3) << 17) |               // N >> 3
+         ((128u >> 4) << 24);             // M >> 4
+}
+
+// Shared-memory matrix descriptor of a K-major tile stored by TMA with the
+// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart. The tile
+// must start on a 1024-byte boundary; advancing K by 16 elements (32 bytes)
+// within the swizzle row adds 2 to the descriptor.
+__device__ __forceinline__ uint64_t tc_desc_sw128(const void* smem_tile) {
+  const uint64_t addr = smem_u32(smem_tile);
+  uint64_t d = (addr >> 4) & 0x3FFFull;     // start address
+  d |= 1ull << 16;                           // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 B
+  d |= 1ull << 46;                           // descriptor version (sm_100)
+  d |= 2ull << 61;                           // 128-byte swizzle
+  return d;
+}
+
+// ---- TMEM -> registers ----------------------------------------------------
+// Warp-wide: thread i of the warp receives 32 consecutive fp32 columns of TMEM
+// lane (lane base + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- TMA ------------------------------------------------------------------
+// Two-dimensional tiled load (no multicast) completing on `bar`. c0 is the
+// inner coordinate in elements; c0 * element size must be a multiple of 16.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+}  // namespace gsp

@@ -29,9 +29,7 @@ namespace {
 // Scratch for batch <= GSP_STATIC_MAX_BATCH and vocab <= GSP_STATIC_MAX_VOCAB:
 // the same layout as the caller-provided workspace (ticket, error word, one
 // 64-bit top-1 key per request, then tile lists), sized for those maxima.
-constexpr size_t kStaticScratchBytes =
-    ((16 + 8 * (size_t)GSP_STATIC_MAX_BATCH + 255) / 256) * 256 +
-    ((4 * (size_t)((GSP_STATIC_MAX_VOCAB + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS) + 255) / 256) * 256 + 256;
+constexpr size_t kStaticScratchBytes = workspace_bytes_for(GSP_STATIC_MAX_BATCH, GSP_STATIC_MAX_VOCAB);
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 

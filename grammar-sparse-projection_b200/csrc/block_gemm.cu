@@ -90,14 +90,18 @@ __host__ __device__ inline GemmLayout gemm_layout(int npad, int stages, int nbui
   return l;
 }
 
-__device__ __forceinline__ int tile_at(const BlockGemmParams& p, const GemmConfig& c, const int* s_pref, int pos) {
-  if (p.dense) return pos;
+// Slot of compacted position `pos` in the workspace tile list (block mode).
+__device__ __forceinline__ int list_slot(const GemmConfig& c, const int* s_pref, int pos) {
   int lo = 0, hi = c.nbuild;  // find j with s_pref[j] <= pos < s_pref[j + 1]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (s_pref[mid] <= pos) lo = mid; else hi = mid;
   }
-  return p.tile_list[lo * kBuilderTiles + (pos - s_pref[lo])];
+  return lo * kBuilderTiles + (pos - s_pref[lo]);
+}
+
+__device__ __forceinline__ int tile_at(const BlockGemmParams& p, const GemmConfig& c, const int* s_pref, int pos) {
+  return p.dense ? pos : p.tile_list[list_slot(c, s_pref, pos)];
 }
 
 template <typename T>
@@ -325,13 +329,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (tid == 0 && p.error) atomicExch(p.error, 1);
     return;
   }
-  if (!want_top) return;
+  // The workspace must be left zero-filled for the next call, whatever its
+  // batch and vocabulary: clear the tile-list slots this CTA consumed (every
+  // reader of them is in this CTA and past the barrier above); the last CTA
+  // clears the per-builder-block counts, which every CTA read at set-up.
+  if (!p.dense)
+    for (int pos = cta + tid * G; pos < total; pos += G * kGemmThreads) p.tile_list[list_slot(c, s_pref, pos)] = 0;
+  if (!want_top && p.dense) return;
   bool did = false;
-  for (int b = tid; b < B; b += kGemmThreads) {
-    const unsigned long long k = s_keys[b];
-    if (k != 0ull) {
-      atomicMax(p.keys + b, k);
-      did = true;
+  if (want_top) {
+    for (int b = tid; b < B; b += kGemmThreads) {
+      const unsigned long long k = s_keys[b];
+      if (k != 0ull) {
+        atomicMax(p.keys + b, k);
+        did = true;
+      }
     }
   }
   if (did) __threadfence();
@@ -343,12 +355,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (s_misc[1]) {
     __threadfence();
-    for (int b = tid; b < B; b += kGemmThreads) {
-      const unsigned long long k = atomicExch(p.keys + b, 0ull);
-      if (p.top_value) p.top_value[b] = key_value(k);
-      if (p.top_index) p.top_index[b] = key_index(k);
-      if (p.top_key) p.top_key[b] = key_to_signed(k);
+    if (want_top) {
+      for (int b = tid; b < B; b += kGemmThreads) {
+        const unsigned long long k = atomicExch(p.keys + b, 0ull);
+        if (p.top_value) p.top_value[b] = key_value(k);
+        if (p.top_index) p.top_index[b] = key_index(k);
+        if (p.top_key) p.top_key[b] = key_to_signed(k);
+      }
     }
+    if (!p.dense)
+      for (int j = tid; j < c.nbuild; j += kGemmThreads) p.tile_counts[j] = 0;
     if (tid == 0) atomicExch(p.ticket, 0u);
   }
 }

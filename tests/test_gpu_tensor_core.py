@@ -80,11 +80,15 @@ def test_batched_clustered_workload(cuda_device, batch):
     mask = O.make_batch_mask(rng, batch, vocab, [1242] * batch, clustered=True, max_runs=16)
     md = torch.from_numpy(mask).to(cuda_device)
     exact = O.masked_logits_exact(hd.cpu(), wd.cpu(), mask)
+    results = {}
     for fn in (_native.block_gemm, _native.dense_masked, _native.row_sparse):
         logits, tv, ti = _run(fn, hd, wd, md)
         _check(exact, logits, torch.float16, fn.__name__)
         assert torch.equal(ti, logits.argmax(-1))
+        results[fn.__name__] = (tv, ti)
+    # top-1 without materialising logits: identical to the same kernel's with-logits run
     _, tv2, ti2 = _run(_native.block_gemm, hd, wd, md, with_logits=False)
+    tv, ti = results["block_gemm"]
     assert torch.equal(ti2, ti) and torch.equal(tv2, tv)
 
 
@@ -148,6 +152,22 @@ def test_adaptive_dispatch_known_answers(cuda_device):
                                                     full_word_fraction=frac, policy="b200")
         assert route_b in tr.ROUTES
         _check(O.masked_logits_exact(h, w, mask.numpy()), got_b.reshape(batch, -1), torch.float16, route_b)
+
+
+def test_workspace_reuse_across_batch_sizes(cuda_device):
+    """One workspace serves calls of different batch sizes and routes: the
+    block path must leave its tile lists zeroed, or a later, larger batch reads
+    them back as top-1 keys."""
+    rng = np.random.default_rng(5)
+    vocab, hidden = 3000, 128
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half().to(cuda_device)
+    for batch in (44, 256, 3, 300, 17):
+        h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).half().to(cuda_device)
+        mask = torch.from_numpy(O.recipe_mask("random+zero+u5+full+c40", rng, batch, vocab)).to(cuda_device)
+        for fn in (_native.block_gemm, _native.dense_masked, _native.row_sparse):
+            logits, tv, ti = _run(fn, h, w, mask)
+            assert torch.equal(ti, logits.argmax(-1)), (batch, fn.__name__)
+            assert torch.equal(tv, logits.float().gather(1, ti[:, None])[:, 0]), (batch, fn.__name__)
 
 
 def test_no_bounded_wait_gave_up_tensor_core(cuda_device):

@@ -65,6 +65,9 @@ def parse_args():
     ap.add_argument("--copies", type=int, default=32, help="weight copies cycled through (one GPU)")
     ap.add_argument("--sweep-steps", type=int, default=100)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--only", choices=("batched", "mixed"), default=None,
+                    help="run one extra section alone (small; for profiling)")
+    ap.add_argument("--batch", type=int, default=32, help="batch of --only batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -246,6 +249,18 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.only:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        peak, _ = read_peaks()
+        if args.only == "batched":
+            g = torch.Generator(device=dev).manual_seed(1234)
+            weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(2)]
+            res = batched_section(dev, weights, peak, steps=max(args.steps, 1), batches=(args.batch,))
+        else:
+            res = mixed_section(dev, peak, steps=max(args.steps, 1))
+        print(json.dumps({"only": args.only, "result": res}), flush=True)
+        return 0
 
     from gsp import _native
     from gsp import vocab_parallel as vp
@@ -403,6 +418,8 @@ def main():
         roofline = None
 
     sweep = None
+    batched = None
+    mixed = None
     same_gpu_dense = None
     cpu_base = None
     if world == 1 and not args.no_sweep:
@@ -421,6 +438,8 @@ def main():
                               "frac_of_hbm": lb / (t_us * 1e-6) / 1e9 / peak,
                               "cold_us_per_step": statistics.mean(ts)})
         same_gpu_dense = time_dense_baseline(dev, weight, hidden, masks, args)
+        batched = batched_section(dev, weights[:8], peak)
+        mixed = mixed_section(dev, peak)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         w_cpu = weight.cpu().numpy()
         h_cpu = hidden.cpu().numpy()
@@ -445,6 +464,8 @@ def main():
             "cold": cold,
             "timed_region_wall_s": t_wall,
             "sweep": sweep,
+            "batched": batched,
+            "mixed": mixed,
             "same_gpu_dense_mask": same_gpu_dense,
         }
         print(json.dumps(line), flush=True)
@@ -465,6 +486,142 @@ def max_over_ranks(x: float, world: int) -> float:
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return float(t.item())
+
+
+def graph_time_us(dev, n, fn):
+    """n calls of fn(i) captured in one CUDA graph; events around one replay (us)."""
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)  # creates this stream's workspace before capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for i in range(n):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    b.synchronize()
+    del graph
+    return a.elapsed_time(b) * 1e3
+
+
+def eager_time_us(n, fn):
+    """Median of n eager calls, each bracketed by its own events (us)."""
+    ts = []
+    for i in range(n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn(i)
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3)
+    return statistics.median(ts)
+
+
+def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
+    """Batched decode at V=248,320, H=2,048 fp16: every request 0.5% legal in
+    <= 16 clustered runs. Times each route, reports the active-tile fraction,
+    the block kernel's roofline and whether the B200 cost model picked the
+    measured best route."""
+    from gsp import _native, triton_runtime as tr
+    from oracle import gsp_oracle as O
+    import torch.nn.functional as F
+    out = []
+    ntiles = (VOCAB + 127) // 128
+    for batch in batches:
+        rng = np.random.default_rng(300 + batch)
+        masks_np = [O.make_batch_mask(rng, batch, VOCAB, [1242] * batch, clustered=True, max_runs=16) for _ in range(8)]
+        masks = [torch.from_numpy(m).to(dev) for m in masks_np]
+        active = [O.active_tiles(m, VOCAB) for m in masks_np]
+        legal = [O.unpack_bitmask(m, VOCAB).sum(axis=1) for m in masks_np]
+        hidden = torch.randn(batch, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(batch)).half()
+        logits = torch.empty(batch, VOCAB, device=dev, dtype=torch.float16)
+        tv = torch.empty(batch, device=dev, dtype=torch.float32)
+        ti = torch.empty(batch, device=dev, dtype=torch.int64)
+        routes = {"block-sparse": _native.block_gemm, "dense-mask": _native.dense_masked, "row-sparse": _native.row_sparse}
+        times = {}
+        for name, fn in routes.items():
+            times[name] = graph_time_us(dev, steps, lambda i, fn=fn: fn(hidden, weights[i % len(weights)], masks[i % 8],
+                                                                         logits=logits, top_value=tv, top_index=ti)) / steps
+        try:
+            import xgrammar as xgr
+
+            def ref_dense(i):
+                lg = F.linear(hidden, weights[i % len(weights)])
+                xgr.apply_token_bitmask_inplace(lg, masks[i % 8], vocab_size=VOCAB, backend="triton")
+            ref_dense(0)
+            times["cublas+xgrammar"] = eager_time_us(10, ref_dense)
+        except Exception as exc:  # pragma: no cover - optional comparison
+            times["cublas+xgrammar"] = None
+        mean_active = float(np.mean(active))
+        block_bytes = mean_active * 128 * HIDDEN * 2
+        best = min(("block-sparse", "dense-mask", "row-sparse"), key=lambda r: times[r])
+        choice = tr.choose_route(batch, VOCAB, HIDDEN, 2, legal[0].tolist(), active[0])
+        out.append({
+            "batch": batch, "active_tile_fraction": mean_active / ntiles,
+            "us_per_step": {k: v for k, v in times.items()},
+            "block_roofline": {"achieved_gbs": block_bytes / (times["block-sparse"] * 1e-6) / 1e9,
+                               "frac": block_bytes / (times["block-sparse"] * 1e-6) / 1e9 / peak,
+                               "algorithmic_bytes": block_bytes},
+            "dense_roofline_frac": VOCAB * HIDDEN * 2 / (times["dense-mask"] * 1e-6) / 1e9 / peak,
+            "speedup_block_vs_cublas_xgrammar": (times["cublas+xgrammar"] / times["block-sparse"]
+                                                 if times["cublas+xgrammar"] else None),
+            "tokens_per_s": batch / (times[best] * 1e-6),
+            "best_route": best, "b200_policy_route": choice,
+        })
+    return out
+
+
+def mixed_section(dev, peak, steps=10):
+    """Mixed-density dispatcher sweep: V=151,936, H=1,024 bf16, batch 64;
+    a seeded mix of near-unconstrained (95% uniform) and constrained (0.2% in
+    <= 16 runs) requests. Reports each route's time and both policies' picks."""
+    from gsp import _native, triton_runtime as tr
+    from oracle import gsp_oracle as O
+    vocab, hidden, batch = 151936, 1024, 64
+    g = torch.Generator(device=dev).manual_seed(5)
+    weights = [(torch.randn(vocab, hidden, device=dev, generator=g) * 0.02).bfloat16() for _ in range(4)]
+    h = torch.randn(batch, hidden, device=dev, generator=g).bfloat16()
+    logits = torch.empty(batch, vocab, device=dev, dtype=torch.bfloat16)
+    tv = torch.empty(batch, device=dev, dtype=torch.float32)
+    ti = torch.empty(batch, device=dev, dtype=torch.int64)
+    out = []
+    for frac in (0.0, 0.25, 0.5, 0.75, 1.0):
+        rng = np.random.default_rng(int(frac * 100))
+        n_con = int(round(frac * batch))
+        masks_np = []
+        for _ in range(4):
+            legal = np.zeros((batch, vocab), dtype=bool)
+            order = rng.permutation(batch)
+            for j, b in enumerate(order):
+                ids = (O.clustered_legal_ids(rng, vocab, int(0.002 * vocab), 16) if j < n_con
+                       else O.uniform_legal_ids(rng, vocab, int(0.95 * vocab)))
+                legal[b, ids] = True
+            masks_np.append(O.pack_bitmask(legal))
+        masks = [torch.from_numpy(m).to(dev) for m in masks_np]
+        times = {}
+        for name, fn in (("block-sparse", _native.block_gemm), ("dense-mask", _native.dense_masked),
+                         ("row-sparse", _native.row_sparse)):
+            times[name] = graph_time_us(dev, steps, lambda i, fn=fn: fn(h, weights[i % 4], masks[i % 4], logits=logits,
+                                                                       top_value=tv, top_index=ti)) / steps
+        best = min(times, key=times.get)
+        fwf = tr.full_word_fraction_cpu(torch.from_numpy(masks_np[0]))
+        ref_route = tr._reference_route(batch, fwf, 0.80)
+        stats_legal = O.unpack_bitmask(masks_np[0], vocab).sum(axis=1).tolist()
+        b200_route = tr.choose_route(batch, vocab, hidden, 2, stats_legal, O.active_tiles(masks_np[0], vocab))
+        out.append({"constrained_fraction": frac, "us_per_step": times, "best_route": best,
+                    "reference_policy_route": ref_route, "reference_policy_us": times[ref_route],
+                    "b200_policy_route": b200_route, "b200_policy_us": times[b200_route],
+                    "tokens_per_s_best": batch / (times[best] * 1e-6)})
+    del weights
+    return out
 
 
 def time_dense_baseline(dev, weight, hidden, masks, args):

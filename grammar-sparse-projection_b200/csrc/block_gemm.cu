@@ -151,6 +151,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_relinquish();
   }
   for (int i = tid; i < kMaxNpad; i += kGemmThreads) s_keys[i] = 0ull;
+  // Everything above overlaps the tile builder; from here on its outputs (and
+  // the inactive-tile -inf fill) are complete and visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (!p.dense && warp == 2) {
     // exclusive prefix of the builder blocks' active-tile counts
     int carry = 0;
@@ -422,21 +425,27 @@ __global__ void __launch_bounds__(kBuilderThreads) tile_builder_kernel(const Blo
   }
   __syncthreads();
 
-  // -inf over every request's outputs in the inactive tiles of this block
+  // The projection kernel may start its set-up now (programmatic dependent
+  // launch); its griddepcontrol.wait still waits for this grid to finish.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  // -inf over every request's outputs in the inactive tiles of this block:
+  // a warp takes one inactive tile and sweeps all requests (256 B per store).
   if (p.logits) {
     const int lane = tid & 31, warp = tid >> 5, nwarps = kBuilderThreads / 32;
     const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
+    const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 7) == 0) && (p.logits_stride % 4 == 0);
-    const int items = s_ninactive * B;
-    for (int it = warp; it < items; it += nwarps) {
-      const int t = s_inactive[it / B], b = it % B;
-      const int r0 = t * kTileRows;
-      uint16_t* dst = static_cast<uint16_t*>(p.logits) + (int64_t)b * p.logits_stride + r0;
+    for (int i = warp; i < s_ninactive; i += nwarps) {
+      const int r0 = s_inactive[i] * kTileRows;
+      uint16_t* base = static_cast<uint16_t*>(p.logits) + r0;
       if (vec_ok && r0 + kTileRows <= V) {
-        const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
-        reinterpret_cast<uint2*>(dst)[lane] = make_uint2(x, x);
+#pragma unroll 4
+        for (int b = 0; b < B; ++b)
+          reinterpret_cast<uint2*>(base + (int64_t)b * p.logits_stride)[lane] = make_uint2(x, x);
       } else {
-        for (int r = lane; r < kTileRows && r0 + r < V; r += 32) dst[r] = ninf;
+        for (int b = 0; b < B; ++b)
+          for (int r = lane; r < kTileRows && r0 + r < V; r += 32) base[(int64_t)b * p.logits_stride + r] = ninf;
       }
     }
   }
@@ -516,8 +525,17 @@ cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream)
   auto k = tc_projection_kernel<T>;
   const size_t smem_bytes = L.total + 1024;
   if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), smem_bytes, dev)) != cudaSuccess) return err;
-  k<<<num_sms(dev), kGemmThreads, smem_bytes, stream>>>(tw, th, p, c);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms(dev));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = p.dense ? 0 : 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, tw, th, p, c);
 }
 
 template <typename T>

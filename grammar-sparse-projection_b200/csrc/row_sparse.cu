@@ -10,23 +10,22 @@
 // [c*U/G, (c+1)*U/G), so legal rows are split evenly across SMs whether they
 // are spread uniformly or packed into a few runs.
 //
-// row_sparse_staged_kernel (fast path: 16-byte aligned operands, mask and
-// hidden states fit in shared memory)
-//   0. warp 0 decodes the CTA's own slice of the mask and fires
-//      cp.async.bulk.prefetch.L2 for up to kPrefetchCap legal rows of it, so
-//      the DRAM and address-translation latency of those rows overlaps the
-//      scan (under uniform masks they are the rows the CTA ends up owning);
-//   1. the CTA copies the whole packed mask (tail bits cleared) and the hidden
-//      states into shared memory with coalesced 16-byte loads: one round trip;
-//   2. one bank-conflict-free pass (warp-contiguous words, lane-strided)
-//      writes every word's warp-local exclusive popcount prefix; a 16-entry
-//      scan of the warp totals turns them into global ranks;
-//   3. every thread checks its warp's words against the CTA's rank range and
-//      emits the units of the overlapping words into a shared list;
-//   4. each warp streams two whole rows at a time with L1-bypassing 16-byte
+// row_sparse_staged_kernel (fast path: 16-byte aligned operands, at most
+// 16,384 mask words, i.e. B * ceil(V/32) <= 16384)
+//   1. every thread loads 16 or 32 consecutive words of the flat (request,
+//      word) mask into registers with 16-byte loads (one round trip), and the
+//      hidden states go to shared memory;
+//   2. (no prefetch: prefetching the CTA's own legal rows into L2 before the
+//      scan was measured slower than not doing it);
+//   3. one block-wide scan of per-thread popcounts gives every thread the
+//      rank of its first legal unit; words and per-word rank prefixes are
+//      staged in shared memory with 16-byte stores;
+//   4. the threads holding the CTA's first and last rank publish its word
+//      range, and every thread emits the units of one word of it;
+//   5. each warp streams two whole rows at a time with L1-bypassing 16-byte
 //      loads, dots them against h in shared memory and reduces with shuffles;
-//   5. -inf is written over the illegal entries of the CTA's slice of the output;
-//   6. greedy top-1 keys (rounded value, inverted index) are kept per warp,
+//   6. -inf is written over the illegal entries of the CTA's slice of the output;
+//   7. greedy top-1 keys (rounded value, inverted index) are kept per warp,
 //      merged in shared memory and then with one global atomicMax per request;
 //      the last CTA to arrive decodes them and re-zeroes the workspace.
 //
@@ -46,8 +45,7 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kListCap = 2048;      // units extracted per round
 constexpr int kUnroll = 8;          // 16-byte loads per lane per pass over a row
-constexpr int kPrefetchCap = 32;    // rows per CTA prefetched into L2 before the scan
-constexpr size_t kStagedSmemMax = 200 * 1024;  // mask + prefix + hidden + list
+constexpr size_t kStagedSmemMax = 200 * 1024;  // list + keys + mask slice + hidden states
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -220,16 +218,42 @@ __device__ __forceinline__ void stream_rows_scalar(const RowSparseParams& p, con
   if (lane == 0) top.flush(s_keys);
 }
 
+// Block-wide exclusive scan of one value per thread (kThreads threads);
+// writes the block total to *total. Contains two __syncthreads.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(FULL_MASK, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t x = lane < kWarps ? s_warp[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(FULL_MASK, x, o);
+      if (lane >= o) x += t;
+    }
+    if (lane < kWarps) s_warp[lane] = x;
+  }
+  __syncthreads();
+  *total = s_warp[kWarps - 1];
+  return incl - v + (warp > 0 ? s_warp[warp - 1] : 0u);
+}
+
 // ===========================================================================
 // staged kernel
 // ===========================================================================
 struct StagedLayout {
-  size_t list, keys, warp, misc, mask, prefix, hidden, total;
+  size_t list, keys, warp, misc, words, pre, hidden, total;
 };
 
-__host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim, int nw, bool has_mask) {
+// `words` = number of mask words staged (kThreads * words per thread).
+__host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim, int words) {
   StagedLayout l;
-  const size_t F = has_mask ? (size_t)batch * nw : 0;
   size_t off = 0;
   l.list = off;
   off += 4 * (size_t)kListCap;
@@ -239,89 +263,86 @@ __host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim,
   off = l.warp + 4 * 32;
   l.misc = align_up(off, 16);
   off = l.misc + 16;
-  l.mask = align_up(off, 16);
-  off = l.mask + 4 * F;
-  l.prefix = align_up(off, 16);
-  off = l.prefix + 4 * F;
+  l.words = align_up(off, 16);
+  off = l.words + 4 * (size_t)words;
+  l.pre = align_up(off, 16);
+  off = l.pre + 4 * (size_t)words;
   l.hidden = align_up(off, 16);
   off = l.hidden + 2 * (size_t)batch * hidden_dim;
   l.total = align_up(off, 128);
   return l;
 }
 
-template <typename T>
+// Slot of flat word f in the transposed staging layout (kWpt words per thread,
+// 16-byte vector v of thread t at vector index v * kThreads + t).
+template <int kWpt>
+__device__ __forceinline__ int staged_index(int f) {
+  const int t = f / kWpt, r = f - t * kWpt;
+  return ((r >> 2) * kThreads + t) * 4 + (r & 3);
+}
+
+// kV 16-byte mask vectors (4 * kV words) per thread: the whole flat
+// (request, word) mask lives in the CTA's registers, kThreads * 4 * kV words.
+template <typename T, int kV>
 __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const RowSparseParams p) {
+  constexpr int kWpt = 4 * kV;  // words per thread
   extern __shared__ __align__(1024) unsigned char smem[];
-  const bool has_mask = p.mask != nullptr;
-  const StagedLayout L = staged_layout(p.batch, p.hidden_dim, p.nw, has_mask);
+  const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * kWpt);
   uint32_t* s_list = reinterpret_cast<uint32_t*>(smem + L.list);
   unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
   uint32_t* s_warp = reinterpret_cast<uint32_t*>(smem + L.warp);
   int* s_misc = reinterpret_cast<int*>(smem + L.misc);
-  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + L.mask);
-  uint32_t* s_prefix = reinterpret_cast<uint32_t*>(smem + L.prefix);
+  uint32_t* s_words = reinterpret_cast<uint32_t*>(smem + L.words);
+  uint32_t* s_pre = reinterpret_cast<uint32_t*>(smem + L.pre);
   uint16_t* s_h = reinterpret_cast<uint16_t*>(smem + L.hidden);
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const int G = gridDim.x, cta = blockIdx.x;
   const int B = p.batch, V = p.vocab, H = p.hidden_dim, nw = p.nw;
   const int nvec = H / 8;
+  const bool has_mask = p.mask != nullptr;
   const bool want_top = (p.top_value != nullptr) | (p.top_index != nullptr) | (p.top_key != nullptr);
-  const int F = has_mask ? B * nw : 0;  // < 2^27: batch * nw * 32 < 2^32 is checked on the host
+  const int F = has_mask ? B * nw : 0;  // <= kThreads * kWpt (checked on the host)
   const int w_lo = (int)((int64_t)F * cta / G), w_hi = (int)((int64_t)F * (cta + 1) / G);
   const uint32_t tail_keep = (V & 31) ? ((1u << (V & 31)) - 1u) : 0xffffffffu;
+  const int f0 = tid * kWpt;  // this thread's words: flat [f0, f0 + kWpt)
 
-  // ---- 0. L2 prefetch of the legal rows in this CTA's own slice ------------
-  if (has_mask && warp == 0) {
-    int issued = 0;
-    for (int f0 = w_lo; f0 < w_hi && issued < kPrefetchCap; f0 += 32) {
-      const int f = f0 + lane;
-      uint32_t word = 0;
-      int w = 0;
-      if (f < w_hi) {
-        const int b = f / nw;
-        w = f - b * nw;
-        word = __ldg(p.mask + (int64_t)b * p.mask_stride + w);
-        if (w == nw - 1) word &= tail_keep;
-      }
-      const uint32_t pc = __popc(word);
-      uint32_t before = pc;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(FULL_MASK, before, o);
-        if (lane >= o) before += t;
-      }
-      before -= pc;  // exclusive prefix within this group of 32 words
-      while (word && issued + (int)before < kPrefetchCap) {
-        const int bit = __ffs(word) - 1;
-        word &= word - 1;
-        bulk_prefetch_l2(static_cast<const uint16_t*>(p.weight) + (int64_t)(w * 32 + bit) * p.weight_stride,
-                         (uint32_t)H * 2u);
-        ++before;
-      }
-      issued += (int)__shfl_sync(FULL_MASK, before, 31);
-    }
-  }
-
-  // ---- 1. mask (tail bits cleared) and hidden states -> shared memory ------
+  // ---- 1. loads: this thread's mask words (registers), hidden states (smem) --
+  uint32_t wd[kWpt];
   if (has_mask) {
     const bool vec = ((reinterpret_cast<uintptr_t>(p.mask) & 15) == 0) && (nw % 4 == 0) &&
                      (B == 1 || p.mask_stride % 4 == 0);
     if (vec) {
-      const int q = nw / 4;
-      for (int i = tid; i < B * q; i += kThreads) {
-        const int b = i / q, j = i - b * q;
-        uint4 v = __ldg(reinterpret_cast<const uint4*>(p.mask + (int64_t)b * p.mask_stride) + j);
-        if (j == q - 1) v.w &= tail_keep;
-        reinterpret_cast<uint4*>(s_mask)[i] = v;
+#pragma unroll
+      for (int v = 0; v < kV; ++v) {
+        const int f = f0 + 4 * v;
+        uint4 x = make_uint4(0, 0, 0, 0);
+        if (f < F) {
+          const int b = f / nw, w = f - b * nw;  // w % 4 == 0
+          x = __ldg(reinterpret_cast<const uint4*>(p.mask + (int64_t)b * p.mask_stride + w));
+          if (w == nw - 4) x.w &= tail_keep;
+        }
+        wd[4 * v] = x.x;
+        wd[4 * v + 1] = x.y;
+        wd[4 * v + 2] = x.z;
+        wd[4 * v + 3] = x.w;
       }
     } else {
-      for (int i = tid; i < F; i += kThreads) {
-        const int b = i / nw, w = i - b * nw;
-        const uint32_t v = __ldg(p.mask + (int64_t)b * p.mask_stride + w);
-        s_mask[i] = (w == nw - 1) ? (v & tail_keep) : v;
+#pragma unroll
+      for (int j = 0; j < kWpt; ++j) {
+        const int f = f0 + j;
+        uint32_t x = 0u;
+        if (f < F) {
+          const int b = f / nw, w = f - b * nw;
+          x = __ldg(p.mask + (int64_t)b * p.mask_stride + w);
+          if (w == nw - 1) x &= tail_keep;
+        }
+        wd[j] = x;
       }
     }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kWpt; ++j) wd[j] = 0u;
   }
   for (int i = tid; i < B * nvec; i += kThreads) {
     const int b = i / nvec, j = i - b * nvec;
@@ -329,50 +350,47 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
         reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
   }
   for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
-  __syncthreads();
 
-  // ---- 2. one-pass scan: warp-local exclusive prefixes, then warp bases ----
-  const int per_warp = ((F + kWarps * 32 - 1) / (kWarps * 32)) * 32;
-  const int wbeg = min(warp * per_warp, F), wend = min(wbeg + per_warp, F);
-  {
-    uint32_t run = 0;
-    for (int f0 = wbeg; f0 < wend; f0 += 32) {
-      const int f = f0 + lane;
-      const uint32_t pc = f < wend ? __popc(s_mask[f]) : 0u;
-      uint32_t incl = pc;
+  uint32_t cnt = 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(FULL_MASK, incl, o);
-        if (lane >= o) incl += t;
-      }
-      if (f < wend) s_prefix[f] = run + incl - pc;
-      run += __shfl_sync(FULL_MASK, incl, 31);
-    }
-    if (lane == 0) s_warp[warp] = run;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    uint32_t x = lane < kWarps ? s_warp[lane] : 0u;
-    uint32_t incl = x;
+  for (int j = 0; j < kWpt; ++j) cnt += __popc(wd[j]);
+
+  // ---- 3. one block scan of per-thread counts -----------------------------
+  uint32_t tot;
+  const uint32_t excl = block_exclusive_scan(cnt, s_warp, &tot);  // contains __syncthreads
+  const uint64_t total = has_mask ? (uint64_t)tot : (uint64_t)B * V;
+  // words and their exclusive rank prefixes -> shared memory, so that
+  // extraction and the -inf fill run one word per thread. Layout: the 16-byte
+  // vector v of thread t sits at vector index v * kThreads + t (conflict-free
+  // stores); staged_index() maps a flat word index to its slot.
+  if (has_mask) {
+    uint32_t run = excl;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_up_sync(FULL_MASK, incl, o);
-      if (lane >= o) incl += t;
+    for (int v = 0; v < kV; ++v) {
+      uint4 pr;
+      pr.x = run;
+      run += __popc(wd[4 * v]);
+      pr.y = run;
+      run += __popc(wd[4 * v + 1]);
+      pr.z = run;
+      run += __popc(wd[4 * v + 2]);
+      pr.w = run;
+      run += __popc(wd[4 * v + 3]);
+      reinterpret_cast<uint4*>(s_words)[v * kThreads + tid] = make_uint4(wd[4 * v], wd[4 * v + 1], wd[4 * v + 2], wd[4 * v + 3]);
+      reinterpret_cast<uint4*>(s_pre)[v * kThreads + tid] = pr;
     }
-    if (lane < kWarps) s_warp[lane] = incl - x;        // exclusive base of warp `lane`
-    if (lane == kWarps - 1) s_misc[2] = (int)incl;      // total legal units
   }
-  __syncthreads();
-  const uint32_t my_base = s_warp[warp];
-  const uint64_t total = has_mask ? (uint64_t)(uint32_t)s_misc[2] : (uint64_t)B * V;
   if (p.offsets != nullptr && cta == 0) {
-    for (int b = tid; b < B; b += kThreads) {
-      if (has_mask) {
-        const int f = b * nw;
-        p.offsets[b] = (int64_t)s_prefix[f] + s_warp[f / per_warp];
-      } else {
-        p.offsets[b] = (int64_t)b * V;
+    if (has_mask) {
+      uint32_t run = excl;
+#pragma unroll
+      for (int j = 0; j < kWpt; ++j) {
+        const int f = f0 + j;
+        if (f < F && f % nw == 0) p.offsets[f / nw] = run;
+        run += __popc(wd[j]);
       }
+    } else {
+      for (int b = tid; b < B; b += kThreads) p.offsets[b] = (int64_t)b * V;
     }
     if (tid == 0) p.offsets[B] = (int64_t)total;
   }
@@ -384,16 +402,35 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   for (uint64_t rbase = lo; rbase < hi; rbase += kListCap) {
     const uint64_t rend = min(hi, rbase + (uint64_t)kListCap);
     const int n = (int)(rend - rbase);
-    // ---- 3. extraction over the warp's own words --------------------------
+    // ---- 4. extraction: the owners of ranks rbase and rend - 1 publish the
+    //         word range, then every thread emits the units of one word ------
     if (has_mask) {
       const uint32_t rb32 = (uint32_t)rbase, re32 = (uint32_t)rend;  // ranks < 2^32
-      for (int f = wbeg + lane; f < wend; f += 32) {
-        const uint32_t pre = s_prefix[f] + my_base;
-        if (pre >= re32) break;  // prefixes grow along the warp's run
-        uint32_t word = s_mask[f];
-        if (pre + __popc(word) <= rb32) continue;
+      if (excl <= rb32 && rb32 < excl + cnt) {
+        uint32_t r = excl;
+#pragma unroll
+        for (int j = 0; j < kWpt; ++j) {
+          const uint32_t pc = __popc(wd[j]);
+          if (r <= rb32 && rb32 < r + pc) s_misc[2] = f0 + j;
+          r += pc;
+        }
+      }
+      if (excl <= re32 - 1 && re32 - 1 < excl + cnt) {
+        uint32_t r = excl;
+#pragma unroll
+        for (int j = 0; j < kWpt; ++j) {
+          const uint32_t pc = __popc(wd[j]);
+          if (r <= re32 - 1 && re32 - 1 < r + pc) s_misc[3] = f0 + j;
+          r += pc;
+        }
+      }
+      __syncthreads();
+      const int fa = s_misc[2], fb = s_misc[3];
+      for (int f = fa + tid; f <= fb; f += kThreads) {
+        const int si = staged_index<kWpt>(f);
+        uint32_t word = s_words[si];
+        uint32_t r = s_pre[si];
         const int b = f / nw, w = f - b * nw;
-        uint32_t r = pre;
         while (word) {
           const int bit = __ffs(word) - 1;
           word &= word - 1;
@@ -409,14 +446,15 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
       }
     }
     __syncthreads();
-    // ---- 4. stream the rows ------------------------------------------------
+    // ---- 5. stream the rows ------------------------------------------------
     stream_rows<T, true>(p, s_list, n, rbase, code_stride, s_h, want_top, s_keys);
     __syncthreads();
   }
 
-  // ---- 5. -inf over the illegal entries of this CTA's output slice ---------
-  if (p.logits && has_mask) fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_mask[f]; });
-  // ---- 6. top-1 ------------------------------------------------------------
+  // ---- 6. -inf over the illegal entries of this CTA's output slice ---------
+  if (p.logits && has_mask)
+    fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_words[staged_index<kWpt>((int)f)]; });
+  // ---- 7. top-1 ------------------------------------------------------------
   if (want_top) finalize_top1(p, s_keys, s_misc);
 }
 
@@ -567,11 +605,19 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
                    (p.weight_stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.hidden) & 15) == 0) &&
                    (p.batch == 1 || p.hidden_stride % 8 == 0);
   if (vec) {
-    const StagedLayout L = staged_layout(p.batch, p.hidden_dim, p.nw, p.mask != nullptr);
-    if (L.total <= kStagedSmemMax) {
-      auto k = row_sparse_staged_kernel<T>;
-      if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
-      k<<<grid, kThreads, L.total, stream>>>(p);
+    const int F = p.mask ? p.batch * p.nw : 0;
+    const int wpt = F <= kThreads * 16 ? 16 : 32;
+    const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * wpt);
+    if (L.total <= kStagedSmemMax && F <= kThreads * 32) {
+      if (wpt == 16) {
+        auto k = row_sparse_staged_kernel<T, 4>;
+        if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
+        k<<<grid, kThreads, L.total, stream>>>(p);
+      } else {
+        auto k = row_sparse_staged_kernel<T, 8>;
+        if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
+        k<<<grid, kThreads, L.total, stream>>>(p);
+      }
       return cudaGetLastError();
     }
   }

@@ -49,6 +49,14 @@ Workspace carve_workspace(void* base, int batch, int vocab) {
   w.tile_list = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * (size_t)ntiles);
   w.tile_counts = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * (size_t)((ntiles + kBuilderTiles - 1) / kBuilderTiles));
+  w.slice_counts = reinterpret_cast<unsigned int*>(p);
+  w.published = reinterpret_cast<unsigned int*>(p + sizeof(unsigned int) * kMaxSlices + 128);
+  p += align256(sizeof(unsigned int) * kMaxSlices + 256);
+  w.slice_ready = reinterpret_cast<unsigned int*>(p);
+  p += align256(sizeof(unsigned int) * kMaxSlices * kFlagStride);
+  w.unit_list = reinterpret_cast<uint32_t*>(p);
+  w.list_cap = (int64_t)unit_list_cap((size_t)batch, (size_t)vocab);
   return w;
 }
 
@@ -155,6 +163,18 @@ RowSparseParams make_row_sparse(const void* hidden, int64_t hidden_row_stride, c
   return p;
 }
 
+void attach_workspace(RowSparseParams& p, void* workspace) {
+  const Workspace w = carve_workspace(workspace, p.batch, p.vocab);
+  p.keys = w.keys;
+  p.ticket = w.ticket;
+  p.error = w.error;
+  p.slice_counts = w.slice_counts;
+  p.published = w.published;
+  p.slice_ready = w.slice_ready;
+  p.unit_list = w.unit_list;
+  p.list_cap = w.list_cap;
+}
+
 int32_t projection_common(const char* fn, bool tensor_core, int dense, const void* hidden,
                           int64_t hidden_row_stride, const void* weight, int64_t weight_row_stride,
                           const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch,
@@ -179,12 +199,7 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
     p.top_value = top_value;
     p.top_index = top_index;
     p.top_key = top_key;
-    if (workspace) {
-      Workspace w = carve_workspace(workspace, batch, vocab);
-      p.keys = w.keys;
-      p.ticket = w.ticket;
-      p.error = w.error;
-    }
+    if (workspace) attach_workspace(p, workspace);
     return cuda_status(launch_row_sparse(p, dtype, s), fn);
   }
   BlockGemmParams p;
@@ -283,12 +298,7 @@ int32_t gsp_row_sparse_compact(const void* hidden, int64_t hidden_row_stride, co
   p.top_value = top_value;
   p.top_index = top_index;
   p.top_key = top_key;
-  if (workspace) {
-    Workspace w = carve_workspace(workspace, batch, vocab);
-    p.keys = w.keys;
-    p.ticket = w.ticket;
-    p.error = w.error;
-  }
+  if (workspace) attach_workspace(p, workspace);
   return cuda_status(launch_row_sparse(p, dtype, static_cast<cudaStream_t>(stream)), fn);
 }
 

@@ -36,6 +36,16 @@ struct RowSparseParams {
   unsigned long long* keys;
   unsigned int* ticket;
   int* error;  // set non-zero when a bounded wait gave up (never cleared by kernels)
+  // cooperative kernel (all zero on entry and exit): per-CTA slice popcounts,
+  // the number of CTAs that have published theirs, per-CTA "units listed"
+  // flags (one per kFlagStride words, so pollers of different flags never
+  // share a cache line), and the list of (request, row) unit codes in rank
+  // order, room for list_cap units
+  unsigned int* slice_counts;
+  unsigned int* published;
+  unsigned int* slice_ready;
+  uint32_t* unit_list;
+  int64_t list_cap;
 };
 
 // Parameters of the tensor-core block / dense projection.
@@ -66,25 +76,48 @@ struct BlockGemmParams {
 
 // Workspace layout (fixed offsets first, so calls with different batch sizes
 // can share one buffer): [0] arrival ticket, [4] error word, [16] per-request
-// top-1 keys, then the tile lists of the block / dense path.
+// top-1 keys, then the tile lists of the block / dense path, the per-CTA slice
+// counts and flags and the unit list of the cooperative row-sparse kernel.
+// Every kernel leaves all of it zero except the error word (calls of other
+// sizes carve the same bytes differently, so nothing may be left behind). A
+// launch that set the error word may have left state behind: the caller
+// re-zeroes such a workspace before reusing it.
 struct Workspace {
   unsigned long long* keys;
   unsigned int* ticket;
   int* error;
   int32_t* tile_list;
   int32_t* tile_counts;
+  unsigned int* slice_counts;
+  unsigned int* published;
+  unsigned int* slice_ready;
+  uint32_t* unit_list;
+  int64_t list_cap;
 };
 
 // Active-tile builder granularity: tiles per builder block (one count each).
 constexpr int kBuilderTiles = 32;
+// Upper bound on the grid of the cooperative row-sparse kernel (one slice
+// count per CTA).
+constexpr int kMaxSlices = 512;
+// Words between consecutive slice flags (one 128-byte line each).
+constexpr int kFlagStride = 32;
+// Units the cooperative kernel's list holds at most (4 bytes each).
+constexpr size_t kUnitListMax = size_t(1) << 20;
+
+constexpr size_t unit_list_cap(size_t batch, size_t vocab) {
+  return batch * vocab < kUnitListMax ? batch * vocab : kUnitListMax;
+}
 
 constexpr size_t align256c(size_t x) { return (x + 255) / 256 * 256; }
 
 // Workspace bytes for (batch, vocab): ticket + error word + one 64-bit key per
-// request, the compacted active-tile list and the per-builder-block counts.
+// request, the compacted active-tile list, the per-builder-block counts, the
+// slice counts and flags, and the unit list.
 constexpr size_t workspace_bytes_for(size_t batch, size_t vocab) {
   return align256c(16 + 8 * batch) + align256c(4 * ((vocab + 127) / 128)) +
-         align256c(4 * (((vocab + 127) / 128 + kBuilderTiles - 1) / kBuilderTiles));
+         align256c(4 * (((vocab + 127) / 128 + kBuilderTiles - 1) / kBuilderTiles)) + align256c(4 * kMaxSlices + 256) +
+         align256c(4 * kMaxSlices * kFlagStride) + align256c(4 * unit_list_cap(batch, vocab));
 }
 
 size_t workspace_bytes(int batch, int vocab);

@@ -33,7 +33,12 @@
 // large for shared memory): the same decomposition, reading the mask and the
 // hidden states from global memory.
 //
-// No CTA ever waits on another; there is no spin-wait in either kernel.
+// row_sparse_coop_kernel (masks of more than 8,192 words, workspace given):
+// launched cooperatively; each CTA scans only its own slice of the mask,
+// publishes its popcount and waits (bounded; on time-out it sets the
+// workspace error word and skips its units) for the other CTAs' counts.
+//
+// In the staged and direct kernels no CTA ever waits on another.
 #include "gsp_async.cuh"
 #include "gsp_common.cuh"
 #include "gsp_internal.h"
@@ -46,6 +51,9 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kListCap = 2048;      // units extracted per round
 constexpr int kUnroll = 8;          // 16-byte loads per lane per pass over a row
 constexpr size_t kStagedSmemMax = 200 * 1024;  // list + keys + mask slice + hidden states
+// Masks of more flat (request, word) entries than this take the cooperative
+// kernel when a workspace is given.
+constexpr int64_t kCoopMinWords = 8192;
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -120,12 +128,17 @@ __device__ __forceinline__ void finalize_top1(const RowSparseParams& p, unsigned
 // -inf over the illegal entries of flat words [w_lo, w_hi). word_of(f, b, w)
 // returns the word with bits at or beyond `vocab` already cleared or not; rows
 // beyond `vocab` are never written either way.
+// Threads [t0, t0 + nt) of the CTA take part (default: all of them).
 template <typename T, typename WordFn>
-__device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w_lo, int64_t w_hi, WordFn word_of) {
+__device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w_lo, int64_t w_hi, WordFn word_of,
+                                             int t0 = 0, int nt = 0) {
   const int V = p.vocab, nw = p.nw;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 15) == 0) && (p.logits_stride % 8 == 0);
   const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
-  for (int64_t g = w_lo * 4 + threadIdx.x; g < w_hi * 4; g += blockDim.x) {
+  if (nt == 0) nt = blockDim.x;
+  const int me = (int)threadIdx.x - t0;
+  if (me < 0 || me >= nt) return;
+  for (int64_t g = w_lo * 4 + me; g < w_hi * 4; g += nt) {
     const int64_t f = g >> 2;
     const int q = (int)(g & 3);
     const int b = (int)(f / nw), w = (int)(f - (int64_t)b * nw);
@@ -145,9 +158,10 @@ __device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w
 }
 
 // Streams units s_list[0, n) (two rows per warp in flight) and emits them.
+// With kHSmem, s_h holds the hidden rows of requests b0, b0 + 1, ... .
 template <typename T, bool kHSmem>
 __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint32_t* s_list, int n, uint64_t rbase,
-                                            uint32_t code_stride, const uint16_t* s_h, bool want_top,
+                                            uint32_t code_stride, const uint16_t* s_h, int b0, bool want_top,
                                             unsigned long long* s_keys) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int H = p.hidden_dim, nvec = H / 8;
@@ -160,10 +174,10 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
     const int bb = (int)(cb / code_stride), vb = (int)(cb - (uint32_t)bb * code_stride);
     const uint16_t* wa = static_cast<const uint16_t*>(p.weight) + (int64_t)va * p.weight_stride;
     const uint16_t* wb = static_cast<const uint16_t*>(p.weight) + (int64_t)vb * p.weight_stride;
-    const uint4* ha = kHSmem ? reinterpret_cast<const uint4*>(s_h + (size_t)ba * H)
+    const uint4* ha = kHSmem ? reinterpret_cast<const uint4*>(s_h + (size_t)(ba - b0) * H)
                              : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) +
                                                               (int64_t)ba * p.hidden_stride);
-    const uint4* hb = kHSmem ? reinterpret_cast<const uint4*>(s_h + (size_t)bb * H)
+    const uint4* hb = kHSmem ? reinterpret_cast<const uint4*>(s_h + (size_t)(bb - b0) * H)
                              : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) +
                                                               (int64_t)bb * p.hidden_stride);
     float acc_a = 0.f, acc_b = 0.f;
@@ -447,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
     }
     __syncthreads();
     // ---- 5. stream the rows ------------------------------------------------
-    stream_rows<T, true>(p, s_list, n, rbase, code_stride, s_h, want_top, s_keys);
+    stream_rows<T, true>(p, s_list, n, rbase, code_stride, s_h, 0, want_top, s_keys);
     __syncthreads();
   }
 
@@ -577,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_direct_kernel(const Ro
     }
     __syncthreads();
     if (kVec)
-      stream_rows<T, false>(p, s_list, n, rbase, code_stride, nullptr, want_top, s_keys);
+      stream_rows<T, false>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
     else
       stream_rows_scalar<T>(p, s_list, n, rbase, code_stride, want_top, s_keys);
     __syncthreads();
@@ -593,6 +607,400 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_direct_kernel(const Ro
 }
 
 // ===========================================================================
+// cooperative kernel (masks too large for one CTA to scan: B * ceil(V/32) >
+// 8,192 words)
+// ===========================================================================
+// The flat mask is cut into G equal word slices, one per CTA. Each CTA counts
+// the legal units of its own slice and publishes the count; after a bounded
+// wait for all G counts every CTA knows each slice's rank base and takes the
+// units of rank [c*U/G, (c+1)*U/G), which it gets from the owners of the
+// slices through a unit list in the workspace (list mode) or by re-scanning
+// those slices. The mask is read from DRAM once in total, not G times.
+constexpr int kCoopWpt = 8;                  // words per thread per chunk scan
+constexpr int kChunk = kThreads * kCoopWpt;  // mask words per chunk scan
+constexpr uint32_t kSliceSpinLimit = 1u << 20;
+static_assert(kMaxSlices <= kThreads, "one slice count per thread");
+
+constexpr int kHStageBytes = 64 * 1024;  // hidden rows of the requests one list round touches
+
+struct CoopLayout {
+  size_t list, keys, warp, misc, cnt, base, words, pre, hidden, total;
+};
+
+__host__ __device__ inline CoopLayout coop_layout(int batch) {
+  CoopLayout l;
+  size_t off = 0;
+  l.list = off;
+  off += 4 * (size_t)kListCap;
+  l.keys = align_up(off, 16);
+  off = l.keys + 8 * (size_t)batch;
+  l.warp = align_up(off, 16);
+  off = l.warp + 4 * 32;
+  l.misc = align_up(off, 16);
+  off = l.misc + 16;
+  l.cnt = align_up(off, 16);
+  off = l.cnt + 4 * (size_t)kMaxSlices;
+  l.base = align_up(off, 16);
+  off = l.base + 4 * (size_t)kMaxSlices;
+  l.words = align_up(off, 16);
+  off = l.words + 4 * (size_t)kChunk;
+  l.pre = align_up(off, 16);
+  off = l.pre + 4 * (size_t)kChunk;
+  l.hidden = align_up(off, 16);
+  off = l.hidden + kHStageBytes;
+  l.total = align_up(off, 128);
+  return l;
+}
+
+// Loads flat mask words [c0, c0 + n) (n <= kChunk; bits beyond the vocabulary
+// cleared) into s_words with coalesced loads and their exclusive popcount
+// prefixes (relative to c0) into s_pre; returns the chunk's popcount. Holds a
+// __syncthreads before its first shared-memory write and after its last, so
+// callers may reuse the buffers around it.
+__device__ __forceinline__ uint32_t scan_chunk(const RowSparseParams& p, int c0, int n, uint32_t* s_words,
+                                               uint32_t* s_pre, uint32_t* s_warp) {
+  const int tid = threadIdx.x, nw = p.nw, V = p.vocab;
+  const uint32_t tail_keep = (V & 31) ? ((1u << (V & 31)) - 1u) : 0xffffffffu;
+  uint32_t ld[kCoopWpt];
+#pragma unroll
+  for (int j = 0; j < kCoopWpt; ++j) {  // all loads in flight at once
+    const int i = tid + j * kThreads;
+    ld[j] = 0u;
+    if (i < n) {
+      const int f = c0 + i;
+      const int b = f / nw, w = f - b * nw;
+      ld[j] = __ldg(p.mask + (int64_t)b * p.mask_stride + w);
+      if (w == nw - 1) ld[j] &= tail_keep;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kCoopWpt; ++j)
+    if (tid + j * kThreads < n) s_words[tid + j * kThreads] = ld[j];
+  __syncthreads();
+  const int i0 = tid * kCoopWpt;
+  const uint4 x0 = reinterpret_cast<const uint4*>(s_words + i0)[0];
+  const uint4 x1 = reinterpret_cast<const uint4*>(s_words + i0)[1];
+  const uint32_t xs[kCoopWpt] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  uint32_t pc[kCoopWpt], cnt = 0;
+#pragma unroll
+  for (int j = 0; j < kCoopWpt; ++j) {
+    pc[j] = (i0 + j < n) ? (uint32_t)__popc(xs[j]) : 0u;
+    cnt += pc[j];
+  }
+  uint32_t tot;
+  uint32_t run = block_exclusive_scan(cnt, s_warp, &tot);
+  uint32_t pre[kCoopWpt];
+#pragma unroll
+  for (int j = 0; j < kCoopWpt; ++j) {
+    pre[j] = run;
+    run += pc[j];
+  }
+  reinterpret_cast<uint4*>(s_pre + i0)[0] = make_uint4(pre[0], pre[1], pre[2], pre[3]);
+  reinterpret_cast<uint4*>(s_pre + i0)[1] = make_uint4(pre[4], pre[5], pre[6], pre[7]);
+  __syncthreads();
+  return tot;
+}
+
+// Stages the hidden rows of the requests s_list[0, n) touches in s_h (when
+// they fit; reused across rounds) and streams the units. Every unit code is
+// checked first (request < B, row < V): a round holding any other code (which
+// only a workspace left dirty by an earlier failed launch can produce) sets
+// the error word and is skipped, so no address is ever formed from it.
+template <typename T>
+__device__ __forceinline__ void coop_stream_round(const RowSparseParams& p, const uint32_t* s_list, int n,
+                                                  uint32_t rbase, uint32_t code_stride, uint16_t* s_h, int& h_lo,
+                                                  int& h_hi, bool want_top, unsigned long long* s_keys) {
+  const int tid = threadIdx.x, H = p.hidden_dim;
+  bool bad = false;
+  for (int i = tid; i < n; i += kThreads) {
+    const uint32_t code = s_list[i];
+    const uint32_t b = code / code_stride;
+    bad |= (b >= (uint32_t)p.batch) || (code - b * code_stride >= (uint32_t)p.vocab);
+  }
+  if (__syncthreads_or(bad)) {
+    if (tid == 0 && p.error) atomicExch(p.error, 2);
+    return;
+  }
+  const int rb0 = (int)(s_list[0] / code_stride), rb1 = (int)(s_list[n - 1] / code_stride);
+  if ((size_t)(rb1 - rb0 + 1) * H * 2 <= (size_t)kHStageBytes) {
+    if (rb0 < h_lo || rb1 >= h_hi) {
+      const int nvec = H / 8;
+      for (int i = tid; i < (rb1 - rb0 + 1) * nvec; i += kThreads) {
+        const int b = rb0 + i / nvec, j = i - (i / nvec) * nvec;
+        reinterpret_cast<uint4*>(s_h)[i] = __ldg(
+            reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
+      }
+      h_lo = rb0;
+      h_hi = rb1 + 1;
+      __syncthreads();
+    }
+    stream_rows<T, true>(p, s_list, n, rbase, code_stride, s_h, h_lo, want_top, s_keys);
+  } else {
+    stream_rows<T, false>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
+  }
+}
+
+// Bounded wait (one polling thread per flag) until *flag != 0; returns the
+// value seen, 0 on time-out.
+__device__ __forceinline__ uint32_t wait_flag(const uint32_t* flag) {
+  uint32_t v = 0;
+  for (uint32_t i = 0; i < kSliceSpinLimit; ++i) {
+    v = ld_acquire_gpu(flag);
+    if (v != 0u) break;
+    __nanosleep(32);
+  }
+  return v;
+}
+
+// End of the cooperative kernel: top-1 keys folded into the workspace, one
+// ticket per CTA; the last CTA decodes the keys and re-zeroes slice counts,
+// flags and ticket (every CTA has passed both of its waits by then).
+__device__ __forceinline__ void coop_finish(const RowSparseParams& p, unsigned long long* s_keys, int* s_flag,
+                                            bool want_top) {
+  const int tid = threadIdx.x, G = gridDim.x;
+  __syncthreads();
+  bool did = false;
+  if (want_top) {
+    for (int b = tid; b < p.batch; b += blockDim.x) {
+      const unsigned long long k = s_keys[b];
+      if (k != 0ull) {
+        atomicMax(p.keys + b, k);
+        did = true;
+      }
+    }
+  }
+  if (did) __threadfence();
+  __syncthreads();
+  if (tid == 0) *s_flag = (atomicAdd(p.ticket, 1u) == (unsigned)G - 1u);
+  __syncthreads();
+  if (*s_flag) {
+    __threadfence();
+    if (want_top) {
+      for (int b = tid; b < p.batch; b += blockDim.x) {
+        const unsigned long long k = atomicExch(p.keys + b, 0ull);
+        if (p.top_value) p.top_value[b] = key_value(k);
+        if (p.top_index) p.top_index[b] = key_index(k);
+        if (p.top_key) p.top_key[b] = key_to_signed(k);
+      }
+    }
+    for (int c = tid; c < G; c += blockDim.x) {
+      p.slice_counts[c] = 0u;
+      p.slice_ready[(size_t)c * kFlagStride] = 0u;
+    }
+    if (tid == 0) {
+      *p.published = 0u;
+      atomicExch(p.ticket, 0u);
+    }
+  }
+}
+
+// Launched cooperatively (every CTA co-resident), grid <= kMaxSlices, with a
+// zeroed workspace; 16-byte aligned weight and hidden rows, H % 8 == 0.
+//
+// List mode (every slice fits one chunk scan and the batch has at most
+// list_cap units): after the counts, each CTA writes the unit codes of its own
+// slice, still in shared memory, into the workspace list at the slice's rank
+// base and raises its slice flag; each CTA then waits only for the flags of
+// the slices its rank range draws from and reads its units from the list.
+// No mask word is read twice and nothing waits on memory once rows stream.
+// Otherwise each CTA re-scans (from L2) the slices its rank range overlaps.
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowSparseParams p) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const CoopLayout L = coop_layout(p.batch);
+  uint32_t* s_list = reinterpret_cast<uint32_t*>(smem + L.list);
+  unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
+  uint32_t* s_warp = reinterpret_cast<uint32_t*>(smem + L.warp);
+  int* s_misc = reinterpret_cast<int*>(smem + L.misc);
+  uint32_t* s_cnt = reinterpret_cast<uint32_t*>(smem + L.cnt);
+  uint32_t* s_base = reinterpret_cast<uint32_t*>(smem + L.base);
+  uint32_t* s_words = reinterpret_cast<uint32_t*>(smem + L.words);
+  uint32_t* s_pre = reinterpret_cast<uint32_t*>(smem + L.pre);
+  uint16_t* s_h = reinterpret_cast<uint16_t*>(smem + L.hidden);
+
+  const int tid = threadIdx.x, G = gridDim.x, cta = blockIdx.x;
+  const int B = p.batch, nw = p.nw, F = B * nw;
+  const bool want_top = (p.top_value != nullptr) | (p.top_index != nullptr) | (p.top_key != nullptr);
+  auto slice_lo = [&](int s) { return (int)((int64_t)F * s / G); };
+  const int my_lo = slice_lo(cta), my_hi = slice_lo(cta + 1);
+  const int max_slice = (F + G - 1) / G;  // every slice holds at most this many words
+  for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
+  if (tid == 0) s_misc[0] = 0;
+
+  // ---- 1. popcount of this CTA's slice, published to the grid --------------
+  // (slice, chunk) currently held in s_words / s_pre, and its popcount
+  int held_slice = -1, held_chunk = -1;
+  uint32_t held_total = 0;
+  uint32_t mine = 0;
+  for (int c0 = my_lo, ch = 0; c0 < my_hi; c0 += kChunk, ++ch) {
+    held_total = scan_chunk(p, c0, min(kChunk, my_hi - c0), s_words, s_pre, s_warp);
+    held_slice = cta;
+    held_chunk = ch;
+    mine += held_total;
+  }
+  if (tid == 0) {
+    p.slice_counts[cta] = mine;
+    __threadfence();
+    atom_add_release_gpu(p.published, 1u);
+  }
+  // While the other counts arrive, warps 1.. (warp 0 holds the poller) write
+  // -inf over the own slice's illegal entries (illegal and legal entries are
+  // disjoint, so the order does not matter). Prefetching the slice's legal
+  // rows into L2 here was measured: it did not shorten the kernel.
+  const int pollers = 32;
+  const bool filled_early = p.logits != nullptr && max_slice <= kChunk;
+  if (filled_early && my_hi > my_lo)
+    fill_illegal<T>(p, my_lo, my_hi, [&](int64_t f, int, int) { return s_words[f - my_lo]; }, pollers,
+                    kThreads - pollers);
+
+  // ---- 2. bounded wait for every slice count; rank base of each slice ------
+  // (one poller per CTA on the published counter, then one load per count)
+  if (tid == 0) {
+    uint32_t v = 0;
+    for (uint32_t i = 0; i < kSliceSpinLimit; ++i) {
+      v = ld_acquire_gpu(p.published);
+      if (v >= (uint32_t)G) break;
+      __nanosleep(64);
+    }
+    if (v < (uint32_t)G) {
+      if (p.error) atomicExch(p.error, 1);
+      s_misc[0] = 1;
+    }
+  }
+  __syncthreads();
+  const uint32_t c = (tid < G && s_misc[0] == 0) ? __ldcg(p.slice_counts + tid) : 0u;
+  uint32_t total;
+  const uint32_t base = block_exclusive_scan(tid < G ? c : 0u, s_warp, &total);
+  if (tid < G) {
+    s_cnt[tid] = c;
+    s_base[tid] = base;
+  }
+  __syncthreads();
+  bool aborted = s_misc[0] != 0;
+
+  const uint32_t lo = aborted ? 0u : (uint32_t)((uint64_t)total * cta / G);
+  const uint32_t hi = aborted ? 0u : (uint32_t)((uint64_t)total * (cta + 1) / G);
+  const uint32_t code_stride = (uint32_t)nw * 32u;
+  const bool list_mode = max_slice <= kChunk && (int64_t)total <= p.list_cap;
+  int h_lo = 0, h_hi = 0;  // requests whose hidden rows are in s_h
+
+  if (list_mode) {
+    // ---- 3. own units -> list at the slice's rank base; flag ---------------
+    if (!aborted) {
+      const uint32_t sb = s_base[cta];
+      for (int i = tid; i < my_hi - my_lo; i += kThreads) {
+        uint32_t word = s_words[i];
+        uint32_t r = sb + s_pre[i];
+        const int f = my_lo + i;
+        const int b = f / nw, w = f - b * nw;
+        if (p.offsets != nullptr && w == 0) p.offsets[b] = (int64_t)r;
+        while (word) {
+          const int bit = __ffs(word) - 1;
+          word &= word - 1;
+          p.unit_list[r++] = (uint32_t)b * code_stride + (uint32_t)(w * 32 + bit);
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        st_release_gpu(p.slice_ready + (size_t)cta * kFlagStride, 1u);
+      }
+      if (p.logits != nullptr && !filled_early && my_hi > my_lo)
+        fill_illegal<T>(p, my_lo, my_hi, [&](int64_t f, int, int) { return s_words[f - my_lo]; });
+    }
+    // ---- 4. wait for the slices this CTA's ranks come from; stream ---------
+    if (lo < hi) {
+      if (tid < G) {
+        const uint32_t sb = s_base[tid], sc = s_cnt[tid];
+        if (sc != 0u && sb < hi && sb + sc > lo && wait_flag(p.slice_ready + (size_t)tid * kFlagStride) == 0u) {
+          if (p.error) atomicExch(p.error, 1);
+          s_misc[0] = 1;
+        }
+      }
+      __syncthreads();
+      aborted = s_misc[0] != 0;
+    }
+    for (uint32_t rbase = lo; rbase < hi && !aborted; rbase += kListCap) {
+      const int n = (int)(min(hi, rbase + (uint32_t)kListCap) - rbase);
+      // read the units and re-zero them: each entry is written by one owner
+      // and read by one CTA, so the list is all zero again on exit
+      for (int i = tid; i < n; i += kThreads) {
+        s_list[i] = __ldcg(p.unit_list + rbase + i);
+        p.unit_list[rbase + i] = 0u;
+      }
+      __syncthreads();
+      coop_stream_round<T>(p, s_list, n, rbase, code_stride, s_h, h_lo, h_hi, want_top, s_keys);
+      __syncthreads();
+    }
+  } else {
+    // ---- 3'. re-scan the slices each round of ranks overlaps ---------------
+    for (uint32_t rbase = lo; rbase < hi; rbase += kListCap) {
+      const uint32_t rend = min(hi, rbase + (uint32_t)kListCap);
+      for (int s = 0; s < G; ++s) {
+        const uint32_t sb = s_base[s], sc = s_cnt[s];
+        if (sb >= rend) break;
+        if (sc == 0u || sb + sc <= rbase) continue;
+        const int s_lo = slice_lo(s), s_hi = slice_lo(s + 1);
+        uint32_t run = sb;
+        for (int c0 = s_lo, ch = 0; c0 < s_hi && run < rend; c0 += kChunk, ++ch) {
+          const int n = min(kChunk, s_hi - c0);
+          if (held_slice != s || held_chunk != ch) {
+            held_total = scan_chunk(p, c0, n, s_words, s_pre, s_warp);
+            held_slice = s;
+            held_chunk = ch;
+          }
+          if (run + held_total > rbase) {
+            for (int i = tid; i < n; i += kThreads) {
+              uint32_t word = s_words[i];
+              uint32_t r = run + s_pre[i];
+              if (word == 0u || r >= rend || r + (uint32_t)__popc(word) <= rbase) continue;
+              const int f = c0 + i;
+              const int b = f / nw, w = f - b * nw;
+              while (word) {
+                const int bit = __ffs(word) - 1;
+                word &= word - 1;
+                if (r >= rbase && r < rend) s_list[r - rbase] = (uint32_t)b * code_stride + (uint32_t)(w * 32 + bit);
+                ++r;
+              }
+            }
+          }
+          run += held_total;
+        }
+      }
+      __syncthreads();
+      coop_stream_round<T>(p, s_list, (int)(rend - rbase), rbase, code_stride, s_h, h_lo, h_hi, want_top, s_keys);
+      __syncthreads();
+    }
+    // ---- 4'. own slice: request offsets (compact output), -inf fill ---------
+    if ((p.logits != nullptr && !filled_early) || p.offsets != nullptr) {
+      uint32_t run = s_base[cta];
+      for (int c0 = my_lo, ch = 0; c0 < my_hi; c0 += kChunk, ++ch) {
+        const int n = min(kChunk, my_hi - c0);
+        if (held_slice != cta || held_chunk != ch) {
+          held_total = scan_chunk(p, c0, n, s_words, s_pre, s_warp);
+          held_slice = cta;
+          held_chunk = ch;
+        }
+        if (p.offsets != nullptr) {
+          for (int i = tid; i < n; i += kThreads) {
+            const int f = c0 + i;
+            if (f % nw == 0) p.offsets[f / nw] = (int64_t)(run + s_pre[i]);
+          }
+        }
+        if (p.logits != nullptr && !filled_early)
+          fill_illegal<T>(p, c0, c0 + n, [&](int64_t f, int, int) { return s_words[f - c0]; });
+        run += held_total;
+      }
+    }
+  }
+  if (p.offsets != nullptr && cta == 0 && tid == 0) p.offsets[B] = (int64_t)total;
+
+  // ---- 5. top-1, workspace reset ------------------------------------------
+  coop_finish(p, s_keys, s_misc + 2, want_top);
+}
+
+// ===========================================================================
 // launch
 // ===========================================================================
 template <typename T>
@@ -604,6 +1012,26 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
   const bool vec = (p.hidden_dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.weight) & 15) == 0) &&
                    (p.weight_stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.hidden) & 15) == 0) &&
                    (p.batch == 1 || p.hidden_stride % 8 == 0);
+  const int64_t F64 = p.mask ? (int64_t)p.batch * p.nw : 0;
+  if (vec && F64 > kCoopMinWords && p.slice_counts != nullptr && p.published != nullptr && p.slice_ready != nullptr &&
+      F64 * 32 < (int64_t)1 << 32) {
+    const CoopLayout L = coop_layout(p.batch);
+    if (L.total <= kStagedSmemMax) {
+      auto k = row_sparse_coop_kernel<T>;
+      if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)min(grid, kMaxSlices));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = L.total;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      return cudaLaunchKernelEx(&cfg, k, p);
+    }
+  }
   if (vec) {
     const int F = p.mask ? p.batch * p.nw : 0;
     const int wpt = F <= kThreads * 16 ? 16 : 32;

@@ -126,6 +126,15 @@ def workspace(device: torch.device, batch: int, vocab: int) -> torch.Tensor:
         return ws
 
 
+def reset_workspace(device: torch.device) -> None:
+    """Re-zeroes the current stream's workspace (needed after a call whose
+    kernel reported an error through workspace_error)."""
+    dev_index = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get((dev_index, torch.cuda.current_stream(device).cuda_stream))
+    if ws is not None:
+        ws.zero_()
+
+
 def workspace_error(device: torch.device) -> int:
     """Error word of the current stream's workspace: non-zero after a kernel
     gave up a bounded wait (reads the device, so it synchronises)."""

@@ -562,6 +562,7 @@ def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
             times["cublas+xgrammar"] = None
         mean_active = float(np.mean(active))
         block_bytes = mean_active * 128 * HIDDEN * 2
+        row_bytes = float(np.mean([l.sum() for l in legal])) * HIDDEN * 2  # legal rows, every request
         best = min(("block-sparse", "dense-mask", "row-sparse"), key=lambda r: times[r])
         choice = tr.choose_route(batch, VOCAB, HIDDEN, 2, legal[0].tolist(), active[0])
         out.append({
@@ -570,6 +571,9 @@ def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
             "block_roofline": {"achieved_gbs": block_bytes / (times["block-sparse"] * 1e-6) / 1e9,
                                "frac": block_bytes / (times["block-sparse"] * 1e-6) / 1e9 / peak,
                                "algorithmic_bytes": block_bytes},
+            "row_sparse_roofline": {"achieved_gbs": row_bytes / (times["row-sparse"] * 1e-6) / 1e9,
+                                    "frac": row_bytes / (times["row-sparse"] * 1e-6) / 1e9 / peak,
+                                    "algorithmic_bytes": row_bytes},
             "dense_roofline_frac": VOCAB * HIDDEN * 2 / (times["dense-mask"] * 1e-6) / 1e9 / peak,
             "speedup_block_vs_cublas_xgrammar": (times["cublas+xgrammar"] / times["block-sparse"]
                                                  if times["cublas+xgrammar"] else None),

@@ -5,7 +5,8 @@
 // serving engine that owns every byte of device memory through its own pool,
 // an FFI binding that is handed only the input and output buffers, or a
 // runtime that forbids allocation on its decode path. gsp_row_sparse_logits
-// needs a small caller-provided workspace for its cross-CTA top-1 merge; this
+// needs a caller-provided workspace for its cross-CTA top-1 merge and, for
+// large batches, its cross-CTA unit exchange; this
 // variant instead uses the file-scope device array below, which the library
 // carries for every GPU that loads it until the process exits.
 //
@@ -28,7 +29,9 @@ namespace {
 
 // Scratch for batch <= GSP_STATIC_MAX_BATCH and vocab <= GSP_STATIC_MAX_VOCAB:
 // the same layout as the caller-provided workspace (ticket, error word, one
-// 64-bit top-1 key per request, then tile lists), sized for those maxima.
+// 64-bit top-1 key per request, tile lists, and the multi-request kernel's
+// slice counts, flags and 1M-entry unit list), sized for those maxima
+// (4,304,384 bytes).
 constexpr size_t kStaticScratchBytes = workspace_bytes_for(GSP_STATIC_MAX_BATCH, GSP_STATIC_MAX_VOCAB);
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];

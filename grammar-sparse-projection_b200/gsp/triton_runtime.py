@@ -239,11 +239,18 @@ def _reference_route(batch: int, full_word_fraction, dense_full_word_threshold: 
 
 
 # B200 cost model of the three routes, in microseconds (see choose_route).
+# Fitted to CUDA-graph timings on B200 at V=248,320, H=2,048 fp16, batch 1-32
+# with 0.5%-legal clustered masks (row-sparse 12 / 18 / 37 us at batch 2 / 8 /
+# 32; block-sparse 24 us up to batch 8, 55 us at batch 32 with 17% of the
+# tiles active; dense 170 us).
 B200_COST = {
-    "hbm_gbs": 6000.0,          # sustained streaming rate of the projection kernels
-    "row_sparse_fixed_us": 4.0,  # launch + mask scan + merge
-    "block_fixed_us": 8.0,       # tile builder + tcgen05 set-up
-    "dense_fixed_us": 6.0,
+    "hbm_gbs": 6000.0,             # legal rows and logits streamed by the row-sparse kernels
+    "row_sparse_fixed_us": 9.0,    # launch, mask scan / slice-count exchange, top-1 merge
+    "block_floor_us": 24.0,        # tile builder + tcgen05 pipeline: the least a block call costs
+    "block_fixed_us": 10.0,
+    "block_gbs": 3800.0,           # effective rate over the active tiles
+    "dense_fixed_us": 5.0,
+    "dense_gbs": 6000.0,
 }
 
 
@@ -251,19 +258,21 @@ def choose_route(batch: int, vocab: int, hidden_dim: int, elem_bytes: int,
                  legal_counts, active_tiles: int, cost: dict | None = None) -> str:
     """B200-calibrated route choice from exact device-side statistics.
 
-    Each route is costed as a fixed latency plus the weight bytes it must
-    stream at HBM rate: row-sparse reads every request's legal rows
-    (sum_b k_b rows), block-sparse reads the union of active 128-row tiles,
-    dense reads all of W. Batch 1 always takes row-sparse, as in the reference.
+    Row-sparse reads every request's legal rows (sum_b k_b rows) and writes the
+    B x V logits; block-sparse reads the union of active 128-row tiles once for
+    all requests, with a floor for its builder and tensor-core pipeline; dense
+    reads all of W. Each is a fixed latency plus its bytes at the rate measured
+    for that kernel. Batch 1 always takes row-sparse, as in the reference.
     """
     c = dict(B200_COST, **(cost or {}))
     if batch == 1:
         return "row-sparse"
     row_bytes = hidden_dim * elem_bytes
-    per_us = c["hbm_gbs"] * 1e3  # bytes per microsecond
-    t_row = c["row_sparse_fixed_us"] + sum(int(k) for k in legal_counts) * row_bytes / per_us
-    t_block = c["block_fixed_us"] + min(active_tiles * TILE_ROWS, vocab) * row_bytes / per_us
-    t_dense = c["dense_fixed_us"] + vocab * row_bytes / per_us
+    out_bytes = batch * vocab * elem_bytes
+    t_row = c["row_sparse_fixed_us"] + (sum(int(k) for k in legal_counts) * row_bytes + out_bytes) / (c["hbm_gbs"] * 1e3)
+    t_block = max(c["block_floor_us"],
+                  c["block_fixed_us"] + min(active_tiles * TILE_ROWS, vocab) * row_bytes / (c["block_gbs"] * 1e3))
+    t_dense = c["dense_fixed_us"] + vocab * row_bytes / (c["dense_gbs"] * 1e3)
     best = min((t_row, "row-sparse"), (t_block, "block-sparse"), (t_dense, "dense-mask"))
     return best[1]
 

@@ -153,8 +153,9 @@ int32_t gsp_dense_masked_logits(const void* hidden, int64_t hidden_row_stride,
  * allocate device memory at all (a plugin inside a serving engine that owns
  * every byte of device memory through its own pool, or an FFI binding that is
  * handed only the input and output buffers). It takes the same arguments minus
- * the workspace: the top-1 scratch lives in a fixed array inside the library,
- * kept on every GPU that loads it until exit, so batch must be
+ * the workspace: the scratch (top-1 keys, and the slice counts, flags and
+ * unit list of the multi-request kernel; 4.3 MB) lives in a fixed array inside
+ * the library, kept on every GPU that loads it until exit, so batch must be
  * <= GSP_STATIC_MAX_BATCH and vocab <= GSP_STATIC_MAX_VOCAB (larger sizes fail
  * with GSP_ERR_INVALID_ARGUMENT and a message in gsp_last_error()).
  * The first call on each device looks up the array's device address

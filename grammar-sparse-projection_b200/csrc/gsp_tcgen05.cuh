@@ -92,7 +92,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---- TMA ------------------------------------------------------------------
-// Two-dimensional tiled load (no multicast) completing on `bar`. c0 is the
+// Two-dimensional tiled load into this CTA's shared memory, completing on `bar`. c0 is the
 // inner coordinate in elements; c0 * element size must be a multiple of 16.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(

@@ -237,9 +237,10 @@ def workload_config(args):
     return {"workload": "batch-1 row-sparse direct-bitmask LM-head GEMV", "vocab": VOCAB, "hidden": HIDDEN,
             "batch": 1, "density": args.density, "mask": f"{args.pattern}, fresh seeded mask per step",
             "weight": "fp16 N(0,0.02) row-major [V,H]", "outputs": "full logits [V] + fused top-1",
-            "l2": ("inputs larger than L2: step i reads weight copy i % copies (1 GB each) and mask i % masks"
-                   if args.gpus == 1 else "flushed before every step (256 MiB write), flush outside the step events"),
-            "parallelism": f"vocab-parallel x{args.gpus}" if args.gpus > 1 else "single GPU"}
+            "l2": ("inputs larger than L2: step i reads weight copy i % copies (each rank's shard of the "
+                   "1 GB head) and mask i % masks"),
+            "parallelism": (f"vocab-parallel x{args.gpus}: row shards of W, top-1 merged across ranks inside the "
+                            "kernel over NVLink peer memory" if args.gpus > 1 else "single GPU")}
 
 
 # ---------------------------------------------------------------------------
@@ -272,15 +273,16 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    group = None
+    xch = None
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        xch = vp.PeerExchange(max_batch=1)
     lo, hi = vp.shard_bounds(VOCAB, world, rank)
 
     # weight shard(s), hidden state and seeded masks (identical on every rank)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    copies = args.copies if world == 1 else 1
+    copies = args.copies
     weights = [(torch.randn(hi - lo, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(copies)]
     weight = weights[0]
     hidden = torch.randn(1, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(99)).half()
@@ -302,9 +304,8 @@ def main():
         if world == 1:
             _native.row_sparse(hidden, w, m, logits=logits, top_value=top_value, top_index=top_index)
         else:
-            _native.row_sparse(hidden, w, m, logits=logits, top_key=top_key, vocab_offset=lo)
-            vp.merge_top1_keys(top_key, group)
-            _native.top1_from_keys(top_key, top_value, top_index)
+            _native.vocab_parallel("row-sparse", hidden, w, m, xch.peers, rank, xch.max_batch, logits=logits,
+                                   top_value=top_value, top_index=top_index, vocab_offset=lo)
 
     def barrier():
         if world > 1:
@@ -353,12 +354,7 @@ def main():
     sampler = ClockSampler(local_rank)
     with sampler:
         t_wall = time.perf_counter()
-        if world == 1:
-            total_us = graph_total_us(args.steps, step)
-            per_step = None
-        else:
-            per_step = timed(args.steps, step, 0)
-            total_us = sum(per_step)
+        total_us = graph_total_us(args.steps, step)
         barrier()
         t_wall = time.perf_counter() - t_wall
     total_us = max_over_ranks(total_us, world)
@@ -386,9 +382,8 @@ def main():
             _native.row_sparse(dev_hidden, weight, dev_mask, logits=logits, top_value=top_value,
                                top_index=top_index)
         else:
-            _native.row_sparse(dev_hidden, weight, dev_mask, logits=logits, top_key=top_key, vocab_offset=lo)
-            vp.merge_top1_keys(top_key, group)
-            _native.top1_from_keys(top_key, top_value, top_index)
+            _native.vocab_parallel("row-sparse", dev_hidden, weight, dev_mask, xch.peers, rank, xch.max_batch,
+                                   logits=logits, top_value=top_value, top_index=top_index, vocab_offset=lo)
         host_top[0:1].copy_(top_index, non_blocking=True)
         host_top[1:2].view(torch.float32)[:1].copy_(top_value, non_blocking=True)
 
@@ -457,7 +452,7 @@ def main():
             "config": workload_config(args),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": e2e_total / args.steps},
-            "gpu_launches": args.steps * (1 if world == 1 else 2),
+            "gpu_launches": args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu_base,
             "clocks": sampler.summary(),
@@ -470,6 +465,7 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        xch.close()
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     return 0

@@ -41,6 +41,7 @@
 #include "gsp_async.cuh"
 #include "gsp_common.cuh"
 #include "gsp_internal.h"
+#include "gsp_peer.cuh"
 #include "gsp_tcgen05.cuh"
 
 namespace gsp {
@@ -359,8 +360,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (s_misc[1]) {
     __threadfence();
     if (want_top) {
+      if (p.peers.world > 1) {  // merge across the ranks of a vocabulary-parallel group
+        for (int b = tid; b < B; b += kGemmThreads) s_keys[b] = atomicExch(p.keys + b, 0ull);
+        peer_exchange_keys(p.peers, s_keys, B, reinterpret_cast<uint32_t*>(s_misc + 2), p.error);
+      }
       for (int b = tid; b < B; b += kGemmThreads) {
-        const unsigned long long k = atomicExch(p.keys + b, 0ull);
+        const unsigned long long k = p.peers.world > 1 ? s_keys[b] : atomicExch(p.keys + b, 0ull);
         if (p.top_value) p.top_value[b] = key_value(k);
         if (p.top_index) p.top_index[b] = key_index(k);
         if (p.top_key) p.top_key[b] = key_to_signed(k);
@@ -569,6 +574,7 @@ cudaError_t launch_typed(const BlockGemmParams& p0, cudaStream_t stream) {
     r.keys = p0.keys;
     r.ticket = p0.ticket;
     r.error = p0.error;
+    r.peers = p0.peers;
     return launch_row_sparse(r, std::is_same<T, __nv_bfloat16>::value ? 1 : 0, stream);
   }
   // Batches above kMaxNpad run as consecutive chunks of requests.
@@ -583,6 +589,7 @@ cudaError_t launch_typed(const BlockGemmParams& p0, cudaStream_t stream) {
     if (p0.top_index) p.top_index = p0.top_index + b0;
     if (p0.top_key) p.top_key = p0.top_key + b0;
     p.keys = p0.keys + b0;
+    p.peers.batch_base = p0.peers.batch_base + b0;
     if ((err = launch_chunk<T>(p, dev, stream)) != cudaSuccess) return err;
   }
   return cudaSuccess;

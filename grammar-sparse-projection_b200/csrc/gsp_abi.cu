@@ -181,7 +181,7 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
                           int32_t vocab, int32_t hidden_dim, int32_t dtype, int64_t vocab_offset,
                           void* logits, int64_t logits_row_stride, float* top_value,
                           int64_t* top_index, int64_t* top_key, void* workspace,
-                          size_t workspace_bytes_, void* stream) {
+                          size_t workspace_bytes_, void* stream, const PeerExchange* peers = nullptr) {
   int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
                                    bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits,
                                    logits_row_stride);
@@ -200,6 +200,7 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
     p.top_index = top_index;
     p.top_key = top_key;
     if (workspace) attach_workspace(p, workspace);
+    if (peers) p.peers = *peers;
     return cuda_status(launch_row_sparse(p, dtype, s), fn);
   }
   BlockGemmParams p;
@@ -227,6 +228,7 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
   p.tile_list = w.tile_list;
   p.tile_counts = w.tile_counts;
   p.dense = dense || bitmask == nullptr;
+  if (peers) p.peers = *peers;
   return cuda_status(launch_block_gemm(p, dtype, s), fn);
 }
 
@@ -364,6 +366,43 @@ int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
   return cuda_status(
       launch_top1_from_keys(keys, batch, top_value, top_index, static_cast<cudaStream_t>(stream)),
       fn);
+}
+
+int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hidden_row_stride,
+                                  const void* weight, int64_t weight_row_stride, const int32_t* bitmask,
+                                  int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                                  int32_t hidden_dim, int32_t dtype, int64_t vocab_offset, void* logits,
+                                  int64_t logits_row_stride, float* top_value, int64_t* top_index,
+                                  int64_t* top_key, void* workspace, size_t workspace_bytes_,
+                                  void* const* peer_buffers, int32_t rank, int32_t world_size,
+                                  int32_t max_batch, void* stream) {
+  const char* fn = "gsp_vocab_parallel_logits";
+  if (route != GSP_ROUTE_ROW_SPARSE && route != GSP_ROUTE_BLOCK_SPARSE && route != GSP_ROUTE_DENSE_MASK)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: unknown route %d", fn, route);
+  if (world_size < 1 || world_size > kMaxPeers || rank < 0 || rank >= world_size)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: rank %d / world size %d (at most %d ranks)", fn, rank,
+                world_size, kMaxPeers);
+  if (!top_value && !top_index && !top_key)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: the exchange merges top-1; give top_value, top_index or top_key", fn);
+  PeerExchange x;
+  std::memset(&x, 0, sizeof(x));
+  x.rank = rank;
+  x.world = world_size;
+  x.max_batch = max_batch;
+  if (world_size > 1) {
+    if (!peer_buffers) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: peer_buffers is required", fn);
+    if (batch > max_batch)
+      return fail(GSP_ERR_INVALID_ARGUMENT, "%s: batch %d exceeds the exchange's max_batch %d", fn, batch, max_batch);
+    for (int q = 0; q < world_size; ++q) {
+      if (!peer_buffers[q]) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: peer_buffers[%d] is NULL", fn, q);
+      x.buf[q] = static_cast<unsigned char*>(peer_buffers[q]);
+    }
+  }
+  const bool tc = route != GSP_ROUTE_ROW_SPARSE;
+  return projection_common(fn, tc, route == GSP_ROUTE_DENSE_MASK ? 1 : 0, hidden, hidden_row_stride, weight,
+                           weight_row_stride, bitmask, bitmask_row_stride, batch, vocab, hidden_dim, dtype, vocab_offset, logits,
+                           logits_row_stride, top_value, top_index, top_key, workspace, workspace_bytes_,
+                           stream, &x);
 }
 
 }  // extern "C"

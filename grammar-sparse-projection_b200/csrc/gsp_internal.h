@@ -7,6 +7,28 @@
 
 namespace gsp {
 
+// Ranks of one vocabulary-parallel group whose projection kernels merge their
+// top-1 keys over peer memory (one process per GPU, one node).
+constexpr int kMaxPeers = 8;
+
+// Exchange buffer of one rank (gsp_peer_exchange_alloc): [0] epoch (calls
+// completed), [128 + 128 q] flag written by rank q (one line per writer),
+// [kPeerKeysOffset] keys[2][world][max_batch] (double-buffered by epoch
+// parity), written by the ranks over NVLink.
+constexpr size_t kPeerKeysOffset = 128 + 128 * kMaxPeers;
+
+constexpr size_t peer_exchange_bytes_for(size_t world, size_t max_batch) {
+  return (kPeerKeysOffset + 2 * world * max_batch * 8 + 255) / 256 * 256;
+}
+
+struct PeerExchange {
+  unsigned char* buf[kMaxPeers];  // rank q's exchange buffer as mapped in this process
+  int rank;
+  int world;       // < 2: no exchange
+  int max_batch;   // key slots per rank
+  int batch_base;  // slot of this launch's request 0 (batch chunks of the block path)
+};
+
 // Parameters of the row-sparse kernel (one launch covers every request).
 struct RowSparseParams {
   const void* hidden;
@@ -46,6 +68,7 @@ struct RowSparseParams {
   unsigned int* slice_ready;
   uint32_t* unit_list;
   int64_t list_cap;
+  PeerExchange peers;  // cross-rank top-1 merge (world < 2: none)
 };
 
 // Parameters of the tensor-core block / dense projection.
@@ -72,6 +95,7 @@ struct BlockGemmParams {
   int32_t* tile_list;     // workspace: compacted active tile ids
   int32_t* tile_counts;   // workspace: per-builder-block active tile counts
   int dense;              // 1: every tile is projected (dense_masked_logits)
+  PeerExchange peers;     // cross-rank top-1 merge (world < 2: none)
 };
 
 // Workspace layout (fixed offsets first, so calls with different batch sizes

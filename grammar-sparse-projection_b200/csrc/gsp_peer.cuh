@@ -1,0 +1,91 @@
+// Cross-rank top-1 merge over NVLink peer memory, run by the last CTA of a
+// projection kernel on every rank of a vocabulary-parallel group.
+//
+// Each rank's exchange buffer (layout in gsp_internal.h) is mapped into every
+// other rank's process. For call number e (the buffer's epoch + 1) the last
+// CTA of rank r
+//   1. stores its per-request keys into slot [e & 1][r] of EVERY rank's buffer
+//      (plain stores to peer memory), fences at system scope and raises flag r
+//      of every rank's buffer to e (release, system scope);
+//   2. waits, bounded, until each of its own flags has reached e (a flag may
+//      already hold e + 1: the writer finished this call and started the next);
+//   3. takes the MAX of the R keys per request and records e as its epoch.
+// A rank can run at most one call ahead of the slowest peer (it cannot finish
+// call e + 1 before every peer has written its e + 1 keys, which each peer does
+// only after reading its call-e keys), so two key buffers suffice. All ranks
+// must make the same sequence of calls. Nothing here uses multicast.
+#pragma once
+
+#include <stdint.h>
+
+#include "gsp_internal.h"
+
+namespace gsp {
+
+constexpr uint32_t kPeerSpinLimit = 1u << 22;  // x ~64 ns back-off: about a quarter of a second
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long* peer_key_slot(const PeerExchange& x, int q, int parity, int src) {
+  return reinterpret_cast<unsigned long long*>(x.buf[q] + kPeerKeysOffset) +
+         ((size_t)parity * x.world + src) * x.max_batch + x.batch_base;
+}
+
+// Called by every thread of ONE CTA with the rank's merged keys in
+// s_keys[0, batch); leaves the group's merged keys there. s_word is one word
+// of shared memory. A wait that runs out sets *error (when given) to 3 and
+// merges what has arrived.
+__device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsigned long long* s_keys, int batch,
+                                                   uint32_t* s_word, int* error) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  unsigned char* self = x.buf[x.rank];
+  uint32_t* epoch = reinterpret_cast<uint32_t*>(self);
+  if (tid == 0) *s_word = *reinterpret_cast<volatile uint32_t*>(epoch) + 1u;
+  __syncthreads();
+  const uint32_t e = *s_word;
+  const int par = (int)(e & 1u);
+  for (int i = tid; i < x.world * batch; i += nt) {
+    const int q = i / batch, b = i - q * batch;
+    peer_key_slot(x, q, par, x.rank)[b] = s_keys[b];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < x.world) st_release_sys(reinterpret_cast<uint32_t*>(x.buf[tid] + 128 + 128 * x.rank), e);
+  if (tid < x.world) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(self + 128 + 128 * tid);
+    bool ok = false;
+    for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
+      if ((int32_t)(ld_acquire_sys(f) - e) >= 0) {
+        ok = true;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (!ok && error) atomicExch(error, 3);
+  }
+  __syncthreads();
+  for (int b = tid; b < batch; b += nt) {
+    unsigned long long k = 0ull;
+    for (int q = 0; q < x.world; ++q) {
+      const unsigned long long v = ld_relaxed_sys_u64(peer_key_slot(x, x.rank, par, q) + b);
+      k = v > k ? v : k;
+    }
+    s_keys[b] = k;
+  }
+  if (tid == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e;
+  __syncthreads();
+}
+
+}  // namespace gsp

@@ -42,6 +42,7 @@
 #include "gsp_async.cuh"
 #include "gsp_common.cuh"
 #include "gsp_internal.h"
+#include "gsp_peer.cuh"
 
 namespace gsp {
 namespace {
@@ -92,6 +93,23 @@ __device__ __forceinline__ void emit_unit(const RowSparseParams& p, int b, int v
     top.add(b, top1_key(DTypeTraits<T>::bits_to_float(bits), (uint64_t)(p.vocab_offset + v)), s_keys);
 }
 
+// Last CTA: takes the merged keys out of the workspace (re-zeroing it), merges
+// them across the ranks of a vocabulary-parallel group when one is given, and
+// writes the decoded top-1. All threads of the CTA call it.
+__device__ __forceinline__ void decode_top1(const RowSparseParams& p, unsigned long long* s_keys, uint32_t* s_word) {
+  const int tid = threadIdx.x;
+  if (p.peers.world > 1) {
+    for (int b = tid; b < p.batch; b += blockDim.x) s_keys[b] = atomicExch(p.keys + b, 0ull);
+    peer_exchange_keys(p.peers, s_keys, p.batch, s_word, p.error);
+  }
+  for (int b = tid; b < p.batch; b += blockDim.x) {
+    const unsigned long long k = p.peers.world > 1 ? s_keys[b] : atomicExch(p.keys + b, 0ull);
+    if (p.top_value) p.top_value[b] = key_value(k);
+    if (p.top_index) p.top_index[b] = key_index(k);
+    if (p.top_key) p.top_key[b] = key_to_signed(k);
+  }
+}
+
 // Cross-CTA top-1 merge: each CTA folds its shared-memory keys into the
 // workspace with atomicMax; the CTA that draws the last ticket decodes them and
 // re-zeroes keys and ticket for the next call. Nobody waits on anybody.
@@ -115,12 +133,7 @@ __device__ __forceinline__ void finalize_top1(const RowSparseParams& p, unsigned
   __syncthreads();
   if (*s_flag) {
     __threadfence();
-    for (int b = tid; b < p.batch; b += blockDim.x) {
-      const unsigned long long k = atomicExch(p.keys + b, 0ull);
-      if (p.top_value) p.top_value[b] = key_value(k);
-      if (p.top_index) p.top_index[b] = key_index(k);
-      if (p.top_key) p.top_key[b] = key_to_signed(k);
-    }
+    decode_top1(p, s_keys, reinterpret_cast<uint32_t*>(s_flag + 1));
     if (tid == 0) atomicExch(p.ticket, 0u);
   }
 }
@@ -776,14 +789,7 @@ __device__ __forceinline__ void coop_finish(const RowSparseParams& p, unsigned l
   __syncthreads();
   if (*s_flag) {
     __threadfence();
-    if (want_top) {
-      for (int b = tid; b < p.batch; b += blockDim.x) {
-        const unsigned long long k = atomicExch(p.keys + b, 0ull);
-        if (p.top_value) p.top_value[b] = key_value(k);
-        if (p.top_index) p.top_index[b] = key_index(k);
-        if (p.top_key) p.top_key[b] = key_to_signed(k);
-      }
-    }
+    if (want_top) decode_top1(p, s_keys, reinterpret_cast<uint32_t*>(s_flag + 1));
     for (int c = tid; c < G; c += blockDim.x) {
       p.slice_counts[c] = 0u;
       p.slice_ready[(size_t)c * kFlagStride] = 0u;

@@ -59,7 +59,18 @@ SIGNATURES = {
     "gsp_top1_from_keys": ([_vp, _i32, _vp, _vp, _vp], _i32),
     "gsp_row_sparse_logits_static": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
                                       _vp, _i64, _vp, _vp, _vp, _vp], _i32),
+    "gsp_peer_exchange_bytes": ([_i32, _i32], _sz),
+    "gsp_peer_exchange_alloc": ([_sz, ctypes.POINTER(_vp), _vp], _i32),
+    "gsp_peer_exchange_open": ([_vp, ctypes.POINTER(_vp)], _i32),
+    "gsp_peer_exchange_close": ([_vp], _i32),
+    "gsp_peer_exchange_free": ([_vp], _i32),
+    "gsp_vocab_parallel_logits": ([_i32] + _PROJECTION_ARGS[:-1] + [ctypes.POINTER(_vp), _i32, _i32, _i32, _vp],
+                                  _i32),
 }
+
+ROUTE_CODES = {"row-sparse": 0, "block-sparse": 1, "dense-mask": 2}
+IPC_HANDLE_BYTES = 64
+MAX_PEERS = 8
 
 
 def load() -> ctypes.CDLL:
@@ -189,6 +200,58 @@ def dense_masked(hidden, weight, mask, logits=None, top_value=None, top_index=No
                  vocab_offset: int = 0) -> None:
     _projection("gsp_dense_masked_logits", hidden, weight, mask, logits, top_value, top_index,
                 top_key, vocab_offset)
+
+
+# ---------------------------------------------------------------------------
+# vocabulary-parallel exchange buffers and the in-kernel cross-rank top-1
+# ---------------------------------------------------------------------------
+def peer_exchange_alloc(world_size: int, max_batch: int) -> tuple[int, bytes]:
+    """Zeroed exchange buffer on the current device: (device pointer, IPC handle)."""
+    lib = load()
+    nbytes = int(lib.gsp_peer_exchange_bytes(world_size, max_batch))
+    if nbytes == 0:
+        raise ValueError(f"bad exchange size: world {world_size}, max_batch {max_batch}")
+    buf = _vp()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib.gsp_peer_exchange_alloc(nbytes, ctypes.byref(buf), handle), "gsp_peer_exchange_alloc")
+    return int(buf.value), handle.raw
+
+
+def peer_exchange_open(handle: bytes) -> int:
+    """Maps another process's exchange buffer (same node) into this one."""
+    out = _vp()
+    _check(load().gsp_peer_exchange_open(ctypes.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES),
+                                         ctypes.byref(out)), "gsp_peer_exchange_open")
+    return int(out.value)
+
+
+def peer_exchange_close(ptr: int) -> None:
+    _check(load().gsp_peer_exchange_close(_vp(ptr)), "gsp_peer_exchange_close")
+
+
+def peer_exchange_free(ptr: int) -> None:
+    _check(load().gsp_peer_exchange_free(_vp(ptr)), "gsp_peer_exchange_free")
+
+
+def vocab_parallel(route: str, hidden, weight, mask, peers: list[int], rank: int, max_batch: int,
+                   logits=None, top_value=None, top_index=None, top_key=None, vocab_offset: int = 0) -> None:
+    """One rank's projection with the cross-rank top-1 merge in the kernel
+    (gsp_vocab_parallel_logits); peers[q] is rank q's exchange buffer as
+    mapped in this process."""
+    _require_cuda(hidden, weight, mask, logits)
+    lib = load()
+    batch, hdim = hidden.shape
+    vocab = weight.shape[0]
+    ws = workspace(hidden.device, batch, vocab)
+    arr = (_vp * len(peers))(*[_vp(int(q)) for q in peers])
+    status = lib.gsp_vocab_parallel_logits(
+        ROUTE_CODES[route], _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+        _ptr(mask), 0 if mask is None else mask.stride(0),
+        batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+        _ptr(logits), 0 if logits is None else logits.stride(0),
+        _ptr(top_value), _ptr(top_index), _ptr(top_key),
+        _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, _stream(hidden.device))
+    _check(status, "gsp_vocab_parallel_logits")
 
 
 def row_sparse_compact(hidden, weight, mask, compact_logits, compact_ids, offsets,

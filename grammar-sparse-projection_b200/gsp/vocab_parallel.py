@@ -12,8 +12,13 @@ slice with vocab_offset = start_r, and the ranks exchange only
   * when full logits are requested, the -inf-filled [B, V/R] logit slices
     (an all-gather).
 
-All collectives go through torch.distributed (NCCL between GPUs; gloo works
-for the host-side logic on CPU ranks).
+Two ways to merge the top-1: `PeerExchange` (the default on GPUs) does it
+inside the projection kernel - the last CTA of every rank stores its keys
+into every rank's exchange buffer over NVLink and waits for the others'
+(gsp_vocab_parallel_logits), so a step is one launch and no collective;
+without one, keys go through a torch.distributed MAX all-reduce (NCCL between
+GPUs; gloo works for the host-side logic on CPU ranks) and a decode launch.
+Full logits always go through an all-gather.
 """
 from __future__ import annotations
 
@@ -97,6 +102,42 @@ def gather_logits(local: torch.Tensor, vocab: int, group=None) -> torch.Tensor:
     return torch.cat([p[:, : hi - lo] for p, (lo, hi) in zip(parts, bounds)], dim=1)
 
 
+class PeerExchange:
+    """Exchange buffers of a vocabulary-parallel group for the in-kernel top-1
+    merge: this rank's own buffer plus every other rank's, mapped into this
+    process through CUDA IPC (one node). Creating and closing are collective:
+    every rank of `group` must take part, in the same order."""
+
+    def __init__(self, max_batch: int, group=None):
+        if not dist.is_initialized():
+            raise RuntimeError("PeerExchange needs an initialised process group")
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _native.MAX_PEERS:
+            raise ValueError(f"at most {_native.MAX_PEERS} ranks share an exchange")
+        self.max_batch = int(max_batch)
+        self.group = group
+        self.own, handle = _native.peer_exchange_alloc(self.world, self.max_batch)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.peers = [self.own if q == self.rank else _native.peer_exchange_open(h) for q, h in enumerate(handles)]
+        dist.barrier(group)  # every rank has mapped every buffer before any kernel writes
+
+    def close(self) -> None:
+        """Collective: after every rank's last exchange call has completed."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        for q, ptr in enumerate(self.peers):
+            if q != self.rank:
+                _native.peer_exchange_close(ptr)
+        dist.barrier(self.group)
+        _native.peer_exchange_free(self.own)
+        self.own = None
+        self.peers = []
+
+
 class VocabParallelHead:
     """This rank's shard of a vocabulary-parallel LM head.
 
@@ -106,7 +147,8 @@ class VocabParallelHead:
     arguments in the same order (the collectives are matched by order).
     """
 
-    def __init__(self, weight_shard: torch.Tensor, vocab: int, start: int, group=None):
+    def __init__(self, weight_shard: torch.Tensor, vocab: int, start: int, group=None,
+                 exchange: PeerExchange | None = None):
         if weight_shard.device.type != "cuda":
             raise ValueError("weight_shard must be a CUDA tensor")
         if start % 32:
@@ -116,13 +158,17 @@ class VocabParallelHead:
         self.start = start
         self.stop = start + weight_shard.shape[0]
         self.group = group
+        self.exchange = exchange
+        if exchange is not None and self.stop <= self.start:
+            raise ValueError("every rank of a peer exchange needs a non-empty shard")
 
     @classmethod
-    def from_full_weight(cls, weight: torch.Tensor, group=None) -> "VocabParallelHead":
+    def from_full_weight(cls, weight: torch.Tensor, group=None,
+                         exchange: PeerExchange | None = None) -> "VocabParallelHead":
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         rank = dist.get_rank(group) if dist.is_initialized() else 0
         lo, hi = shard_bounds(weight.shape[0], world, rank)
-        return cls(weight[lo:hi], weight.shape[0], lo, group)
+        return cls(weight[lo:hi], weight.shape[0], lo, group, exchange)
 
     def local_mask(self, bitmask_gpu: torch.Tensor) -> torch.Tensor:
         w0 = self.start // 32
@@ -137,6 +183,14 @@ class VocabParallelHead:
         mask = None if bitmask_gpu is None else self.local_mask(bitmask_gpu.reshape(batch, -1))
         local_logits = (torch.empty((batch, self.stop - self.start), device=dev, dtype=hidden.dtype)
                         if full_logits else None)
+        if self.exchange is not None:
+            top_value = torch.empty(batch, device=dev, dtype=torch.float32)
+            top_index = torch.empty(batch, device=dev, dtype=torch.int64)
+            _native.vocab_parallel(route, hidden_2d, self.weight, mask, self.exchange.peers, self.exchange.rank,
+                                   self.exchange.max_batch, logits=local_logits, top_value=top_value,
+                                   top_index=top_index, vocab_offset=self.start)
+            logits = gather_logits(local_logits, self.vocab, self.group) if full_logits else None
+            return top_value, top_index, logits
         keys = torch.empty(batch, device=dev, dtype=torch.int64)
         fn = {"row-sparse": _native.row_sparse, "block-sparse": _native.block_gemm,
               "dense-mask": _native.dense_masked}[route]

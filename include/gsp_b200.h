@@ -185,6 +185,55 @@ int32_t gsp_row_sparse_logits_static(const void* hidden, int64_t hidden_row_stri
 int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
                            int64_t* top_index, void* stream);
 
+/*
+ * Vocabulary-parallel head: top-1 merged across ranks inside the kernel.
+ *
+ * One process per GPU on one node, up to GSP_MAX_PEERS ranks; rank r holds a
+ * contiguous row shard of W (vocab_offset = its first global row) and the
+ * matching words of every request's mask. Set-up, once per rank:
+ *   1. gsp_peer_exchange_alloc(gsp_peer_exchange_bytes(R, max_batch), &buf,
+ *      handle): device memory (zeroed) and its IPC handle;
+ *   2. send the GSP_IPC_HANDLE_BYTES handle to every other rank over any host
+ *      channel (torch.distributed, a socket, ...);
+ *   3. gsp_peer_exchange_open(handle_q, &peer_q) for every other rank q
+ *      (peer access over NVLink is enabled by the mapping).
+ * Then every call of gsp_vocab_parallel_logits with peer_buffers[q] = rank q's
+ * buffer as mapped here (peer_buffers[rank] = buf) ends, inside the projection
+ * kernel, with an exchange over peer memory: the last CTA stores the rank's
+ * per-request top-1 keys into every rank's buffer, raises its flag there,
+ * waits (bounded, about a quarter of a second) for the other ranks' flags and
+ * writes the GLOBAL top-1 (global token ids) to top_value / top_index /
+ * top_key. Logits, when given, are this rank's shard only. No collective
+ * library call and no extra launch is involved, so the call can be captured
+ * in a CUDA graph. Every rank must make the same sequence of calls with the
+ * same route and batch; a wait that runs out sets the workspace error word
+ * to 3, after which the exchange buffers must be re-created. route is one of
+ * GSP_ROUTE_*; world_size 1 runs the plain projection.
+ * Replaces NCCL all-gather of (max, index) pairs; the reference is
+ * single-GPU and has no counterpart.
+ */
+#define GSP_MAX_PEERS 8
+#define GSP_IPC_HANDLE_BYTES 64
+#define GSP_ROUTE_ROW_SPARSE 0
+#define GSP_ROUTE_BLOCK_SPARSE 1
+#define GSP_ROUTE_DENSE_MASK 2
+
+size_t gsp_peer_exchange_bytes(int32_t world_size, int32_t max_batch);
+int32_t gsp_peer_exchange_alloc(size_t bytes, void** buffer, void* ipc_handle);
+int32_t gsp_peer_exchange_open(const void* ipc_handle, void** peer_buffer);
+int32_t gsp_peer_exchange_close(void* peer_buffer);
+int32_t gsp_peer_exchange_free(void* buffer);
+int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hidden_row_stride,
+                                  const void* weight, int64_t weight_row_stride,
+                                  const int32_t* bitmask, int64_t bitmask_row_stride,
+                                  int32_t batch, int32_t vocab, int32_t hidden_dim,
+                                  int32_t dtype, int64_t vocab_offset, void* logits,
+                                  int64_t logits_row_stride, float* top_value,
+                                  int64_t* top_index, int64_t* top_key, void* workspace,
+                                  size_t workspace_bytes, void* const* peer_buffers,
+                                  int32_t rank, int32_t world_size, int32_t max_batch,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,133 @@
+"""Vocabulary-parallel head on 2 GPUs (one spawned process per GPU, NCCL for
+the set-up): the in-kernel peer exchange (gsp_vocab_parallel_logits) and the
+NCCL all-reduce path both give the global greedy top-1 of the full head, equal
+to the oracle's exact argmax outside the near-tie window and bit-identical to
+each other, for every route, over repeated calls and CUDA-graph replays.
+Skipped on machines with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROUTES = ("row-sparse", "block-sparse", "dense-mask")
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(vocab, hidden, batch, seed, dtype):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), ".."))
+    from oracle import gsp_oracle as O
+    rng = np.random.default_rng(seed)
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * 0.05).to(dtype)
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).to(dtype)
+    ks = [int(k) for k in rng.integers(1, max(2, vocab // 50), size=batch)]
+    mask = O.make_batch_mask(rng, batch, vocab, ks, clustered=True, max_runs=8)
+    return w, h, mask
+
+
+def _worker(rank, world, port, result_path):
+    import sys
+    import datetime
+    root = os.path.join(os.path.dirname(__file__), "..")
+    sys.path.insert(0, root)
+    sys.path.insert(0, os.path.join(root, "grammar-sparse-projection_b200"))
+    import torch.distributed as dist
+    from gsp import _native
+    from gsp import vocab_parallel as vp
+    from oracle import gsp_oracle as O
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    failures = []
+    try:
+        xch = vp.PeerExchange(max_batch=40)
+        for vocab, hidden, batch, seed, dtype in ((50000, 256, 1, 1, torch.float16),
+                                                  (40000, 128, 3, 2, torch.bfloat16),
+                                                  (30001, 64, 33, 3, torch.float16)):
+            w, h, mask = _case(vocab, hidden, batch, seed, dtype)
+            exact = O.masked_logits_exact(h, w, mask)
+            head_peer = vp.VocabParallelHead.from_full_weight(w.to(dev), exchange=xch)
+            head_nccl = vp.VocabParallelHead.from_full_weight(w.to(dev))
+            hd, md = h.to(dev), torch.from_numpy(mask).to(dev)
+            for route in ROUTES:
+                tv_n, ti_n, _ = head_nccl.forward(hd, md, route=route)
+                for rep in range(3):  # repeated calls advance the exchange epoch
+                    tv_p, ti_p, lg = head_peer.forward(hd, md, route=route, full_logits=(rep == 0))
+                    if not (torch.equal(tv_p, tv_n) and torch.equal(ti_p, ti_n)):
+                        failures.append(f"{route} V={vocab} B={batch} rep {rep}: peer != nccl")
+                    if not O.top1_agrees(exact, ti_p.cpu(), dtype=dtype):
+                        failures.append(f"{route} V={vocab} B={batch}: top-1 vs oracle")
+                    if lg is not None:
+                        rep_ = O.compare_logits(exact, lg.cpu(), dtype=dtype)
+                        if not (rep_["support"] and rep_["values"]):
+                            failures.append(f"{route} V={vocab} B={batch}: gathered logits")
+            # CUDA graph: three exchange calls per replay, replayed twice
+            tv_g = torch.empty(batch, device=dev)
+            ti_g = torch.empty(batch, device=dev, dtype=torch.int64)
+            mask_local = head_peer.local_mask(md)
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                _native.vocab_parallel("row-sparse", hd, head_peer.weight, mask_local, xch.peers, xch.rank,
+                                       xch.max_batch, top_value=tv_g, top_index=ti_g, vocab_offset=head_peer.start)
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            dist.barrier()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(3):
+                    _native.vocab_parallel("row-sparse", hd, head_peer.weight, mask_local, xch.peers, xch.rank,
+                                           xch.max_batch, top_value=tv_g, top_index=ti_g,
+                                           vocab_offset=head_peer.start)
+            for _ in range(2):
+                dist.barrier()
+                g.replay()
+                torch.cuda.synchronize()
+                tv_n, ti_n, _ = head_nccl.forward(hd, md, route="row-sparse")
+                if not (torch.equal(tv_g, tv_n) and torch.equal(ti_g, ti_n)):
+                    failures.append(f"graph replay V={vocab} B={batch}")
+            del g
+        if _native.workspace_error(dev) != 0:
+            failures.append("workspace error word set")
+        dist.barrier()
+        xch.close()
+    except Exception as exc:  # reported to the parent
+        failures.append(f"exception: {exc!r}")
+    finally:
+        with open(f"{result_path}.{rank}", "w") as f:
+            f.write("\n".join(failures))
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_vocab_parallel_peer_exchange_two_gpus(tmp_path):
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    port = _free_port()
+    result = str(tmp_path / "result")
+    ctx = mp.spawn(_worker, args=(2, port, result), nprocs=2, join=False)
+    done = False
+    for _ in range(60):  # up to 10 minutes
+        done = ctx.join(timeout=10)
+        if done:
+            break
+    if not done:
+        for proc in ctx.processes:
+            proc.kill()
+        pytest.fail("vocab-parallel workers did not finish")
+    for r in range(2):
+        text = open(f"{result}.{r}").read()
+        assert text == "", f"rank {r}: {text}"

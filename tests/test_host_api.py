@@ -74,6 +74,32 @@ def test_c_abi_validation_rejects_before_launch():
     assert lib.gsp_top1_from_keys(None, 1, None, None, None) == _native.GSP_ERR_INVALID_ARGUMENT
 
 
+def _vp_call(route=0, batch=1, tv=FAKE, peers=None, rank=0, world=2, max_batch=4):
+    lib = _native.load()
+    arr = None if peers is None else (ctypes.c_void_p * len(peers))(*peers)
+    return lib.gsp_vocab_parallel_logits(route, FAKE, 8, FAKE, 8, None, 0, batch, 64, 8, 0, 0, None, 64,
+                                         tv, None, None, FAKE, 1 << 30, arr, rank, world, max_batch, None)
+
+
+def test_vocab_parallel_entry_validation():
+    lib = _native.load()
+    ok_peers = [FAKE, FAKE]
+    assert _vp_call(route=5, peers=ok_peers) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert b"route" in lib.gsp_last_error()
+    assert _vp_call(world=9, peers=ok_peers) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert _vp_call(rank=2, peers=ok_peers) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert _vp_call(tv=None, peers=ok_peers) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert b"top-1" in lib.gsp_last_error()
+    assert _vp_call(peers=None) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert _vp_call(peers=[FAKE, None]) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert _vp_call(batch=5, peers=ok_peers, max_batch=4) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert b"max_batch" in lib.gsp_last_error()
+    assert lib.gsp_peer_exchange_bytes(0, 4) == 0 and lib.gsp_peer_exchange_bytes(9, 4) == 0
+    assert lib.gsp_peer_exchange_bytes(8, 128) >= 1152 + 2 * 8 * 128 * 8
+    assert lib.gsp_peer_exchange_alloc(16, None, None) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert lib.gsp_peer_exchange_close(None) == _native.GSP_OK and lib.gsp_peer_exchange_free(None) == _native.GSP_OK
+
+
 def test_python_api_rejects_cpu_tensors_like_the_reference():
     h = torch.zeros(2, 8, dtype=torch.float16)
     w = torch.zeros(64, 8, dtype=torch.float16)

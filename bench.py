@@ -304,7 +304,7 @@ def main():
         if world == 1:
             _native.row_sparse(hidden, w, m, logits=logits, top_value=top_value, top_index=top_index)
         else:
-            _native.vocab_parallel("row-sparse", hidden, w, m, xch.peers, rank, xch.max_batch, logits=logits,
+            _native.vocab_parallel("row-sparse", hidden, w, m, xch.peers, rank, xch.max_batch, VOCAB, logits=logits,
                                    top_value=top_value, top_index=top_index, vocab_offset=lo)
 
     def barrier():
@@ -383,7 +383,7 @@ def main():
                                top_index=top_index)
         else:
             _native.vocab_parallel("row-sparse", dev_hidden, weight, dev_mask, xch.peers, rank, xch.max_batch,
-                                   logits=logits, top_value=top_value, top_index=top_index, vocab_offset=lo)
+                                   VOCAB, logits=logits, top_value=top_value, top_index=top_index, vocab_offset=lo)
         host_top[0:1].copy_(top_index, non_blocking=True)
         host_top[1:2].view(torch.float32)[:1].copy_(top_value, non_blocking=True)
 

@@ -375,7 +375,7 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
                                   int64_t logits_row_stride, float* top_value, int64_t* top_index,
                                   int64_t* top_key, void* workspace, size_t workspace_bytes_,
                                   void* const* peer_buffers, int32_t rank, int32_t world_size,
-                                  int32_t max_batch, void* stream) {
+                                  int32_t max_batch, int64_t total_vocab, void* stream) {
   const char* fn = "gsp_vocab_parallel_logits";
   if (route != GSP_ROUTE_ROW_SPARSE && route != GSP_ROUTE_BLOCK_SPARSE && route != GSP_ROUTE_DENSE_MASK)
     return fail(GSP_ERR_INVALID_ARGUMENT, "%s: unknown route %d", fn, route);
@@ -389,6 +389,10 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
   x.rank = rank;
   x.world = world_size;
   x.max_batch = max_batch;
+  if (vocab_offset < 0 || vocab_offset + (int64_t)vocab > total_vocab)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: shard [%lld, %lld) outside the head's %lld tokens", fn,
+                (long long)vocab_offset, (long long)(vocab_offset + vocab), (long long)total_vocab);
+  x.tagged = total_vocab < (int64_t)0xFFFFFF;  // the same on every rank
   if (world_size > 1) {
     if (!peer_buffers) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: peer_buffers is required", fn);
     if (batch > max_batch)

@@ -27,6 +27,7 @@ struct PeerExchange {
   int world;       // < 2: no exchange
   int max_batch;   // key slots per rank
   int batch_base;  // slot of this launch's request 0 (batch chunks of the block path)
+  int tagged;      // global token ids < 2^24 - 1: one self-tagged store per key, no flag
 };
 
 // Parameters of the row-sparse kernel (one launch covers every request).

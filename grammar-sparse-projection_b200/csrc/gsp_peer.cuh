@@ -10,6 +10,11 @@
 //   2. waits, bounded, until each of its own flags has reached e (a flag may
 //      already hold e + 1: the writer finished this call and started the next);
 //   3. takes the MAX of the R keys per request and records e as its epoch.
+// When every global token id is below 2^24 - 1 (x.tagged), steps 1-2 need no
+// fence and no flag: bits 24..31 of a key are then always set (the low word is
+// 0xffffffff - id), so they are replaced by the low 8 bits of e and each key
+// travels as one self-tagged 8-byte store; the reader polls each slot until it
+// carries tag e. The empty key (no legal token) travels as tag e alone.
 // A rank can run at most one call ahead of the slowest peer (it cannot finish
 // call e + 1 before every peer has written its e + 1 keys, which each peer does
 // only after reading its call-e keys), so two key buffers suffice. All ranks
@@ -38,6 +43,23 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
   return v;
 }
 
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+constexpr unsigned long long kTagMask = 0xFF000000ull;
+
+__device__ __forceinline__ unsigned long long tag_key(unsigned long long k, uint32_t e) {
+  return (k & ~kTagMask) | ((unsigned long long)(e & 0xFFu) << 24);
+}
+__device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t e) {
+  return ((w >> 24) & 0xFFu) == (e & 0xFFu);
+}
+__device__ __forceinline__ unsigned long long untag_key(unsigned long long w) {
+  const unsigned long long k = w & ~kTagMask;
+  return (k & 0xFFFFFFull) == 0ull ? 0ull : (k | kTagMask);  // low 24 bits 0: the empty key
+}
+
 __device__ __forceinline__ unsigned long long* peer_key_slot(const PeerExchange& x, int q, int parity, int src) {
   return reinterpret_cast<unsigned long long*>(x.buf[q] + kPeerKeysOffset) +
          ((size_t)parity * x.world + src) * x.max_batch + x.batch_base;
@@ -56,11 +78,42 @@ __device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsign
   __syncthreads();
   const uint32_t e = *s_word;
   const int par = (int)(e & 1u);
+  if (x.tagged) {
+    for (int i = tid; i < x.world * batch; i += nt) {
+      const int q = i / batch, b = i - q * batch;
+      st_relaxed_sys_u64(peer_key_slot(x, q, par, x.rank) + b, tag_key(s_keys[b], e));
+    }
+    for (int i = tid; i < x.world * batch; i += nt) {
+      const int q = i / batch, b = i - q * batch;
+      const unsigned long long* slot = peer_key_slot(x, x.rank, par, q) + b;
+      bool ok = false;
+      for (uint32_t it = 0; it < kPeerSpinLimit; ++it) {
+        if (tag_is(ld_relaxed_sys_u64(slot), e)) {
+          ok = true;
+          break;
+        }
+        __nanosleep(32);
+      }
+      if (!ok && error) atomicExch(error, 3);
+    }
+    __syncthreads();
+    for (int b = tid; b < batch; b += nt) {
+      unsigned long long k = 0ull;
+      for (int q = 0; q < x.world; ++q) {
+        const unsigned long long v = untag_key(ld_relaxed_sys_u64(peer_key_slot(x, x.rank, par, q) + b));
+        k = v > k ? v : k;
+      }
+      s_keys[b] = k;
+    }
+    if (tid == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e;
+    __syncthreads();
+    return;
+  }
   for (int i = tid; i < x.world * batch; i += nt) {
     const int q = i / batch, b = i - q * batch;
     peer_key_slot(x, q, par, x.rank)[b] = s_keys[b];
   }
-  __threadfence_system();
+  if (tid < x.world * batch) __threadfence_system();  // only the threads that stored keys
   __syncthreads();
   if (tid < x.world) st_release_sys(reinterpret_cast<uint32_t*>(x.buf[tid] + 128 + 128 * x.rank), e);
   if (tid < x.world) {

@@ -64,8 +64,8 @@ SIGNATURES = {
     "gsp_peer_exchange_open": ([_vp, ctypes.POINTER(_vp)], _i32),
     "gsp_peer_exchange_close": ([_vp], _i32),
     "gsp_peer_exchange_free": ([_vp], _i32),
-    "gsp_vocab_parallel_logits": ([_i32] + _PROJECTION_ARGS[:-1] + [ctypes.POINTER(_vp), _i32, _i32, _i32, _vp],
-                                  _i32),
+    "gsp_vocab_parallel_logits": ([_i32] + _PROJECTION_ARGS[:-1] + [ctypes.POINTER(_vp), _i32, _i32, _i32, _i64,
+                                                               _vp], _i32),
 }
 
 ROUTE_CODES = {"row-sparse": 0, "block-sparse": 1, "dense-mask": 2}
@@ -234,10 +234,11 @@ def peer_exchange_free(ptr: int) -> None:
 
 
 def vocab_parallel(route: str, hidden, weight, mask, peers: list[int], rank: int, max_batch: int,
-                   logits=None, top_value=None, top_index=None, top_key=None, vocab_offset: int = 0) -> None:
+                   total_vocab: int, logits=None, top_value=None, top_index=None, top_key=None,
+                   vocab_offset: int = 0) -> None:
     """One rank's projection with the cross-rank top-1 merge in the kernel
     (gsp_vocab_parallel_logits); peers[q] is rank q's exchange buffer as
-    mapped in this process."""
+    mapped in this process, total_vocab the whole head's vocabulary."""
     _require_cuda(hidden, weight, mask, logits)
     lib = load()
     batch, hdim = hidden.shape
@@ -250,7 +251,7 @@ def vocab_parallel(route: str, hidden, weight, mask, peers: list[int], rank: int
         batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
         _ptr(logits), 0 if logits is None else logits.stride(0),
         _ptr(top_value), _ptr(top_index), _ptr(top_key),
-        _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, _stream(hidden.device))
+        _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, total_vocab, _stream(hidden.device))
     _check(status, "gsp_vocab_parallel_logits")
 
 

@@ -187,8 +187,8 @@ class VocabParallelHead:
             top_value = torch.empty(batch, device=dev, dtype=torch.float32)
             top_index = torch.empty(batch, device=dev, dtype=torch.int64)
             _native.vocab_parallel(route, hidden_2d, self.weight, mask, self.exchange.peers, self.exchange.rank,
-                                   self.exchange.max_batch, logits=local_logits, top_value=top_value,
-                                   top_index=top_index, vocab_offset=self.start)
+                                   self.exchange.max_batch, self.vocab, logits=local_logits,
+                                   top_value=top_value, top_index=top_index, vocab_offset=self.start)
             logits = gather_logits(local_logits, self.vocab, self.group) if full_logits else None
             return top_value, top_index, logits
         keys = torch.empty(batch, device=dev, dtype=torch.int64)

@@ -208,7 +208,9 @@ int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
  * in a CUDA graph. Every rank must make the same sequence of calls with the
  * same route and batch; a wait that runs out sets the workspace error word
  * to 3, after which the exchange buffers must be re-created. route is one of
- * GSP_ROUTE_*; world_size 1 runs the plain projection.
+ * GSP_ROUTE_*; world_size 1 runs the plain projection. total_vocab is the
+ * whole head's vocabulary, the same on every rank (below 2^24 - 1 each key
+ * travels as one self-tagged store; larger heads add a fence and a flag).
  * Replaces NCCL all-gather of (max, index) pairs; the reference is
  * single-GPU and has no counterpart.
  */
@@ -232,7 +234,7 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
                                   int64_t* top_index, int64_t* top_key, void* workspace,
                                   size_t workspace_bytes, void* const* peer_buffers,
                                   int32_t rank, int32_t world_size, int32_t max_batch,
-                                  void* stream);
+                                  int64_t total_vocab, void* stream);
 
 #ifdef __cplusplus
 }

@@ -74,6 +74,17 @@ def _worker(rank, world, port, result_path):
                         rep_ = O.compare_logits(exact, lg.cpu(), dtype=dtype)
                         if not (rep_["support"] and rep_["values"]):
                             failures.append(f"{route} V={vocab} B={batch}: gathered logits")
+            # the fence-and-flag protocol of heads with 2^24 - 1 or more tokens
+            mask_local = head_peer.local_mask(md)
+            tv_n, ti_n, _ = head_nccl.forward(hd, md, route="row-sparse")
+            for _ in range(3):
+                tv_f = torch.empty(batch, device=dev)
+                ti_f = torch.empty(batch, device=dev, dtype=torch.int64)
+                _native.vocab_parallel("row-sparse", hd, head_peer.weight, mask_local, xch.peers, xch.rank,
+                                       xch.max_batch, 1 << 25, top_value=tv_f, top_index=ti_f,
+                                       vocab_offset=head_peer.start)
+                if not (torch.equal(tv_f, tv_n) and torch.equal(ti_f, ti_n)):
+                    failures.append(f"flag protocol V={vocab} B={batch}")
             # CUDA graph: three exchange calls per replay, replayed twice
             tv_g = torch.empty(batch, device=dev)
             ti_g = torch.empty(batch, device=dev, dtype=torch.int64)
@@ -82,7 +93,8 @@ def _worker(rank, world, port, result_path):
             s.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(s):
                 _native.vocab_parallel("row-sparse", hd, head_peer.weight, mask_local, xch.peers, xch.rank,
-                                       xch.max_batch, top_value=tv_g, top_index=ti_g, vocab_offset=head_peer.start)
+                                       xch.max_batch, vocab, top_value=tv_g, top_index=ti_g,
+                                       vocab_offset=head_peer.start)
             torch.cuda.current_stream().wait_stream(s)
             torch.cuda.synchronize()
             dist.barrier()
@@ -90,7 +102,7 @@ def _worker(rank, world, port, result_path):
             with torch.cuda.graph(g, stream=s):
                 for _ in range(3):
                     _native.vocab_parallel("row-sparse", hd, head_peer.weight, mask_local, xch.peers, xch.rank,
-                                           xch.max_batch, top_value=tv_g, top_index=ti_g,
+                                           xch.max_batch, vocab, top_value=tv_g, top_index=ti_g,
                                            vocab_offset=head_peer.start)
             for _ in range(2):
                 dist.barrier()

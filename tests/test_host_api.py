@@ -74,11 +74,11 @@ def test_c_abi_validation_rejects_before_launch():
     assert lib.gsp_top1_from_keys(None, 1, None, None, None) == _native.GSP_ERR_INVALID_ARGUMENT
 
 
-def _vp_call(route=0, batch=1, tv=FAKE, peers=None, rank=0, world=2, max_batch=4):
+def _vp_call(route=0, batch=1, tv=FAKE, peers=None, rank=0, world=2, max_batch=4, offset=0, total=128):
     lib = _native.load()
     arr = None if peers is None else (ctypes.c_void_p * len(peers))(*peers)
-    return lib.gsp_vocab_parallel_logits(route, FAKE, 8, FAKE, 8, None, 0, batch, 64, 8, 0, 0, None, 64,
-                                         tv, None, None, FAKE, 1 << 30, arr, rank, world, max_batch, None)
+    return lib.gsp_vocab_parallel_logits(route, FAKE, 8, FAKE, 8, None, 0, batch, 64, 8, 0, offset, None, 64,
+                                         tv, None, None, FAKE, 1 << 30, arr, rank, world, max_batch, total, None)
 
 
 def test_vocab_parallel_entry_validation():
@@ -94,6 +94,8 @@ def test_vocab_parallel_entry_validation():
     assert _vp_call(peers=[FAKE, None]) == _native.GSP_ERR_INVALID_ARGUMENT
     assert _vp_call(batch=5, peers=ok_peers, max_batch=4) == _native.GSP_ERR_INVALID_ARGUMENT
     assert b"max_batch" in lib.gsp_last_error()
+    assert _vp_call(peers=ok_peers, offset=96, total=128) == _native.GSP_ERR_INVALID_ARGUMENT
+    assert b"outside" in lib.gsp_last_error()
     assert lib.gsp_peer_exchange_bytes(0, 4) == 0 and lib.gsp_peer_exchange_bytes(9, 4) == 0
     assert lib.gsp_peer_exchange_bytes(8, 128) >= 1152 + 2 * 8 * 128 * 8
     assert lib.gsp_peer_exchange_alloc(16, None, None) == _native.GSP_ERR_INVALID_ARGUMENT

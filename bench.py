@@ -65,7 +65,8 @@ def parse_args():
     ap.add_argument("--copies", type=int, default=32, help="weight copies cycled through (one GPU)")
     ap.add_argument("--sweep-steps", type=int, default=100)
     ap.add_argument("--no-sweep", action="store_true")
-    ap.add_argument("--only", choices=("batched", "mixed"), default=None,
+    ap.add_argument("--no-vp", action="store_true", help="skip the vocabulary-parallel head section")
+    ap.add_argument("--only", choices=("batched", "mixed", "vp"), default=None,
                     help="run one extra section alone (small; for profiling)")
     ap.add_argument("--batch", type=int, default=32, help="batch of --only batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -77,16 +78,16 @@ def parse_args():
 # workload
 # ---------------------------------------------------------------------------
 def make_masks(n: int, density: float, pattern: str, seed: int) -> np.ndarray:
-    from oracle import gsp_oracle as O  # seeded generators only
+    from gsp import workloads as wl
     rng = np.random.default_rng(seed)
     k = int(round(density * VOCAB))
-    return np.concatenate([O.make_batch_mask(rng, 1, VOCAB, [k], clustered=(pattern == "clustered"),
+    return np.concatenate([wl.make_batch_mask(rng, 1, VOCAB, [k], clustered=(pattern == "clustered"),
                                              max_runs=64) for _ in range(n)])
 
 
 def legal_counts(masks: np.ndarray) -> np.ndarray:
-    from oracle import gsp_oracle as O
-    return O.unpack_bitmask(masks, VOCAB).sum(axis=1)
+    from gsp import workloads as wl
+    return wl.unpack_bitmask(masks, VOCAB).sum(axis=1)
 
 
 def read_peaks():
@@ -258,6 +259,8 @@ def main():
             g = torch.Generator(device=dev).manual_seed(1234)
             weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(2)]
             res = batched_section(dev, weights, peak, steps=max(args.steps, 1), batches=(args.batch,))
+        elif args.only == "vp":
+            res = vocab_parallel_section(dev, 1, 0, peak, steps=max(args.steps, 1), batches=(args.batch,))
         else:
             res = mixed_section(dev, peak, steps=max(args.steps, 1))
         print(json.dumps({"only": args.only, "result": res}), flush=True)
@@ -435,6 +438,7 @@ def main():
         same_gpu_dense = time_dense_baseline(dev, weight, hidden, masks, args)
         batched = batched_section(dev, weights[:8], peak)
         mixed = mixed_section(dev, peak)
+    vp_head = None if args.no_vp else vocab_parallel_section(dev, world, rank, peak)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         w_cpu = weight.cpu().numpy()
         h_cpu = hidden.cpu().numpy()
@@ -462,6 +466,7 @@ def main():
             "batched": batched,
             "mixed": mixed,
             "same_gpu_dense_mask": same_gpu_dense,
+            "vocab_parallel_head": vp_head,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -472,8 +477,8 @@ def main():
 
 
 def legal_counts_local(masks_np: np.ndarray, lo: int, hi: int) -> np.ndarray:
-    from oracle import gsp_oracle as O
-    return O.unpack_bitmask(masks_np, VOCAB)[:, lo:hi].sum(axis=1)
+    from gsp import workloads as wl
+    return wl.unpack_bitmask(masks_np, VOCAB)[:, lo:hi].sum(axis=1)
 
 
 def max_over_ranks(x: float, world: int) -> float:
@@ -527,16 +532,16 @@ def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
     the block kernel's roofline and whether the B200 cost model picked the
     measured best route."""
     from gsp import _native, triton_runtime as tr
-    from oracle import gsp_oracle as O
+    from gsp import workloads as wl
     import torch.nn.functional as F
     out = []
     ntiles = (VOCAB + 127) // 128
     for batch in batches:
         rng = np.random.default_rng(300 + batch)
-        masks_np = [O.make_batch_mask(rng, batch, VOCAB, [1242] * batch, clustered=True, max_runs=16) for _ in range(8)]
+        masks_np = [wl.make_batch_mask(rng, batch, VOCAB, [1242] * batch, clustered=True, max_runs=16) for _ in range(8)]
         masks = [torch.from_numpy(m).to(dev) for m in masks_np]
-        active = [O.active_tiles(m, VOCAB) for m in masks_np]
-        legal = [O.unpack_bitmask(m, VOCAB).sum(axis=1) for m in masks_np]
+        active = [wl.active_tiles(m, VOCAB) for m in masks_np]
+        legal = [wl.unpack_bitmask(m, VOCAB).sum(axis=1) for m in masks_np]
         hidden = torch.randn(batch, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(batch)).half()
         logits = torch.empty(batch, VOCAB, device=dev, dtype=torch.float16)
         tv = torch.empty(batch, device=dev, dtype=torch.float32)
@@ -579,12 +584,101 @@ def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
     return out
 
 
+VP_VOCAB, VP_HIDDEN = 262144, 8192
+
+
+def vocab_parallel_section(dev, world, rank, peak, steps=10, batches=(1, 32, 128)):
+    """Vocabulary-parallel head: V=262,144, H=8,192 bf16, W ~ N(0, 0.01)
+    row-sharded over the ranks (this rank's contiguous shard on its GPU),
+    batch 1 / 32 / 128, each request 1% legal in <= 16 clustered runs, greedy
+    top-1 merged across the ranks inside the kernel (one rank: the plain
+    kernels). Every route graph-timed on every rank, max over ranks; the
+    per-rank roofline uses each route's algorithmic bytes on the shard."""
+    from gsp import _native, triton_runtime as tr, vocab_parallel as vp
+    from gsp import workloads as wl
+    lo, hi = vp.shard_bounds(VP_VOCAB, world, rank)
+    vloc = hi - lo
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    w = (torch.randn(vloc, VP_HIDDEN, device=dev, generator=g) * 0.01).bfloat16()
+    xch = vp.PeerExchange(max_batch=max(batches)) if world > 1 else None
+    plain = {"row-sparse": _native.row_sparse, "block-sparse": _native.block_gemm,
+             "dense-mask": _native.dense_masked}
+    row_bytes = VP_HIDDEN * 2
+    out = []
+    for batch in batches:
+        rng = np.random.default_rng(500 + batch)  # the same masks on every rank
+        full = [wl.make_batch_mask(rng, batch, VP_VOCAB, [VP_VOCAB // 100] * batch, clustered=True, max_runs=16)
+                for _ in range(4)]
+        local_np = [np.ascontiguousarray(m[:, lo // 32:(hi + 31) // 32]) for m in full]
+        masks = [torch.from_numpy(m).to(dev) for m in local_np]
+        legal = [wl.unpack_bitmask(m, VP_VOCAB)[:, lo:hi].sum(axis=1) for m in full]
+        active = [wl.active_tiles(m, vloc) for m in local_np]
+        h = torch.randn(batch, VP_HIDDEN, device=dev,
+                        generator=torch.Generator(device=dev).manual_seed(600 + batch)).bfloat16()
+        tv = torch.empty(batch, device=dev, dtype=torch.float32)
+        ti = torch.empty(batch, device=dev, dtype=torch.int64)
+        times, fracs = {}, {}
+        route_bytes = {"row-sparse": float(np.mean([l.sum() for l in legal])) * row_bytes,
+                       "block-sparse": float(np.mean(active)) * 128 * row_bytes,
+                       "dense-mask": float(vloc) * row_bytes}
+        for route in ("row-sparse", "block-sparse", "dense-mask"):
+            def fn(i, route=route):
+                m = masks[i % 4]
+                if xch is None:
+                    plain[route](h, w, m, top_value=tv, top_index=ti)
+                else:
+                    _native.vocab_parallel(route, h, w, m, xch.peers, rank, xch.max_batch, VP_VOCAB,
+                                           top_value=tv, top_index=ti, vocab_offset=lo)
+            t = max_over_ranks(synced_graph_time_us(dev, steps, fn, world), world) / steps
+            times[route] = t
+            fracs[route] = route_bytes[route] / (t * 1e-6) / 1e9 / peak
+        best = min(times, key=times.get)
+        choice = tr.choose_route(batch, vloc, VP_HIDDEN, 2, legal[0].tolist(), active[0])
+        out.append({"batch": batch, "us_per_step": times, "hbm_roofline_frac_per_rank": fracs,
+                    "active_tile_fraction_per_rank": float(np.mean(active)) / ((vloc + 127) // 128),
+                    "best_route": best, "b200_policy_route": choice,
+                    "tokens_per_s": batch / (times[best] * 1e-6)})
+    if xch is not None:
+        xch.close()
+    return {"vocab": VP_VOCAB, "hidden": VP_HIDDEN, "dtype": "bf16", "ranks": world,
+            "outputs": "greedy top-1 (global ids), no logits", "results": out}
+
+
+def synced_graph_time_us(dev, n, fn, world):
+    """Like graph_time_us, with the ranks aligned by a barrier before each
+    replay (their kernels wait on one another inside the exchange)."""
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(2):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for i in range(n):
+            fn(i)
+    if world > 1:
+        torch.distributed.barrier()
+    graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    b.synchronize()
+    del graph
+    return a.elapsed_time(b) * 1e3
+
+
 def mixed_section(dev, peak, steps=10):
     """Mixed-density dispatcher sweep: V=151,936, H=1,024 bf16, batch 64;
     a seeded mix of near-unconstrained (95% uniform) and constrained (0.2% in
     <= 16 runs) requests. Reports each route's time and both policies' picks."""
     from gsp import _native, triton_runtime as tr
-    from oracle import gsp_oracle as O
+    from gsp import workloads as wl
     vocab, hidden, batch = 151936, 1024, 64
     g = torch.Generator(device=dev).manual_seed(5)
     weights = [(torch.randn(vocab, hidden, device=dev, generator=g) * 0.02).bfloat16() for _ in range(4)]
@@ -601,10 +695,10 @@ def mixed_section(dev, peak, steps=10):
             legal = np.zeros((batch, vocab), dtype=bool)
             order = rng.permutation(batch)
             for j, b in enumerate(order):
-                ids = (O.clustered_legal_ids(rng, vocab, int(0.002 * vocab), 16) if j < n_con
-                       else O.uniform_legal_ids(rng, vocab, int(0.95 * vocab)))
+                ids = (wl.clustered_legal_ids(rng, vocab, int(0.002 * vocab), 16) if j < n_con
+                       else wl.uniform_legal_ids(rng, vocab, int(0.95 * vocab)))
                 legal[b, ids] = True
-            masks_np.append(O.pack_bitmask(legal))
+            masks_np.append(wl.pack_bitmask(legal))
         masks = [torch.from_numpy(m).to(dev) for m in masks_np]
         times = {}
         for name, fn in (("block-sparse", _native.block_gemm), ("dense-mask", _native.dense_masked),
@@ -614,8 +708,8 @@ def mixed_section(dev, peak, steps=10):
         best = min(times, key=times.get)
         fwf = tr.full_word_fraction_cpu(torch.from_numpy(masks_np[0]))
         ref_route = tr._reference_route(batch, fwf, 0.80)
-        stats_legal = O.unpack_bitmask(masks_np[0], vocab).sum(axis=1).tolist()
-        b200_route = tr.choose_route(batch, vocab, hidden, 2, stats_legal, O.active_tiles(masks_np[0], vocab))
+        stats_legal = wl.unpack_bitmask(masks_np[0], vocab).sum(axis=1).tolist()
+        b200_route = tr.choose_route(batch, vocab, hidden, 2, stats_legal, wl.active_tiles(masks_np[0], vocab))
         out.append({"constrained_fraction": frac, "us_per_step": times, "best_route": best,
                     "reference_policy_route": ref_route, "reference_policy_us": times[ref_route],
                     "b200_policy_route": b200_route, "b200_policy_us": times[b200_route],

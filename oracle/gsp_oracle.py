@@ -25,6 +25,7 @@ interpreter, its gsp.runtime on CPU tensors, xgrammar's CPU mask kernel).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -282,42 +283,23 @@ def constrained_projection(hidden, weight, allowed_ids, *, dense_threshold: floa
 # ---------------------------------------------------------------------------
 # seeded synthetic inputs (the workload generators shared by tests and bench)
 # ---------------------------------------------------------------------------
-def uniform_legal_ids(rng: np.random.Generator, vocab: int, k: int) -> np.ndarray:
-    """k distinct token ids drawn uniformly (tests/test_triton_block_gemm.py:16-22 style)."""
-    return np.sort(rng.choice(vocab, size=k, replace=False))
+# Seeded legal-set generators: the package's workload module (numpy only),
+# loaded from its file so that this module never imports a package named
+# `gsp` (the golden-vector script imports the reference's).
+def _load_workloads():
+    import importlib.util
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                        "grammar-sparse-projection_b200", "gsp", "workloads.py")
+    spec = importlib.util.spec_from_file_location("gsp_b200_workloads", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
-def clustered_legal_ids(rng: np.random.Generator, vocab: int, k: int, max_runs: int) -> np.ndarray:
-    """k distinct token ids packed into 1..max_runs contiguous runs (enum-like
-    grammar states), at random non-overlapping positions."""
-    k = int(min(max(k, 0), vocab))
-    if k == 0:
-        return np.zeros(0, dtype=np.int64)
-    runs = int(rng.integers(1, max(1, min(max_runs, k)) + 1))
-    # split k into `runs` positive lengths
-    cuts = np.sort(rng.choice(np.arange(1, k), size=runs - 1, replace=False)) if runs > 1 else np.zeros(0, dtype=np.int64)
-    lengths = np.diff(np.concatenate([[0], cuts, [k]])).astype(np.int64)
-    # place runs with random gaps that sum to vocab - k
-    free = vocab - k
-    gaps = rng.multinomial(free, np.ones(runs + 1) / (runs + 1))
-    ids = []
-    pos = 0
-    for r in range(runs):
-        pos += int(gaps[r])
-        ids.append(np.arange(pos, pos + lengths[r], dtype=np.int64))
-        pos += int(lengths[r])
-    return np.concatenate(ids)
-
-
-def make_batch_mask(rng: np.random.Generator, batch: int, vocab: int, k_per_request,
-                    *, clustered: bool = False, max_runs: int = 64) -> np.ndarray:
-    """Packed int32 mask [batch, ceil(V/32)] with the given legal counts."""
-    ks = list(k_per_request) if np.ndim(k_per_request) else [int(k_per_request)] * batch
-    legal = np.zeros((batch, vocab), dtype=bool)
-    for b, k in enumerate(ks):
-        ids = clustered_legal_ids(rng, vocab, k, max_runs) if clustered else uniform_legal_ids(rng, vocab, k)
-        legal[b, ids] = True
-    return pack_bitmask(legal)
+_workloads = _load_workloads()
+uniform_legal_ids = _workloads.uniform_legal_ids
+clustered_legal_ids = _workloads.clustered_legal_ids
+make_batch_mask = _workloads.make_batch_mask
 
 
 def cpu_row_sparse_step(hidden: np.ndarray, weight: np.ndarray, mask: np.ndarray, vocab: int) -> tuple[np.ndarray, np.ndarray]:

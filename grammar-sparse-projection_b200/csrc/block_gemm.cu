@@ -10,8 +10,7 @@
 // Two launches:
 //  * tile_builder_kernel: for every 128-row vocabulary tile, OR of the batch's
 //    mask words (4 words per request); active tile ids are compacted per
-//    builder block of kBuilderTiles tiles, and -inf is written over every
-//    request's outputs in inactive tiles. Skipped in dense mode.
+//    builder block of kBuilderTiles tiles. Skipped in dense mode.
 //  * tc_projection_kernel: one persistent CTA per SM, 6 warps.
 //      warp 0      one lane issues TMA loads of the W tile (128 rows x 64 K,
 //                  128-byte swizzle) and of h (Npad rows x 64 K) into a ring of
@@ -20,7 +19,9 @@
 //                  rows, N = batch padded to a multiple of 32, K = 16 per
 //                  instruction) into one of two TMEM accumulators, committing
 //                  each stage back to the producer and each tile to the epilogue;
-//      warps 2-5   epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
+//      warps 2-5   epilogue: first -inf over every request's outputs in the
+//                  inactive tiles (block mode; while the first accumulator is
+//                  computed), then per tile tcgen05.ld of the accumulator (one TMEM lane = one
 //                  vocabulary row per thread), mask bit, rounding, -inf, logits
 //                  stores coalesced along the vocabulary, and 64-bit top-1 keys
 //                  reduced across the warp's 32 rows with a transpose-reduce.
@@ -103,6 +104,41 @@ __device__ __forceinline__ int list_slot(const GemmConfig& c, const int* s_pref,
 
 __device__ __forceinline__ int tile_at(const BlockGemmParams& p, const GemmConfig& c, const int* s_pref, int pos) {
   return p.dense ? pos : p.tile_list[list_slot(c, s_pref, pos)];
+}
+
+// -inf over every request's outputs in the inactive 128-row tiles
+// t = cta + G * (ew + 4 j) (block mode): a tile is inactive when no request
+// has a legal token in it, the same test the builder applies. Run by the
+// epilogue warps (ew = 0..3) before their first accumulator arrives.
+template <typename T>
+__device__ __forceinline__ void fill_inactive_tiles(const BlockGemmParams& p, int ntiles, int cta, int G, int ew,
+                                                    int lane) {
+  const int V = p.vocab, nw = p.nw, B = p.batch;
+  const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
+  const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 15) == 0) && (p.logits_stride % 8 == 0);
+  for (int t = cta + ew * G; t < ntiles; t += 4 * G) {
+    uint32_t any = 0u;
+    for (int b = lane; b < B; b += 32) {
+      const uint32_t* row = p.mask + (int64_t)b * p.mask_stride;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int w = t * 4 + j;
+        if (w < nw) any |= tail_clip(__ldg(row + w), w, V);
+      }
+    }
+    if (__any_sync(FULL_MASK, any != 0u)) continue;
+    const int r0 = t * kTileRows;
+    uint16_t* base = static_cast<uint16_t*>(p.logits) + r0;
+    if (vec_ok && r0 + kTileRows <= V) {
+      // 256 B per request: lanes 0-15 take request b, lanes 16-31 request b + 1
+      for (int b = lane >> 4; b < B; b += 2)
+        reinterpret_cast<uint4*>(base + (int64_t)b * p.logits_stride)[lane & 15] = make_uint4(x, x, x, x);
+    } else {
+      for (int b = 0; b < B; ++b)
+        for (int r = lane; r < kTileRows && r0 + r < V; r += 32) base[(int64_t)b * p.logits_stride + r] = ninf;
+    }
+  }
 }
 
 template <typename T>
@@ -252,6 +288,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;
     const int nchunks = c.npad / 32;
     const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
+    if (!p.dense && p.logits) fill_inactive_tiles<T>(p, c.ntiles, cta, G, warp - 2, lane);
     unsigned long long running[kMaxNpad / 32];
 #pragma unroll
     for (int j = 0; j < kMaxNpad / 32; ++j) running[j] = 0ull;
@@ -385,8 +422,6 @@ constexpr int kBuilderThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kBuilderThreads) tile_builder_kernel(const BlockGemmParams p, int ntiles) {
   __shared__ uint32_t s_act[kBuilderTiles];
-  __shared__ int s_inactive[kBuilderTiles];
-  __shared__ int s_ninactive;
   const int tid = threadIdx.x;
   const int t0 = blockIdx.x * kBuilderTiles;
   const int V = p.vocab, nw = p.nw, B = p.batch;
@@ -419,41 +454,13 @@ __global__ void __launch_bounds__(kBuilderThreads) tile_builder_kernel(const Blo
     const bool valid = t < ntiles;
     const bool act = valid && s_act[tid] != 0u;
     const unsigned am = __ballot_sync(FULL_MASK, act);
-    const unsigned im = __ballot_sync(FULL_MASK, valid && !act);
     const unsigned below = (1u << tid) - 1u;
     if (act) p.tile_list[t0 + __popc(am & below)] = t;
-    if (valid && !act) s_inactive[__popc(im & below)] = t;
-    if (tid == 0) {
-      p.tile_counts[blockIdx.x] = __popc(am);
-      s_ninactive = __popc(im);
-    }
+    if (tid == 0) p.tile_counts[blockIdx.x] = __popc(am);
   }
-  __syncthreads();
-
   // The projection kernel may start its set-up now (programmatic dependent
   // launch); its griddepcontrol.wait still waits for this grid to finish.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-
-  // -inf over every request's outputs in the inactive tiles of this block:
-  // a warp takes one inactive tile and sweeps all requests (256 B per store).
-  if (p.logits) {
-    const int lane = tid & 31, warp = tid >> 5, nwarps = kBuilderThreads / 32;
-    const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
-    const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
-    const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 7) == 0) && (p.logits_stride % 4 == 0);
-    for (int i = warp; i < s_ninactive; i += nwarps) {
-      const int r0 = s_inactive[i] * kTileRows;
-      uint16_t* base = static_cast<uint16_t*>(p.logits) + r0;
-      if (vec_ok && r0 + kTileRows <= V) {
-#pragma unroll 4
-        for (int b = 0; b < B; ++b)
-          reinterpret_cast<uint2*>(base + (int64_t)b * p.logits_stride)[lane] = make_uint2(x, x);
-      } else {
-        for (int b = 0; b < B; ++b)
-          for (int r = lane; r < kTileRows && r0 + r < V; r += 32) base[(int64_t)b * p.logits_stride + r] = ninf;
-      }
-    }
-  }
 }
 
 // ---------------------------------------------------------------------------

@@ -184,6 +184,38 @@ def _projection(entry: str, hidden: torch.Tensor, weight: torch.Tensor, mask: to
     _check(status, entry)
 
 
+class PreparedProjection:
+    """One projection call with its arguments converted once: device pointers,
+    strides, sizes, dtype, workspace and stream are fixed at construction, so
+    each call() only crosses the C ABI. For decode loops that call the head
+    repeatedly on the same buffers (new contents each step). entry is
+    "gsp_row_sparse_logits", "gsp_block_gemm_logits" or
+    "gsp_dense_masked_logits"; the stream is the current one at construction."""
+
+    def __init__(self, entry: str, hidden, weight, mask, logits=None, top_value=None, top_index=None,
+                 top_key=None, vocab_offset: int = 0):
+        _require_cuda(hidden, weight, mask, logits)
+        lib = load()
+        batch, hdim = hidden.shape
+        vocab = weight.shape[0]
+        ws = workspace(hidden.device, batch, vocab)
+        self._keep = (hidden, weight, mask, logits, top_value, top_index, top_key, ws)
+        self._entry = entry
+        self._fn = getattr(lib, entry)
+        self._args = (
+            _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+            _ptr(mask), 0 if mask is None else mask.stride(0),
+            batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+            _ptr(logits), 0 if logits is None else logits.stride(0),
+            _ptr(top_value), _ptr(top_index), _ptr(top_key),
+            _ptr(ws), ws.numel(), _stream(hidden.device))
+
+    def __call__(self) -> None:
+        status = self._fn(*self._args)
+        if status:
+            _check(status, self._entry)
+
+
 def row_sparse(hidden, weight, mask, logits=None, top_value=None, top_index=None, top_key=None,
                vocab_offset: int = 0) -> None:
     _projection("gsp_row_sparse_logits", hidden, weight, mask, logits, top_value, top_index,

@@ -3,6 +3,7 @@
 // or host synchronisation happens here.
 #include <cstdarg>
 #include <cstdio>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 
@@ -37,6 +38,9 @@ int tile_builder_blocks(int vocab) {
 }
 
 size_t workspace_bytes(int batch, int vocab) { return workspace_bytes_for((size_t)batch, (size_t)vocab); }
+size_t row_sparse_workspace_bytes(int batch, int vocab) {
+  return row_sparse_workspace_bytes_for((size_t)batch, (size_t)vocab);
+}
 
 Workspace carve_workspace(void* base, int batch, int vocab) {
   const int ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
@@ -57,6 +61,10 @@ Workspace carve_workspace(void* base, int batch, int vocab) {
   p += align256(sizeof(unsigned int) * kMaxSlices * kFlagStride);
   w.unit_list = reinterpret_cast<uint32_t*>(p);
   w.list_cap = (int64_t)unit_list_cap((size_t)batch, (size_t)vocab);
+  p += align256(sizeof(uint32_t) * (size_t)w.list_cap);
+  w.sample_keys = reinterpret_cast<unsigned long long*>(p);
+  p += align256(sizeof(unsigned long long) * (size_t)batch);
+  w.stat_partials = reinterpret_cast<unsigned long long*>(p);
   return w;
 }
 
@@ -131,13 +139,14 @@ int32_t validate_projection(const char* fn, const void* hidden, int64_t hidden_r
   return GSP_OK;
 }
 
+// full: the call uses the sampler's part of the workspace too.
 int32_t check_workspace(const char* fn, bool needed, void* workspace, size_t bytes, int32_t batch,
-                        int32_t vocab) {
+                        int32_t vocab, bool full = false) {
   if (!needed) return GSP_OK;
   if (!workspace) return fail(GSP_ERR_WORKSPACE, "%s: workspace is required for this call", fn);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return fail(GSP_ERR_WORKSPACE, "%s: workspace must be 256-byte aligned", fn);
-  const size_t need = workspace_bytes(batch, vocab);
+  const size_t need = full ? workspace_bytes(batch, vocab) : row_sparse_workspace_bytes(batch, vocab);
   if (bytes < need)
     return fail(GSP_ERR_WORKSPACE, "%s: workspace has %zu bytes, needs %zu", fn, bytes, need);
   return GSP_OK;
@@ -173,6 +182,8 @@ void attach_workspace(RowSparseParams& p, void* workspace) {
   p.slice_ready = w.slice_ready;
   p.unit_list = w.unit_list;
   p.list_cap = w.list_cap;
+  p.sample_keys = w.sample_keys;
+  p.stat_partials = w.stat_partials;
 }
 
 int32_t projection_common(const char* fn, bool tensor_core, int dense, const void* hidden,
@@ -366,6 +377,37 @@ int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
   return cuda_status(
       launch_top1_from_keys(keys, batch, top_value, top_index, static_cast<cudaStream_t>(stream)),
       fn);
+}
+
+int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                              int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride,
+                              int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype,
+                              int64_t vocab_offset, void* logits, int64_t logits_row_stride, float temperature,
+                              const uint64_t* seeds, uint64_t offset, int64_t* sample_index,
+                              float* sample_logsumexp, float* top_value, int64_t* top_index, void* workspace,
+                              size_t workspace_bytes_, void* stream) {
+  const char* fn = "gsp_row_sparse_sample";
+  int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                   bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
+  if (st != GSP_OK) return st;
+  if (!(temperature > 0.f) || !std::isfinite(temperature))
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: temperature must be positive and finite", fn);
+  if (!seeds || !sample_index) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: seeds and sample_index are required", fn);
+  st = check_workspace(fn, true, workspace, workspace_bytes_, batch, vocab, true);
+  if (st != GSP_OK) return st;
+  RowSparseParams p = make_row_sparse(hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                      bitmask_row_stride, batch, vocab, hidden_dim, vocab_offset);
+  p.logits = logits;
+  p.logits_stride = batch > 1 ? logits_row_stride : vocab;
+  p.top_value = top_value;
+  p.top_index = top_index;
+  attach_workspace(p, workspace);
+  p.sample_index = sample_index;
+  p.sample_lse = sample_logsumexp;
+  p.seeds = seeds;
+  p.offset = offset;
+  p.inv_temp = 1.0f / temperature;
+  return cuda_status(launch_row_sparse(p, dtype, static_cast<cudaStream_t>(stream)), fn);
 }
 
 int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hidden_row_stride,

@@ -70,6 +70,14 @@ struct RowSparseParams {
   uint32_t* unit_list;
   int64_t list_cap;
   PeerExchange peers;  // cross-rank top-1 merge (world < 2: none)
+  // fused sampler (sample_index != nullptr; contract in gsp_sampler.cuh)
+  int64_t* sample_index;             // [batch] sampled global token ids
+  float* sample_lse;                 // [batch] log-sum-exp of legal logits * inv_temp (optional)
+  const uint64_t* seeds;             // [batch] per-request generator keys
+  uint64_t offset;                   // step counter
+  float inv_temp;                    // 1 / temperature
+  unsigned long long* sample_keys;   // workspace [batch]
+  unsigned long long* stat_partials; // workspace [kMaxSlices][batch]
 };
 
 // Parameters of the tensor-core block / dense projection.
@@ -118,6 +126,8 @@ struct Workspace {
   unsigned int* slice_ready;
   uint32_t* unit_list;
   int64_t list_cap;
+  unsigned long long* sample_keys;
+  unsigned long long* stat_partials;
 };
 
 // Active-tile builder granularity: tiles per builder block (one count each).
@@ -136,16 +146,22 @@ constexpr size_t unit_list_cap(size_t batch, size_t vocab) {
 
 constexpr size_t align256c(size_t x) { return (x + 255) / 256 * 256; }
 
-// Workspace bytes for (batch, vocab): ticket + error word + one 64-bit key per
-// request, the compacted active-tile list, the per-builder-block counts, the
-// slice counts and flags, and the unit list.
-constexpr size_t workspace_bytes_for(size_t batch, size_t vocab) {
+// Workspace bytes for (batch, vocab) of every call but the sampler: ticket +
+// error word + one 64-bit key per request, the compacted active-tile list, the
+// per-builder-block counts, the slice counts and flags, and the unit list.
+constexpr size_t row_sparse_workspace_bytes_for(size_t batch, size_t vocab) {
   return align256c(16 + 8 * batch) + align256c(4 * ((vocab + 127) / 128)) +
          align256c(4 * (((vocab + 127) / 128 + kBuilderTiles - 1) / kBuilderTiles)) + align256c(4 * kMaxSlices + 256) +
          align256c(4 * kMaxSlices * kFlagStride) + align256c(4 * unit_list_cap(batch, vocab));
 }
 
+// ... plus the sampler's per-request keys and per-CTA (max, sum) partials.
+constexpr size_t workspace_bytes_for(size_t batch, size_t vocab) {
+  return row_sparse_workspace_bytes_for(batch, vocab) + align256c(8 * batch) + align256c(8 * kMaxSlices * batch);
+}
+
 size_t workspace_bytes(int batch, int vocab);
+size_t row_sparse_workspace_bytes(int batch, int vocab);
 Workspace carve_workspace(void* base, int batch, int vocab);
 
 int num_sms(int device);

@@ -1,0 +1,117 @@
+// Fused grammar-conditioned sampler: the sampling contract and its device
+// helpers.
+//
+// For request b with legal tokens L_b, rounded logits x_v (the values the
+// materialised logits would hold), temperature T = 1 / inv_temp, seed k_b and
+// step counter `offset`:
+//
+//   u_v  = ((philox4x32_10({v, offset_lo, offset_hi, 0}, {k_lo, k_hi}).x >> 8) + 0.5) * 2^-24
+//   g_v  = -log(-log(u_v))                         (standard Gumbel noise)
+//   s_v  = x_v * inv_temp + g_v                     (all in fp32)
+//   sample_b = argmax_{v in L_b} s_v                (ties to the lowest id)
+//   lse_b    = log sum_{v in L_b} exp(x_v * inv_temp)
+//
+// By the Gumbel-max property, sample_b is distributed exactly as softmax of
+// x * inv_temp over the legal tokens; lse_b gives the sampled token's log
+// probability, x * inv_temp - lse_b. u_v takes 2^24 values strictly inside
+// (0, 1), each exact in fp32. v is the global token id (vocab_offset + row).
+//
+// Philox4x32-10 is the counter-based generator of Salmon, Moraes, Dror and
+// Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC 2011): ten rounds
+// of two 32x32 -> 64-bit multiplies with the published multipliers, the key
+// bumped by the published Weyl constants between rounds.
+#pragma once
+
+#include <stdint.h>
+
+#include "gsp_common.cuh"
+
+namespace gsp {
+
+__host__ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  constexpr uint32_t kM0 = 0xD2511F53u, kM1 = 0xCD9E8D57u;  // round multipliers
+  constexpr uint32_t kW0 = 0x9E3779B9u, kW1 = 0xBB67AE85u;  // key schedule
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)kM0 * c[0], p1 = (uint64_t)kM1 * c[2];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    c[1] = (uint32_t)p1;
+    c[3] = (uint32_t)p0;
+    c[0] = n0;
+    c[2] = n2;
+    k0 += kW0;
+    k1 += kW1;
+  }
+}
+
+// Gumbel noise of token `v` for a request with key `seed` at step `offset`.
+__device__ __forceinline__ float gumbel_noise(uint64_t seed, uint64_t offset, uint64_t v) {
+  uint32_t c[4] = {(uint32_t)v, (uint32_t)offset, (uint32_t)(offset >> 32), 0u};
+  philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+  const float u = ((float)(c[0] >> 8) + 0.5f) * 5.9604644775390625e-8f;  // 2^-24
+  return -logf(-logf(u));
+}
+
+// (running max m, sum of exp(y - m)) packed as two floats: hi word m, lo word s.
+// The empty pair is (-inf, 0).
+__device__ __forceinline__ unsigned long long pack_stats(float m, float s) {
+  return ((unsigned long long)__float_as_uint(m) << 32) | (unsigned long long)__float_as_uint(s);
+}
+__device__ __forceinline__ float stats_m(unsigned long long w) { return __uint_as_float((uint32_t)(w >> 32)); }
+__device__ __forceinline__ float stats_s(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ unsigned long long empty_stats() { return pack_stats(-INFINITY, 0.f); }
+
+// Merge of two (m, s) pairs: max of the maxima, sums rescaled to it.
+__device__ __forceinline__ void merge_stats(float& m, float& s, float m2, float s2) {
+  if (s2 == 0.f) return;
+  if (s == 0.f) {
+    m = m2;
+    s = s2;
+    return;
+  }
+  const float mm = fmaxf(m, m2);
+  s = s * __expf(m - mm) + s2 * __expf(m2 - mm);
+  m = mm;
+}
+
+// Lock-free merge of (m, s) into a packed shared- or global-memory word.
+__device__ __forceinline__ void merge_stats_atomic(unsigned long long* w, float m, float s) {
+  if (s == 0.f) return;
+  unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(w), assumed;
+  do {
+    assumed = old;
+    float mo = stats_m(assumed), so = stats_s(assumed);
+    merge_stats(mo, so, m, s);
+    old = atomicCAS(w, assumed, pack_stats(mo, so));
+  } while (old != assumed);
+}
+
+// Per-lane running statistics of one request run (units arrive grouped by request).
+struct RunningStats {
+  int b = -1;
+  float m = -INFINITY, s = 0.f;
+  __device__ __forceinline__ void flush(unsigned long long* s_stats) {
+    if (b >= 0) merge_stats_atomic(&s_stats[b], m, s);
+    b = -1;
+    m = -INFINITY;
+    s = 0.f;
+  }
+  __device__ __forceinline__ void add(int req, float y, unsigned long long* s_stats) {
+    if (req != b) {
+      flush(s_stats);
+      b = req;
+    }
+    if (s == 0.f) {
+      m = y;
+      s = 1.f;
+    } else if (y > m) {
+      s = s * __expf(m - y) + 1.f;
+      m = y;
+    } else {
+      s += __expf(y - m);
+    }
+  }
+};
+
+}  // namespace gsp

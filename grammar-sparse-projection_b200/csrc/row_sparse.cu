@@ -43,6 +43,7 @@
 #include "gsp_common.cuh"
 #include "gsp_internal.h"
 #include "gsp_peer.cuh"
+#include "gsp_sampler.cuh"
 
 namespace gsp {
 namespace {
@@ -80,9 +81,39 @@ struct RunningTop {
   }
 };
 
-template <typename T>
+// Shared-memory state of the fused sampler (kSample kernels): per request the
+// running Gumbel-max key, the (max, sum) pair of the scaled logits, and the
+// generator key. The three arrays follow the top-1 keys in the CTA's keys
+// region ([4 * batch] 64-bit words).
+struct SampleSmem {
+  unsigned long long* keys;
+  unsigned long long* stats;
+  const uint64_t* seeds;
+};
+
+__device__ __forceinline__ SampleSmem sample_smem(unsigned long long* s_keys, int batch) {
+  return SampleSmem{s_keys + batch, s_keys + 2 * batch, reinterpret_cast<const uint64_t*>(s_keys + 3 * batch)};
+}
+
+// Initialises the CTA's sampler state (call before the first __syncthreads).
+__device__ __forceinline__ void sample_smem_init(const RowSparseParams& p, unsigned long long* s_keys) {
+  for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
+    s_keys[p.batch + b] = 0ull;
+    s_keys[2 * p.batch + b] = empty_stats();
+    s_keys[3 * p.batch + b] = p.seeds[b];
+  }
+}
+
+// Running per-lane sampler state of one request run.
+struct RunningSample {
+  RunningTop key;
+  RunningStats stats;
+};
+
+template <typename T, bool kSample>
 __device__ __forceinline__ void emit_unit(const RowSparseParams& p, int b, int v, uint64_t rank, float acc,
-                                          bool want_top, RunningTop& top, unsigned long long* s_keys) {
+                                          bool want_top, RunningTop& top, unsigned long long* s_keys,
+                                          RunningSample& rs, const SampleSmem& ss, float noise) {
   const uint16_t bits = DTypeTraits<T>::round_bits(acc);
   if (p.logits) static_cast<uint16_t*>(p.logits)[(int64_t)b * p.logits_stride + v] = bits;
   if (p.compact && rank < (uint64_t)p.capacity) {
@@ -91,6 +122,49 @@ __device__ __forceinline__ void emit_unit(const RowSparseParams& p, int b, int v
   }
   if (want_top)
     top.add(b, top1_key(DTypeTraits<T>::bits_to_float(bits), (uint64_t)(p.vocab_offset + v)), s_keys);
+  if constexpr (kSample) {
+    const float y = DTypeTraits<T>::bits_to_float(bits) * p.inv_temp;
+    rs.stats.add(b, y, ss.stats);
+    rs.key.add(b, top1_key(y + noise, (uint64_t)(p.vocab_offset + v)), ss.keys);
+  }
+}
+
+// Noise of unit (b, v) for the lane that will emit it.
+template <bool kSample>
+__device__ __forceinline__ float unit_noise(const RowSparseParams& p, const SampleSmem& ss, int b, int v) {
+  if constexpr (kSample) return gumbel_noise(ss.seeds[b], p.offset, (uint64_t)(p.vocab_offset + v));
+  return 0.f;
+}
+
+// Every CTA: publishes its sampler state (sample keys by atomicMax, its (max,
+// sum) partials into its own row of the workspace). Followed by the ticket.
+__device__ __forceinline__ bool sample_publish(const RowSparseParams& p, const SampleSmem& ss) {
+  bool did = false;
+  for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
+    const unsigned long long k = ss.keys[b];
+    if (k != 0ull) atomicMax(p.sample_keys + b, k);
+    p.stat_partials[(size_t)blockIdx.x * p.batch + b] = ss.stats[b];
+    did = true;
+  }
+  return did;
+}
+
+// Last CTA: sampled ids and log-sum-exp per request; re-zeroes the sampler's
+// workspace (keys and every CTA's partials).
+__device__ __forceinline__ void sample_finish(const RowSparseParams& p) {
+  const int G = gridDim.x;
+  for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
+    const unsigned long long k = atomicExch(p.sample_keys + b, 0ull);
+    p.sample_index[b] = key_index(k);
+    float m = -INFINITY, sum = 0.f;
+    for (int c = 0; c < G; ++c) {
+      unsigned long long* w = p.stat_partials + (size_t)c * p.batch + b;
+      const unsigned long long x = __ldcg(w);
+      merge_stats(m, sum, stats_m(x), stats_s(x));
+      *w = 0ull;
+    }
+    if (p.sample_lse) p.sample_lse[b] = sum > 0.f ? m + logf(sum) : -INFINITY;
+  }
 }
 
 // Last CTA: takes the merged keys out of the workspace (re-zeroing it), merges
@@ -113,17 +187,22 @@ __device__ __forceinline__ void decode_top1(const RowSparseParams& p, unsigned l
 // Cross-CTA top-1 merge: each CTA folds its shared-memory keys into the
 // workspace with atomicMax; the CTA that draws the last ticket decodes them and
 // re-zeroes keys and ticket for the next call. Nobody waits on anybody.
-__device__ __forceinline__ void finalize_top1(const RowSparseParams& p, unsigned long long* s_keys, int* s_flag) {
+template <bool kSample>
+__device__ __forceinline__ void finalize_top1(const RowSparseParams& p, unsigned long long* s_keys, int* s_flag,
+                                              bool want_top) {
   const int tid = threadIdx.x;
   __syncthreads();
   bool did = false;
-  for (int b = tid; b < p.batch; b += blockDim.x) {
-    const unsigned long long k = s_keys[b];
-    if (k != 0ull) {
-      atomicMax(p.keys + b, k);
-      did = true;
+  if (want_top) {
+    for (int b = tid; b < p.batch; b += blockDim.x) {
+      const unsigned long long k = s_keys[b];
+      if (k != 0ull) {
+        atomicMax(p.keys + b, k);
+        did = true;
+      }
     }
   }
+  if constexpr (kSample) did |= sample_publish(p, sample_smem(s_keys, p.batch));
   if (did) __threadfence();  // only the threads that published keys need the fence
   __syncthreads();
   if (tid == 0) {
@@ -133,7 +212,8 @@ __device__ __forceinline__ void finalize_top1(const RowSparseParams& p, unsigned
   __syncthreads();
   if (*s_flag) {
     __threadfence();
-    decode_top1(p, s_keys, reinterpret_cast<uint32_t*>(s_flag + 1));
+    if (want_top) decode_top1(p, s_keys, reinterpret_cast<uint32_t*>(s_flag + 1));
+    if constexpr (kSample) sample_finish(p);
     if (tid == 0) atomicExch(p.ticket, 0u);
   }
 }
@@ -172,13 +252,15 @@ __device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w
 
 // Streams units s_list[0, n) (two rows per warp in flight) and emits them.
 // With kHSmem, s_h holds the hidden rows of requests b0, b0 + 1, ... .
-template <typename T, bool kHSmem>
+template <typename T, bool kHSmem, bool kSample>
 __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint32_t* s_list, int n, uint64_t rbase,
                                             uint32_t code_stride, const uint16_t* s_h, int b0, bool want_top,
                                             unsigned long long* s_keys) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int H = p.hidden_dim, nvec = H / 8;
   RunningTop top;
+  RunningSample rs;
+  const SampleSmem ss = kSample ? sample_smem(s_keys, p.batch) : SampleSmem{nullptr, nullptr, nullptr};
   for (int i = warp; i < n; i += 2 * kWarps) {
     const int j = i + kWarps;
     const bool has2 = j < n;
@@ -194,6 +276,7 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
                              : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) +
                                                               (int64_t)bb * p.hidden_stride);
     float acc_a = 0.f, acc_b = 0.f;
+    float noise = 0.f;
     for (int base = 0; base < nvec; base += 32 * kUnroll) {
       uint4 ra[kUnroll], rb[kUnroll];
 #pragma unroll
@@ -202,6 +285,8 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
         ra[u] = e < nvec ? ld_stream_v4(wa + e * 8) : make_uint4(0, 0, 0, 0);
         rb[u] = (has2 && e < nvec) ? ld_stream_v4(wb + e * 8) : make_uint4(0, 0, 0, 0);
       }
+      // sampler noise of the two units, while the rows are in flight
+      if (kSample && base == 0 && lane < 2) noise = unit_noise<kSample>(p, ss, lane ? bb : ba, lane ? vb : va);
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const int e = base + u * 32 + lane;
@@ -216,20 +301,29 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
       acc_a += __shfl_xor_sync(FULL_MASK, acc_a, o);
       acc_b += __shfl_xor_sync(FULL_MASK, acc_b, o);
     }
-    if (lane == 0) emit_unit<T>(p, ba, va, rbase + (uint64_t)i, acc_a, want_top, top, s_keys);
-    if (lane == 1 && has2) emit_unit<T>(p, bb, vb, rbase + (uint64_t)j, acc_b, want_top, top, s_keys);
+    if (lane == 0) emit_unit<T, kSample>(p, ba, va, rbase + (uint64_t)i, acc_a, want_top, top, s_keys, rs, ss, noise);
+    if (lane == 1 && has2)
+      emit_unit<T, kSample>(p, bb, vb, rbase + (uint64_t)j, acc_b, want_top, top, s_keys, rs, ss, noise);
   }
-  if (lane < 2) top.flush(s_keys);
+  if (lane < 2) {
+    top.flush(s_keys);
+    if constexpr (kSample) {
+      rs.key.flush(ss.keys);
+      rs.stats.flush(ss.stats);
+    }
+  }
 }
 
 // Scalar fallback of stream_rows (any alignment, any H).
-template <typename T>
+template <typename T, bool kSample>
 __device__ __forceinline__ void stream_rows_scalar(const RowSparseParams& p, const uint32_t* s_list, int n,
                                                    uint64_t rbase, uint32_t code_stride, bool want_top,
                                                    unsigned long long* s_keys) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int H = p.hidden_dim;
   RunningTop top;
+  RunningSample rs;
+  const SampleSmem ss = kSample ? sample_smem(s_keys, p.batch) : SampleSmem{nullptr, nullptr, nullptr};
   for (int i = warp; i < n; i += kWarps) {
     const uint32_t c = s_list[i];
     const int b = (int)(c / code_stride), v = (int)(c - (uint32_t)b * code_stride);
@@ -240,9 +334,16 @@ __device__ __forceinline__ void stream_rows_scalar(const RowSparseParams& p, con
       acc = fmaf(DTypeTraits<T>::bits_to_float(__ldg(w + k)), DTypeTraits<T>::bits_to_float(__ldg(h + k)), acc);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL_MASK, acc, o);
-    if (lane == 0) emit_unit<T>(p, b, v, rbase + (uint64_t)i, acc, want_top, top, s_keys);
+    if (lane == 0) emit_unit<T, kSample>(p, b, v, rbase + (uint64_t)i, acc, want_top, top, s_keys, rs, ss,
+                                         unit_noise<kSample>(p, ss, b, v));
   }
-  if (lane == 0) top.flush(s_keys);
+  if (lane == 0) {
+    top.flush(s_keys);
+    if constexpr (kSample) {
+      rs.key.flush(ss.keys);
+      rs.stats.flush(ss.stats);
+    }
+  }
 }
 
 // Block-wide exclusive scan of one value per thread (kThreads threads);
@@ -285,7 +386,7 @@ __host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim,
   l.list = off;
   off += 4 * (size_t)kListCap;
   l.keys = align_up(off, 16);
-  off = l.keys + 8 * (size_t)batch;
+  off = l.keys + 32 * (size_t)batch;  // top-1 keys + the sampler's three arrays
   l.warp = align_up(off, 16);
   off = l.warp + 4 * 32;
   l.misc = align_up(off, 16);
@@ -310,7 +411,7 @@ __device__ __forceinline__ int staged_index(int f) {
 
 // kV 16-byte mask vectors (4 * kV words) per thread: the whole flat
 // (request, word) mask lives in the CTA's registers, kThreads * 4 * kV words.
-template <typename T, int kV>
+template <typename T, int kV, bool kSample>
 __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const RowSparseParams p) {
   constexpr int kWpt = 4 * kV;  // words per thread
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -377,6 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
         reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
   }
   for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
+  if constexpr (kSample) sample_smem_init(p, s_keys);
 
   uint32_t cnt = 0;
 #pragma unroll
@@ -474,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
     }
     __syncthreads();
     // ---- 5. stream the rows ------------------------------------------------
-    stream_rows<T, true>(p, s_list, n, rbase, code_stride, s_h, 0, want_top, s_keys);
+    stream_rows<T, true, kSample>(p, s_list, n, rbase, code_stride, s_h, 0, want_top, s_keys);
     __syncthreads();
   }
 
@@ -482,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   if (p.logits && has_mask)
     fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_words[staged_index<kWpt>((int)f)]; });
   // ---- 7. top-1 ------------------------------------------------------------
-  if (want_top) finalize_top1(p, s_keys, s_misc);
+  if (want_top || kSample) finalize_top1<kSample>(p, s_keys, s_misc, want_top);
 }
 
 // ===========================================================================
@@ -496,13 +598,13 @@ __host__ __device__ inline DirectLayout direct_layout(int batch) {
   DirectLayout l;
   l.list = 0;
   l.keys = align_up(l.list + sizeof(uint32_t) * kListCap, 16);
-  l.warp = align_up(l.keys + sizeof(unsigned long long) * batch, 16);
+  l.warp = align_up(l.keys + 4 * sizeof(unsigned long long) * batch, 16);  // + sampler arrays
   l.misc = align_up(l.warp + sizeof(uint32_t) * 32, 16);
   l.total = align_up(l.misc + 16, 128);
   return l;
 }
 
-template <typename T, bool kVec>
+template <typename T, bool kVec, bool kSample>
 __global__ void __launch_bounds__(kThreads, 1) row_sparse_direct_kernel(const RowSparseParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const DirectLayout L = direct_layout(p.batch);
@@ -516,6 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_direct_kernel(const Ro
   const int B = p.batch, V = p.vocab, nw = p.nw;
   const bool want_top = (p.top_value != nullptr) | (p.top_index != nullptr) | (p.top_key != nullptr);
   for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
+  if constexpr (kSample) sample_smem_init(p, s_keys);
 
   // per-thread contiguous segments of the flat (request, word) space
   const int64_t F = p.mask ? (int64_t)B * nw : 0;
@@ -604,9 +707,9 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_direct_kernel(const Ro
     }
     __syncthreads();
     if (kVec)
-      stream_rows<T, false>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
+      stream_rows<T, false, kSample>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
     else
-      stream_rows_scalar<T>(p, s_list, n, rbase, code_stride, want_top, s_keys);
+      stream_rows_scalar<T, kSample>(p, s_list, n, rbase, code_stride, want_top, s_keys);
     __syncthreads();
   }
 
@@ -616,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_direct_kernel(const Ro
       return __ldg(p.mask + (int64_t)b * p.mask_stride + w);
     });
   }
-  if (want_top) finalize_top1(p, s_keys, s_misc);
+  if (want_top || kSample) finalize_top1<kSample>(p, s_keys, s_misc, want_top);
 }
 
 // ===========================================================================
@@ -646,7 +749,7 @@ __host__ __device__ inline CoopLayout coop_layout(int batch) {
   l.list = off;
   off += 4 * (size_t)kListCap;
   l.keys = align_up(off, 16);
-  off = l.keys + 8 * (size_t)batch;
+  off = l.keys + 32 * (size_t)batch;  // top-1 keys + the sampler's three arrays
   l.warp = align_up(off, 16);
   off = l.warp + 4 * 32;
   l.misc = align_up(off, 16);
@@ -720,7 +823,7 @@ __device__ __forceinline__ uint32_t scan_chunk(const RowSparseParams& p, int c0,
 // checked first (request < B, row < V): a round holding any other code (which
 // only a workspace left dirty by an earlier failed launch can produce) sets
 // the error word and is skipped, so no address is ever formed from it.
-template <typename T>
+template <typename T, bool kSample>
 __device__ __forceinline__ void coop_stream_round(const RowSparseParams& p, const uint32_t* s_list, int n,
                                                   uint32_t rbase, uint32_t code_stride, uint16_t* s_h, int& h_lo,
                                                   int& h_hi, bool want_top, unsigned long long* s_keys) {
@@ -748,9 +851,9 @@ __device__ __forceinline__ void coop_stream_round(const RowSparseParams& p, cons
       h_hi = rb1 + 1;
       __syncthreads();
     }
-    stream_rows<T, true>(p, s_list, n, rbase, code_stride, s_h, h_lo, want_top, s_keys);
+    stream_rows<T, true, kSample>(p, s_list, n, rbase, code_stride, s_h, h_lo, want_top, s_keys);
   } else {
-    stream_rows<T, false>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
+    stream_rows<T, false, kSample>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
   }
 }
 
@@ -769,6 +872,7 @@ __device__ __forceinline__ uint32_t wait_flag(const uint32_t* flag) {
 // End of the cooperative kernel: top-1 keys folded into the workspace, one
 // ticket per CTA; the last CTA decodes the keys and re-zeroes slice counts,
 // flags and ticket (every CTA has passed both of its waits by then).
+template <bool kSample>
 __device__ __forceinline__ void coop_finish(const RowSparseParams& p, unsigned long long* s_keys, int* s_flag,
                                             bool want_top) {
   const int tid = threadIdx.x, G = gridDim.x;
@@ -783,6 +887,7 @@ __device__ __forceinline__ void coop_finish(const RowSparseParams& p, unsigned l
       }
     }
   }
+  if constexpr (kSample) did |= sample_publish(p, sample_smem(s_keys, p.batch));
   if (did) __threadfence();
   __syncthreads();
   if (tid == 0) *s_flag = (atomicAdd(p.ticket, 1u) == (unsigned)G - 1u);
@@ -790,6 +895,7 @@ __device__ __forceinline__ void coop_finish(const RowSparseParams& p, unsigned l
   if (*s_flag) {
     __threadfence();
     if (want_top) decode_top1(p, s_keys, reinterpret_cast<uint32_t*>(s_flag + 1));
+    if constexpr (kSample) sample_finish(p);
     for (int c = tid; c < G; c += blockDim.x) {
       p.slice_counts[c] = 0u;
       p.slice_ready[(size_t)c * kFlagStride] = 0u;
@@ -811,7 +917,7 @@ __device__ __forceinline__ void coop_finish(const RowSparseParams& p, unsigned l
 // the slices its rank range draws from and reads its units from the list.
 // No mask word is read twice and nothing waits on memory once rows stream.
 // Otherwise each CTA re-scans (from L2) the slices its rank range overlaps.
-template <typename T>
+template <typename T, bool kSample>
 __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowSparseParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const CoopLayout L = coop_layout(p.batch);
@@ -832,6 +938,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowS
   const int my_lo = slice_lo(cta), my_hi = slice_lo(cta + 1);
   const int max_slice = (F + G - 1) / G;  // every slice holds at most this many words
   for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
+  if constexpr (kSample) sample_smem_init(p, s_keys);
   if (tid == 0) s_misc[0] = 0;
 
   // ---- 1. popcount of this CTA's slice, published to the grid --------------
@@ -936,7 +1043,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowS
         p.unit_list[rbase + i] = 0u;
       }
       __syncthreads();
-      coop_stream_round<T>(p, s_list, n, rbase, code_stride, s_h, h_lo, h_hi, want_top, s_keys);
+      coop_stream_round<T, kSample>(p, s_list, n, rbase, code_stride, s_h, h_lo, h_hi, want_top, s_keys);
       __syncthreads();
     }
   } else {
@@ -975,7 +1082,8 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowS
         }
       }
       __syncthreads();
-      coop_stream_round<T>(p, s_list, (int)(rend - rbase), rbase, code_stride, s_h, h_lo, h_hi, want_top, s_keys);
+      coop_stream_round<T, kSample>(p, s_list, (int)(rend - rbase), rbase, code_stride, s_h, h_lo, h_hi, want_top,
+                                    s_keys);
       __syncthreads();
     }
     // ---- 4'. own slice: request offsets (compact output), -inf fill ---------
@@ -1003,13 +1111,13 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowS
   if (p.offsets != nullptr && cta == 0 && tid == 0) p.offsets[B] = (int64_t)total;
 
   // ---- 5. top-1, workspace reset ------------------------------------------
-  coop_finish(p, s_keys, s_misc + 2, want_top);
+  coop_finish<kSample>(p, s_keys, s_misc + 2, want_top);
 }
 
 // ===========================================================================
 // launch
 // ===========================================================================
-template <typename T>
+template <typename T, bool kSample>
 cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -1023,7 +1131,7 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
       F64 * 32 < (int64_t)1 << 32) {
     const CoopLayout L = coop_layout(p.batch);
     if (L.total <= kStagedSmemMax) {
-      auto k = row_sparse_coop_kernel<T>;
+      auto k = row_sparse_coop_kernel<T, kSample>;
       if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3((unsigned)min(grid, kMaxSlices));
@@ -1044,11 +1152,11 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
     const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * wpt);
     if (L.total <= kStagedSmemMax && F <= kThreads * 32) {
       if (wpt == 16) {
-        auto k = row_sparse_staged_kernel<T, 4>;
+        auto k = row_sparse_staged_kernel<T, 4, kSample>;
         if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
         k<<<grid, kThreads, L.total, stream>>>(p);
       } else {
-        auto k = row_sparse_staged_kernel<T, 8>;
+        auto k = row_sparse_staged_kernel<T, 8, kSample>;
         if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
         k<<<grid, kThreads, L.total, stream>>>(p);
       }
@@ -1057,11 +1165,11 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
   }
   const DirectLayout L = direct_layout(p.batch);
   if (vec) {
-    auto k = row_sparse_direct_kernel<T, true>;
+    auto k = row_sparse_direct_kernel<T, true, kSample>;
     if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
     k<<<grid, kThreads, L.total, stream>>>(p);
   } else {
-    auto k = row_sparse_direct_kernel<T, false>;
+    auto k = row_sparse_direct_kernel<T, false, kSample>;
     if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
     k<<<grid, kThreads, L.total, stream>>>(p);
   }
@@ -1071,8 +1179,9 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_row_sparse(const RowSparseParams& p, int dtype, cudaStream_t stream) {
-  if (dtype == 1) return launch_typed<__nv_bfloat16>(p, stream);
-  return launch_typed<__half>(p, stream);
+  const bool sample = p.sample_index != nullptr;
+  if (dtype == 1) return sample ? launch_typed<__nv_bfloat16, true>(p, stream) : launch_typed<__nv_bfloat16, false>(p, stream);
+  return sample ? launch_typed<__half, true>(p, stream) : launch_typed<__half, false>(p, stream);
 }
 
 }  // namespace gsp

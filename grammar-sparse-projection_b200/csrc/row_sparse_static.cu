@@ -30,9 +30,9 @@ namespace {
 // Scratch for batch <= GSP_STATIC_MAX_BATCH and vocab <= GSP_STATIC_MAX_VOCAB:
 // the same layout as the caller-provided workspace (ticket, error word, one
 // 64-bit top-1 key per request, tile lists, and the multi-request kernel's
-// slice counts, flags and 1M-entry unit list), sized for those maxima
-// (4,304,384 bytes).
-constexpr size_t kStaticScratchBytes = workspace_bytes_for(GSP_STATIC_MAX_BATCH, GSP_STATIC_MAX_VOCAB);
+// slice counts, flags and 1M-entry unit list; not the sampler's part), sized
+// for those maxima (4,304,384 bytes).
+constexpr size_t kStaticScratchBytes = row_sparse_workspace_bytes_for(GSP_STATIC_MAX_BATCH, GSP_STATIC_MAX_VOCAB);
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 

@@ -59,6 +59,8 @@ SIGNATURES = {
     "gsp_top1_from_keys": ([_vp, _i32, _vp, _vp, _vp], _i32),
     "gsp_row_sparse_logits_static": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
                                       _vp, _i64, _vp, _vp, _vp, _vp], _i32),
+    "gsp_row_sparse_sample": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _vp, _i64,
+                               ctypes.c_float, _vp, ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, _sz, _vp], _i32),
     "gsp_peer_exchange_bytes": ([_i32, _i32], _sz),
     "gsp_peer_exchange_alloc": ([_sz, ctypes.POINTER(_vp), _vp], _i32),
     "gsp_peer_exchange_open": ([_vp, ctypes.POINTER(_vp)], _i32),
@@ -285,6 +287,28 @@ def vocab_parallel(route: str, hidden, weight, mask, peers: list[int], rank: int
         _ptr(top_value), _ptr(top_index), _ptr(top_key),
         _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, total_vocab, _stream(hidden.device))
     _check(status, "gsp_vocab_parallel_logits")
+
+
+def row_sparse_sample(hidden, weight, mask, seeds, offset: int, temperature: float, sample_index,
+                      sample_logsumexp=None, logits=None, top_value=None, top_index=None,
+                      vocab_offset: int = 0) -> None:
+    """Fused sampler (gsp_row_sparse_sample): Gumbel-max draw per request from
+    softmax(logits / temperature) over the legal tokens, keyed by
+    seeds[b] (uint64 stored as int64) and the step counter `offset`."""
+    _require_cuda(hidden, weight, mask, seeds, sample_index, sample_logsumexp, logits)
+    lib = load()
+    batch, hdim = hidden.shape
+    vocab = weight.shape[0]
+    ws = workspace(hidden.device, batch, vocab)
+    status = lib.gsp_row_sparse_sample(
+        _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+        _ptr(mask), 0 if mask is None else mask.stride(0),
+        batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+        _ptr(logits), 0 if logits is None else logits.stride(0),
+        float(temperature), _ptr(seeds), int(offset) & 0xFFFFFFFFFFFFFFFF,
+        _ptr(sample_index), _ptr(sample_logsumexp), _ptr(top_value), _ptr(top_index),
+        _ptr(ws), ws.numel(), _stream(hidden.device))
+    _check(status, "gsp_row_sparse_sample")
 
 
 def row_sparse_compact(hidden, weight, mask, compact_logits, compact_ids, offsets,

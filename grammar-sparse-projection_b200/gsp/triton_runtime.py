@@ -24,6 +24,8 @@ Differences from the reference, all deliberate:
 """
 from __future__ import annotations
 
+from typing import NamedTuple
+
 import torch
 
 from . import _native
@@ -38,6 +40,8 @@ __all__ = [
     "full_word_fraction_cpu",
     "adaptive_grammar_logits",
     "grammar_logits_with_top1",
+    "grammar_sample",
+    "SampleResult",
     "bitmask_compact_logits",
     "mask_stats",
     "choose_route",
@@ -369,6 +373,46 @@ def grammar_logits_with_top1(
     top_index = torch.empty(batch, device=dev, dtype=torch.int64)
     fn(hidden_2d, weight, mask_2d, logits=logits, top_value=top_value, top_index=top_index)
     return logits, top_value, top_index
+
+
+class SampleResult(NamedTuple):
+    token_ids: torch.Tensor   # int64 [B]: sampled token per request
+    logsumexp: torch.Tensor   # float32 [B]: log sum exp(legal logits / T)
+    top_value: torch.Tensor   # float32 [B]: greedy top-1 logit
+    top_index: torch.Tensor   # int64 [B]: greedy top-1 token
+    logits: torch.Tensor | None
+
+
+def grammar_sample(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torch.Tensor, *,
+                   seeds: torch.Tensor, step: int, temperature: float = 1.0,
+                   return_logits: bool = False) -> SampleResult:
+    """Grammar-conditioned fused sampler: one launch projects the legal rows
+    and draws each request's next token from softmax(logits / temperature)
+    over its legal tokens, without writing vocabulary-shaped logits unless
+    asked (the "fused grammar-aware sampler" the reference's paper leaves
+    open, paper/draft.md section 6.4).
+
+    The draw is Gumbel-max over the dtype-rounded legal logits with Philox
+    noise keyed by seeds[b] (CUDA int64 [B], read as uint64) and counted by
+    (token id, step): the same (seeds, step) reproduce the same tokens, on any
+    route decomposition; use a new step per decode step. logsumexp gives the
+    sampled token's log-probability, logit / temperature - logsumexp. The
+    greedy top-1 comes with it. Shapes are [B, ...] always.
+    """
+    hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
+    if seeds.device.type != "cuda" or seeds.dtype != torch.int64 or seeds.numel() != batch:
+        raise ValueError("seeds must be a CUDA int64 tensor with one seed per request")
+    if not (temperature > 0.0) or temperature == float("inf"):
+        raise ValueError("temperature must be positive and finite")
+    dev = hidden.device
+    logits = torch.empty((batch, vocab), device=dev, dtype=hidden.dtype) if return_logits else None
+    token_ids = torch.empty(batch, device=dev, dtype=torch.int64)
+    lse = torch.empty(batch, device=dev, dtype=torch.float32)
+    top_value = torch.empty(batch, device=dev, dtype=torch.float32)
+    top_index = torch.empty(batch, device=dev, dtype=torch.int64)
+    _native.row_sparse_sample(hidden_2d, weight, mask_2d, seeds.contiguous(), step, temperature, token_ids,
+                              sample_logsumexp=lse, logits=logits, top_value=top_value, top_index=top_index)
+    return SampleResult(token_ids, lse, top_value, top_index, logits)
 
 
 def bitmask_compact_logits(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torch.Tensor,

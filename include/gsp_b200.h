@@ -186,6 +186,41 @@ int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
                            int64_t* top_index, void* stream);
 
 /*
+ * Fused grammar-conditioned sampler (row-sparse path): the projection of
+ * gsp_row_sparse_logits reduced on chip to sampling statistics; logits are
+ * optional (NULL: no vocabulary-shaped output is written at all). Per request
+ * b, with x_v the legal logits rounded to `dtype`:
+ *   sample_index[b]     = argmax over legal v of x_v / T + g_v, ties to the
+ *                         lowest id (0 if no token is legal), where
+ *                         g_v = -log(-log(u_v)) and u_v =
+ *                         ((Philox4x32-10(counter {v, offset lo, offset hi, 0},
+ *                         key {seeds[b] lo, seeds[b] hi}).word0 >> 8) + 0.5) / 2^24,
+ *                         all in fp32: an exact draw from softmax(x / T) over the
+ *                         legal tokens (Gumbel-max), reproducible from
+ *                         (seeds[b], offset, v);
+ *   sample_logsumexp[b] = log sum over legal v of exp(x_v / T) (optional;
+ *                         -inf if no token is legal), so the sampled token's
+ *                         log-probability is x / T - sample_logsumexp; its
+ *                         partial sums merge in arrival order, so repeated calls
+ *                         agree to fp32 rounding (the sampled ids bit for bit);
+ *   top_value / top_index: the greedy top-1, as in gsp_row_sparse_logits.
+ * temperature > 0 and finite; seeds is a device array [batch]; offset is the
+ * caller's step counter (use a new one per step). The workspace must hold
+ * gsp_workspace_bytes(batch, vocab) bytes. No counterpart in the reference
+ * (its paper, paper/draft.md section 6.4, names this as the next step).
+ */
+int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride,
+                              const void* weight, int64_t weight_row_stride,
+                              const int32_t* bitmask, int64_t bitmask_row_stride,
+                              int32_t batch, int32_t vocab, int32_t hidden_dim,
+                              int32_t dtype, int64_t vocab_offset, void* logits,
+                              int64_t logits_row_stride, float temperature,
+                              const uint64_t* seeds, uint64_t offset,
+                              int64_t* sample_index, float* sample_logsumexp,
+                              float* top_value, int64_t* top_index, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/*
  * Vocabulary-parallel head: top-1 merged across ranks inside the kernel.
  *
  * One process per GPU on one node, up to GSP_MAX_PEERS ranks; rank r holds a

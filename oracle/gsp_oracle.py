@@ -302,6 +302,67 @@ clustered_legal_ids = _workloads.clustered_legal_ids
 make_batch_mask = _workloads.make_batch_mask
 
 
+# ---------------------------------------------------------------------------
+# fused sampler (no counterpart in the reference; its paper names it as the
+# next step, paper/draft.md section 6.4). Restates the contract the kernels
+# implement, independently, for the checker:
+#   u = ((Philox4x32-10({v, offset lo, offset hi, 0}, {seed lo, seed hi}).word0 >> 8) + 0.5) / 2^24
+#   g = -log(-log(u)); s = x * (1/T) + g (fp32); sample = argmax s (lowest id on ties)
+#   lse = log sum exp(x / T)
+# ---------------------------------------------------------------------------
+_PHILOX_M0, _PHILOX_M1 = 0xD2511F53, 0xCD9E8D57  # Salmon et al., SC 2011
+_PHILOX_W0, _PHILOX_W1 = 0x9E3779B9, 0xBB67AE85
+_U32 = np.uint64(0xFFFFFFFF)
+
+
+def philox4x32_10(counters, key0: int, key1: int) -> np.ndarray:
+    """Philox4x32-10 of each row of counters [N, 4] (uint32) under key
+    (key0, key1): ten rounds, key bumped by the Weyl constants between them."""
+    c = np.asarray(counters, dtype=np.uint64).reshape(-1, 4)
+    c0, c1, c2, c3 = c[:, 0].copy(), c[:, 1].copy(), c[:, 2].copy(), c[:, 3].copy()
+    k0, k1 = np.uint64(key0 & 0xFFFFFFFF), np.uint64(key1 & 0xFFFFFFFF)
+    for _ in range(10):
+        p0 = c0 * np.uint64(_PHILOX_M0)
+        p1 = c2 * np.uint64(_PHILOX_M1)
+        c0, c1, c2, c3 = (p1 >> np.uint64(32)) ^ c1 ^ k0, p1 & _U32, (p0 >> np.uint64(32)) ^ c3 ^ k1, p0 & _U32
+        k0 = (k0 + np.uint64(_PHILOX_W0)) & _U32
+        k1 = (k1 + np.uint64(_PHILOX_W1)) & _U32
+    return np.stack([c0, c1, c2, c3], axis=1).astype(np.uint32)
+
+
+def gumbel_noise(seed: int, offset: int, ids) -> np.ndarray:
+    """fp32 Gumbel noise of global token ids for one request's seed and step."""
+    ids = np.asarray(ids, dtype=np.uint64)
+    ctr = np.stack([ids & _U32, np.full_like(ids, offset & 0xFFFFFFFF), np.full_like(ids, (offset >> 32) & 0xFFFFFFFF),
+                    np.zeros_like(ids)], axis=1)
+    word0 = philox4x32_10(ctr, seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)[:, 0]
+    u = ((word0 >> np.uint32(8)).astype(np.float32) + np.float32(0.5)) * np.float32(2.0 ** -24)
+    return (-np.log(-np.log(u))).astype(np.float32)
+
+
+def sample_reference(hidden, weight, mask, dtype: torch.dtype, temperature: float, seeds, offset: int,
+                     vocab_offset: int = 0):
+    """Per request: (sampled id or 0, logsumexp in float64, perturbed scores
+    of the legal tokens as float32, the legal ids). x is the exact logit
+    rounded to `dtype` (what the materialised logits hold)."""
+    exact = masked_logits_exact(hidden, weight, mask)
+    rounded = exact.to(dtype).float().numpy()
+    inv_t = np.float32(1.0) / np.float32(temperature)
+    out = []
+    for b in range(rounded.shape[0]):
+        legal = np.flatnonzero(np.isfinite(rounded[b]))
+        if legal.size == 0:
+            out.append((0, float("-inf"), np.zeros(0, np.float32), legal))
+            continue
+        y = rounded[b, legal].astype(np.float32) * inv_t
+        scores = y + gumbel_noise(int(seeds[b]), offset, legal + vocab_offset)
+        pick = int(legal[int(np.argmax(scores))]) + vocab_offset
+        y64 = y.astype(np.float64)
+        lse = float(y64.max() + np.log(np.exp(y64 - y64.max()).sum()))
+        out.append((pick, lse, scores, legal + vocab_offset))
+    return out
+
+
 def cpu_row_sparse_step(hidden: np.ndarray, weight: np.ndarray, mask: np.ndarray, vocab: int) -> tuple[np.ndarray, np.ndarray]:
     """One CPU step of the reference's row-sparse semantics for the timed CPU
     baseline: decode the bitmask, gather legal rows (gsp/runtime.py:50-51),

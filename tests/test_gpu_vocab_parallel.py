@@ -143,3 +143,39 @@ def test_vocab_parallel_peer_exchange_two_gpus(tmp_path):
     for r in range(2):
         text = open(f"{result}.{r}").read()
         assert text == "", f"rank {r}: {text}"
+
+
+def test_exchange_wait_runs_out_on_one_gpu(cuda_device):
+    """Failure detection without a fault: a two-rank exchange whose second
+    rank never runs (its buffer is a second local one that nothing writes).
+    The last CTA's bounded wait gives up, the call returns, the workspace
+    error word reads 3, and after re-zeroing the workspace the device keeps
+    working (a plain call on the same stream succeeds)."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "..", "grammar-sparse-projection_b200"))
+    from gsp import _native
+    dev = cuda_device
+    rng = np.random.default_rng(3)
+    vocab, hidden = 4096, 64
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)).half().to(dev)
+    h = torch.from_numpy(rng.standard_normal((1, hidden), dtype=np.float32)).half().to(dev)
+    mask = torch.full((1, vocab // 32), -1, dtype=torch.int32, device=dev)
+    own, _ = _native.peer_exchange_alloc(2, 1)
+    silent, _ = _native.peer_exchange_alloc(2, 1)
+    try:
+        _native.reset_workspace(dev)
+        tv = torch.empty(1, device=dev)
+        ti = torch.empty(1, device=dev, dtype=torch.int64)
+        _native.vocab_parallel("row-sparse", h, w[: vocab // 2], mask[:, : vocab // 64], [own, silent], 0, 1,
+                               vocab, top_value=tv, top_index=ti)
+        torch.cuda.synchronize()
+        assert _native.workspace_error(dev) == 3
+        _native.reset_workspace(dev)
+        logits = torch.empty(1, vocab, device=dev, dtype=torch.float16)
+        _native.row_sparse(h, w, mask, logits=logits, top_value=tv, top_index=ti)
+        torch.cuda.synchronize()
+        assert _native.workspace_error(dev) == 0
+        assert ti.item() == logits.argmax(-1).item()
+    finally:
+        _native.peer_exchange_free(own)
+        _native.peer_exchange_free(silent)

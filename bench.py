@@ -66,7 +66,7 @@ def parse_args():
     ap.add_argument("--sweep-steps", type=int, default=100)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-vp", action="store_true", help="skip the vocabulary-parallel head section")
-    ap.add_argument("--only", choices=("batched", "mixed", "vp"), default=None,
+    ap.add_argument("--only", choices=("batched", "mixed", "vp", "sampler"), default=None,
                     help="run one extra section alone (small; for profiling)")
     ap.add_argument("--batch", type=int, default=32, help="batch of --only batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -261,6 +261,10 @@ def main():
             res = batched_section(dev, weights, peak, steps=max(args.steps, 1), batches=(args.batch,))
         elif args.only == "vp":
             res = vocab_parallel_section(dev, 1, 0, peak, steps=max(args.steps, 1), batches=(args.batch,))
+        elif args.only == "sampler":
+            g = torch.Generator(device=dev).manual_seed(1234)
+            weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(4)]
+            res = sampler_section(dev, weights, steps=max(args.steps, 1), batches=(1, args.batch))
         else:
             res = mixed_section(dev, peak, steps=max(args.steps, 1))
         print(json.dumps({"only": args.only, "result": res}), flush=True)
@@ -437,6 +441,7 @@ def main():
     sweep = None
     batched = None
     mixed = None
+    sampler = None
     same_gpu_dense = None
     cpu_base = None
     if world == 1 and not args.no_sweep:
@@ -457,6 +462,7 @@ def main():
         same_gpu_dense = time_dense_baseline(dev, weight, hidden, masks, args)
         batched = batched_section(dev, weights[:8], peak)
         mixed = mixed_section(dev, peak)
+        sampler = sampler_section(dev, weights[:8])
     vp_head = None if args.no_vp else vocab_parallel_section(dev, world, rank, peak)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         w_cpu = weight.cpu().numpy()
@@ -489,6 +495,7 @@ def main():
             "mixed": mixed,
             "same_gpu_dense_mask": same_gpu_dense,
             "vocab_parallel_head": vp_head,
+            "sampler": sampler,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -603,6 +610,53 @@ def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
             "tokens_per_s": batch / (times[best] * 1e-6),
             "best_route": best, "b200_policy_route": choice,
         })
+    return out
+
+
+def sampler_section(dev, weights, steps=50, batches=(1, 32)):
+    """Fused grammar-conditioned sampler against the unfused pipeline at the
+    headline shape (V=248,320, H=2,048 fp16; batch 1: 1% uniform legal tokens,
+    batch 32: 0.5% in <= 16 runs per request), graph-timed over the weight
+    copies: `fused` = gsp_row_sparse_sample, no logits written; `greedy` = the
+    row-sparse kernel with full logits and fused top-1 (the headline step);
+    `unfused` = the same kernel writing full logits, then Gumbel-max sampling
+    over them in torch (rand, two logs, scale, add, argmax)."""
+    from gsp import _native, workloads as wl
+    out = []
+    temperature = 0.8
+    for batch in batches:
+        rng = np.random.default_rng(700 + batch)
+        if batch == 1:
+            masks_np = [wl.make_batch_mask(rng, 1, VOCAB, [VOCAB // 100]) for _ in range(8)]
+        else:
+            masks_np = [wl.make_batch_mask(rng, batch, VOCAB, [1242] * batch, clustered=True, max_runs=16)
+                        for _ in range(8)]
+        masks = [torch.from_numpy(m).to(dev) for m in masks_np]
+        hidden = torch.randn(batch, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).half()
+        seeds = torch.arange(batch, dtype=torch.int64, device=dev) * 7919 + 17
+        logits = torch.empty(batch, VOCAB, device=dev, dtype=torch.float16)
+        tv = torch.empty(batch, device=dev, dtype=torch.float32)
+        ti = torch.empty(batch, device=dev, dtype=torch.int64)
+        tok = torch.empty(batch, device=dev, dtype=torch.int64)
+        lse = torch.empty(batch, device=dev, dtype=torch.float32)
+
+        def fused(i):
+            _native.row_sparse_sample(hidden, weights[i % len(weights)], masks[i % 8], seeds, i, temperature, tok,
+                                      sample_logsumexp=lse, top_value=tv, top_index=ti)
+
+        def greedy(i):
+            _native.row_sparse(hidden, weights[i % len(weights)], masks[i % 8], logits=logits, top_value=tv,
+                               top_index=ti)
+
+        def unfused(i):
+            greedy(i)
+            u = torch.rand(batch, VOCAB, device=dev)
+            tok.copy_((logits.float() / temperature - torch.log(-torch.log(u))).argmax(-1))
+
+        times = {name: graph_time_us(dev, steps, fn) / steps
+                 for name, fn in (("fused", fused), ("greedy", greedy), ("unfused", unfused))}
+        out.append({"batch": batch, "us_per_step": times,
+                    "speedup_fused_vs_unfused": times["unfused"] / times["fused"]})
     return out
 
 

@@ -77,7 +77,7 @@ struct RowSparseParams {
   uint64_t offset;                   // step counter
   float inv_temp;                    // 1 / temperature
   unsigned long long* sample_keys;   // workspace [batch]
-  unsigned long long* stat_partials; // workspace [kMaxSlices][batch]
+  unsigned long long* stat_partials; // workspace [batch][kMaxSlices]
 };
 
 // Parameters of the tensor-core block / dense projection.

@@ -75,43 +75,4 @@ __device__ __forceinline__ void merge_stats(float& m, float& s, float m2, float 
   m = mm;
 }
 
-// Lock-free merge of (m, s) into a packed shared- or global-memory word.
-__device__ __forceinline__ void merge_stats_atomic(unsigned long long* w, float m, float s) {
-  if (s == 0.f) return;
-  unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(w), assumed;
-  do {
-    assumed = old;
-    float mo = stats_m(assumed), so = stats_s(assumed);
-    merge_stats(mo, so, m, s);
-    old = atomicCAS(w, assumed, pack_stats(mo, so));
-  } while (old != assumed);
-}
-
-// Per-lane running statistics of one request run (units arrive grouped by request).
-struct RunningStats {
-  int b = -1;
-  float m = -INFINITY, s = 0.f;
-  __device__ __forceinline__ void flush(unsigned long long* s_stats) {
-    if (b >= 0) merge_stats_atomic(&s_stats[b], m, s);
-    b = -1;
-    m = -INFINITY;
-    s = 0.f;
-  }
-  __device__ __forceinline__ void add(int req, float y, unsigned long long* s_stats) {
-    if (req != b) {
-      flush(s_stats);
-      b = req;
-    }
-    if (s == 0.f) {
-      m = y;
-      s = 1.f;
-    } else if (y > m) {
-      s = s * __expf(m - y) + 1.f;
-      m = y;
-    } else {
-      s += __expf(y - m);
-    }
-  }
-};
-
 }  // namespace gsp

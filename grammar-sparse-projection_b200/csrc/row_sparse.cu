@@ -86,34 +86,100 @@ struct RunningTop {
 // generator key. The three arrays follow the top-1 keys in the CTA's keys
 // region ([4 * batch] 64-bit words).
 struct SampleSmem {
-  unsigned long long* keys;
-  unsigned long long* stats;
-  const uint64_t* seeds;
+  unsigned long long* keys;   // [B] running Gumbel-max keys
+  unsigned long long* stats;  // [B] the CTA's (max, sum) pairs so far
+  const uint64_t* seeds;      // [B]
+  float* noise;               // [kListCap] Gumbel noise of the round's units
+  float* y;                   // [kListCap] scaled logits of the round's units
+  unsigned int* rmax;         // [B] the round's max per request (ordered bits)
+  float* rsum;                // [B] the round's sum of exp(y - rmax) per request
 };
 
 __device__ __forceinline__ SampleSmem sample_smem(unsigned long long* s_keys, int batch) {
-  return SampleSmem{s_keys + batch, s_keys + 2 * batch, reinterpret_cast<const uint64_t*>(s_keys + 3 * batch)};
+  float* noise = reinterpret_cast<float*>(s_keys + 4 * batch);
+  unsigned int* rmax = reinterpret_cast<unsigned int*>(noise + 2 * kListCap);
+  return SampleSmem{s_keys + batch, s_keys + 2 * batch, reinterpret_cast<const uint64_t*>(s_keys + 3 * batch),
+                    noise, noise + kListCap, rmax, reinterpret_cast<float*>(rmax + batch)};
 }
+
+// Bytes of a kernel's keys region: top-1 keys and the sampler's arrays.
+__host__ __device__ inline size_t keys_region_bytes(int batch) { return 40 * (size_t)batch + 8 * (size_t)kListCap; }
 
 // Initialises the CTA's sampler state (call before the first __syncthreads).
 __device__ __forceinline__ void sample_smem_init(const RowSparseParams& p, unsigned long long* s_keys) {
+  const SampleSmem ss = sample_smem(s_keys, p.batch);
   for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
-    s_keys[p.batch + b] = 0ull;
-    s_keys[2 * p.batch + b] = empty_stats();
+    ss.keys[b] = 0ull;
+    ss.stats[b] = empty_stats();
     s_keys[3 * p.batch + b] = p.seeds[b];
+    ss.rmax[b] = 0u;
+    ss.rsum[b] = 0.f;
   }
 }
 
 // Running per-lane sampler state of one request run.
 struct RunningSample {
   RunningTop key;
-  RunningStats stats;
 };
 
+// After a round's units are streamed (their scaled logits in ss.y): the
+// round's (max, sum) per request with native shared-memory atomics (a 32-bit
+// max of ordered bits, then float adds of exp(y - max)), folded into the
+// CTA's running pair by one thread per request. Contains three __syncthreads
+// and must be reached by the whole CTA.
+template <bool kSample>
+__device__ __forceinline__ void round_stats(const SampleSmem& ss, const uint32_t* s_list, int n,
+                                            uint32_t code_stride) {
+  if constexpr (kSample) {
+    // Units are sorted by request, so a warp's 32 consecutive units hold a few
+    // contiguous runs of one request each: reduce each run in the warp, then
+    // one atomic per run (all units of a CTA usually share one or two
+    // requests, and same-address shared atomics serialise).
+    const int lane = threadIdx.x & 31;
+    __syncthreads();
+    for (int base = (int)(threadIdx.x & ~31u); base < n; base += blockDim.x) {
+      const int i = base + lane;
+      const bool valid = i < n;
+      const int b = valid ? (int)(s_list[i] / code_stride) : -1 - lane;  // invalid lanes: runs of their own
+      const unsigned run = __match_any_sync(FULL_MASK, b);
+      const unsigned mx = __reduce_max_sync(run, valid ? ordered_bits(ss.y[i]) : 0u);
+      if (valid && lane == __ffs(run) - 1) atomicMax(&ss.rmax[b], mx);
+    }
+    __syncthreads();
+    for (int base = (int)(threadIdx.x & ~31u); base < n; base += blockDim.x) {
+      const int i = base + lane;
+      const bool valid = i < n;
+      const int b = valid ? (int)(s_list[i] / code_stride) : -1 - lane;
+      float e = valid ? __expf(ss.y[i] - from_ordered_bits(ss.rmax[b])) : 0.f;
+      // suffix sums within each contiguous run; its first lane ends with the run's sum
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float e2 = __shfl_down_sync(FULL_MASK, e, o);
+        const int b2 = __shfl_down_sync(FULL_MASK, b, o);
+        if (lane + o < 32 && b2 == b) e += e2;
+      }
+      const int bp = __shfl_up_sync(FULL_MASK, b, 1);
+      if (valid && (lane == 0 || bp != b)) atomicAdd(&ss.rsum[b], e);
+    }
+    __syncthreads();
+    const int b0 = (int)(s_list[0] / code_stride), b1 = (int)(s_list[n - 1] / code_stride);
+    for (int b = b0 + (int)threadIdx.x; b <= b1; b += blockDim.x) {
+      if (ss.rsum[b] > 0.f) {
+        float m = stats_m(ss.stats[b]), sum = stats_s(ss.stats[b]);
+        merge_stats(m, sum, from_ordered_bits(ss.rmax[b]), ss.rsum[b]);
+        ss.stats[b] = pack_stats(m, sum);
+      }
+      ss.rmax[b] = 0u;
+      ss.rsum[b] = 0.f;
+    }
+  }
+}
+
+// ui: the unit's index in the round (its slot in the sampler's per-unit arrays).
 template <typename T, bool kSample>
 __device__ __forceinline__ void emit_unit(const RowSparseParams& p, int b, int v, uint64_t rank, float acc,
                                           bool want_top, RunningTop& top, unsigned long long* s_keys,
-                                          RunningSample& rs, const SampleSmem& ss, float noise) {
+                                          RunningSample& rs, int ui) {
   const uint16_t bits = DTypeTraits<T>::round_bits(acc);
   if (p.logits) static_cast<uint16_t*>(p.logits)[(int64_t)b * p.logits_stride + v] = bits;
   if (p.compact && rank < (uint64_t)p.capacity) {
@@ -123,17 +189,28 @@ __device__ __forceinline__ void emit_unit(const RowSparseParams& p, int b, int v
   if (want_top)
     top.add(b, top1_key(DTypeTraits<T>::bits_to_float(bits), (uint64_t)(p.vocab_offset + v)), s_keys);
   if constexpr (kSample) {
+    // the sampler's arrays are derived here, not held across the row loop
+    const SampleSmem ss = sample_smem(s_keys, p.batch);
     const float y = DTypeTraits<T>::bits_to_float(bits) * p.inv_temp;
-    rs.stats.add(b, y, ss.stats);
-    rs.key.add(b, top1_key(y + noise, (uint64_t)(p.vocab_offset + v)), ss.keys);
+    ss.y[ui] = y;
+    rs.key.add(b, top1_key(y + ss.noise[ui], (uint64_t)(p.vocab_offset + v)), ss.keys);
   }
 }
 
-// Noise of unit (b, v) for the lane that will emit it.
+// Gumbel noise of the round's units s_list[0, n), one unit per thread, into
+// ss.noise (kSample kernels; between the two __syncthreads that bracket the
+// round's list and its streaming).
 template <bool kSample>
-__device__ __forceinline__ float unit_noise(const RowSparseParams& p, const SampleSmem& ss, int b, int v) {
-  if constexpr (kSample) return gumbel_noise(ss.seeds[b], p.offset, (uint64_t)(p.vocab_offset + v));
-  return 0.f;
+__device__ __forceinline__ void round_noise(const RowSparseParams& p, const SampleSmem& ss, const uint32_t* s_list,
+                                            int n, uint32_t code_stride) {
+  if constexpr (kSample) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t c = s_list[i];
+      const int b = (int)(c / code_stride), v = (int)(c - (uint32_t)b * code_stride);
+      ss.noise[i] = gumbel_noise(ss.seeds[b], p.offset, (uint64_t)(p.vocab_offset + v));
+    }
+    __syncthreads();
+  }
 }
 
 // Every CTA: publishes its sampler state (sample keys by atomicMax, its (max,
@@ -143,27 +220,45 @@ __device__ __forceinline__ bool sample_publish(const RowSparseParams& p, const S
   for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
     const unsigned long long k = ss.keys[b];
     if (k != 0ull) atomicMax(p.sample_keys + b, k);
-    p.stat_partials[(size_t)blockIdx.x * p.batch + b] = ss.stats[b];
+    p.stat_partials[(size_t)b * kMaxSlices + blockIdx.x] = ss.stats[b];  // request-major
     did = true;
   }
   return did;
 }
 
 // Last CTA: sampled ids and log-sum-exp per request; re-zeroes the sampler's
-// workspace (keys and every CTA's partials).
+// workspace (keys and every CTA's partials). The ids take one thread per
+// request; the log-sum-exp a warp per request, its lanes loading the G
+// partials (request-major, so each load instruction is coalesced) eight at a
+// time (one L2 round trip per 256 CTAs), then merging across the warp with
+// shuffles.
 __device__ __forceinline__ void sample_finish(const RowSparseParams& p) {
-  const int G = gridDim.x;
-  for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
-    const unsigned long long k = atomicExch(p.sample_keys + b, 0ull);
-    p.sample_index[b] = key_index(k);
+  constexpr int kChunkLoads = 8;
+  const int G = gridDim.x, B = p.batch, lane = threadIdx.x & 31, warp = threadIdx.x >> 5,
+            nwarps = blockDim.x >> 5;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) p.sample_index[b] = key_index(atomicExch(p.sample_keys + b, 0ull));
+  for (int b = warp; b < B; b += nwarps) {
     float m = -INFINITY, sum = 0.f;
-    for (int c = 0; c < G; ++c) {
-      unsigned long long* w = p.stat_partials + (size_t)c * p.batch + b;
-      const unsigned long long x = __ldcg(w);
-      merge_stats(m, sum, stats_m(x), stats_s(x));
-      *w = 0ull;
+    for (int c0 = 0; c0 < G; c0 += 32 * kChunkLoads) {
+      unsigned long long x[kChunkLoads];
+#pragma unroll
+      for (int k = 0; k < kChunkLoads; ++k) {
+        const int c = c0 + lane + 32 * k;
+        x[k] = c < G ? __ldcg(p.stat_partials + (size_t)b * kMaxSlices + c) : empty_stats();
+      }
+#pragma unroll
+      for (int k = 0; k < kChunkLoads; ++k) {
+        const int c = c0 + lane + 32 * k;
+        if (c < G) p.stat_partials[(size_t)b * kMaxSlices + c] = 0ull;
+        merge_stats(m, sum, stats_m(x[k]), stats_s(x[k]));
+      }
     }
-    if (p.sample_lse) p.sample_lse[b] = sum > 0.f ? m + logf(sum) : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(FULL_MASK, m, o), s2 = __shfl_xor_sync(FULL_MASK, sum, o);
+      merge_stats(m, sum, m2, s2);
+    }
+    if (lane == 0 && p.sample_lse) p.sample_lse[b] = sum > 0.f ? m + logf(sum) : -INFINITY;
   }
 }
 
@@ -260,7 +355,6 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
   const int H = p.hidden_dim, nvec = H / 8;
   RunningTop top;
   RunningSample rs;
-  const SampleSmem ss = kSample ? sample_smem(s_keys, p.batch) : SampleSmem{nullptr, nullptr, nullptr};
   for (int i = warp; i < n; i += 2 * kWarps) {
     const int j = i + kWarps;
     const bool has2 = j < n;
@@ -276,7 +370,6 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
                              : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) +
                                                               (int64_t)bb * p.hidden_stride);
     float acc_a = 0.f, acc_b = 0.f;
-    float noise = 0.f;
     for (int base = 0; base < nvec; base += 32 * kUnroll) {
       uint4 ra[kUnroll], rb[kUnroll];
 #pragma unroll
@@ -285,8 +378,6 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
         ra[u] = e < nvec ? ld_stream_v4(wa + e * 8) : make_uint4(0, 0, 0, 0);
         rb[u] = (has2 && e < nvec) ? ld_stream_v4(wb + e * 8) : make_uint4(0, 0, 0, 0);
       }
-      // sampler noise of the two units, while the rows are in flight
-      if (kSample && base == 0 && lane < 2) noise = unit_noise<kSample>(p, ss, lane ? bb : ba, lane ? vb : va);
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const int e = base + u * 32 + lane;
@@ -301,16 +392,12 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
       acc_a += __shfl_xor_sync(FULL_MASK, acc_a, o);
       acc_b += __shfl_xor_sync(FULL_MASK, acc_b, o);
     }
-    if (lane == 0) emit_unit<T, kSample>(p, ba, va, rbase + (uint64_t)i, acc_a, want_top, top, s_keys, rs, ss, noise);
-    if (lane == 1 && has2)
-      emit_unit<T, kSample>(p, bb, vb, rbase + (uint64_t)j, acc_b, want_top, top, s_keys, rs, ss, noise);
+    if (lane == 0) emit_unit<T, kSample>(p, ba, va, rbase + (uint64_t)i, acc_a, want_top, top, s_keys, rs, i);
+    if (lane == 1 && has2) emit_unit<T, kSample>(p, bb, vb, rbase + (uint64_t)j, acc_b, want_top, top, s_keys, rs, j);
   }
   if (lane < 2) {
     top.flush(s_keys);
-    if constexpr (kSample) {
-      rs.key.flush(ss.keys);
-      rs.stats.flush(ss.stats);
-    }
+    if constexpr (kSample) rs.key.flush(s_keys + p.batch);
   }
 }
 
@@ -323,7 +410,6 @@ __device__ __forceinline__ void stream_rows_scalar(const RowSparseParams& p, con
   const int H = p.hidden_dim;
   RunningTop top;
   RunningSample rs;
-  const SampleSmem ss = kSample ? sample_smem(s_keys, p.batch) : SampleSmem{nullptr, nullptr, nullptr};
   for (int i = warp; i < n; i += kWarps) {
     const uint32_t c = s_list[i];
     const int b = (int)(c / code_stride), v = (int)(c - (uint32_t)b * code_stride);
@@ -334,15 +420,11 @@ __device__ __forceinline__ void stream_rows_scalar(const RowSparseParams& p, con
       acc = fmaf(DTypeTraits<T>::bits_to_float(__ldg(w + k)), DTypeTraits<T>::bits_to_float(__ldg(h + k)), acc);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL_MASK, acc, o);
-    if (lane == 0) emit_unit<T, kSample>(p, b, v, rbase + (uint64_t)i, acc, want_top, top, s_keys, rs, ss,
-                                         unit_noise<kSample>(p, ss, b, v));
+    if (lane == 0) emit_unit<T, kSample>(p, b, v, rbase + (uint64_t)i, acc, want_top, top, s_keys, rs, i);
   }
   if (lane == 0) {
     top.flush(s_keys);
-    if constexpr (kSample) {
-      rs.key.flush(ss.keys);
-      rs.stats.flush(ss.stats);
-    }
+    if constexpr (kSample) rs.key.flush(s_keys + p.batch);
   }
 }
 
@@ -386,7 +468,7 @@ __host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim,
   l.list = off;
   off += 4 * (size_t)kListCap;
   l.keys = align_up(off, 16);
-  off = l.keys + 32 * (size_t)batch;  // top-1 keys + the sampler's three arrays
+  off = l.keys + keys_region_bytes(batch);
   l.warp = align_up(off, 16);
   off = l.warp + 4 * 32;
   l.misc = align_up(off, 16);
@@ -575,8 +657,10 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
       }
     }
     __syncthreads();
+    round_noise<kSample>(p, sample_smem(s_keys, B), s_list, n, code_stride);
     // ---- 5. stream the rows ------------------------------------------------
     stream_rows<T, true, kSample>(p, s_list, n, rbase, code_stride, s_h, 0, want_top, s_keys);
+    round_stats<kSample>(sample_smem(s_keys, B), s_list, n, code_stride);
     __syncthreads();
   }
 
@@ -598,7 +682,7 @@ __host__ __device__ inline DirectLayout direct_layout(int batch) {
   DirectLayout l;
   l.list = 0;
   l.keys = align_up(l.list + sizeof(uint32_t) * kListCap, 16);
-  l.warp = align_up(l.keys + 4 * sizeof(unsigned long long) * batch, 16);  // + sampler arrays
+  l.warp = align_up(l.keys + keys_region_bytes(batch), 16);
   l.misc = align_up(l.warp + sizeof(uint32_t) * 32, 16);
   l.total = align_up(l.misc + 16, 128);
   return l;
@@ -706,10 +790,12 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_direct_kernel(const Ro
       }
     }
     __syncthreads();
+    round_noise<kSample>(p, sample_smem(s_keys, B), s_list, n, code_stride);
     if (kVec)
       stream_rows<T, false, kSample>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
     else
       stream_rows_scalar<T, kSample>(p, s_list, n, rbase, code_stride, want_top, s_keys);
+    round_stats<kSample>(sample_smem(s_keys, B), s_list, n, code_stride);
     __syncthreads();
   }
 
@@ -749,7 +835,7 @@ __host__ __device__ inline CoopLayout coop_layout(int batch) {
   l.list = off;
   off += 4 * (size_t)kListCap;
   l.keys = align_up(off, 16);
-  off = l.keys + 32 * (size_t)batch;  // top-1 keys + the sampler's three arrays
+  off = l.keys + keys_region_bytes(batch);
   l.warp = align_up(off, 16);
   off = l.warp + 4 * 32;
   l.misc = align_up(off, 16);
@@ -838,6 +924,7 @@ __device__ __forceinline__ void coop_stream_round(const RowSparseParams& p, cons
     if (tid == 0 && p.error) atomicExch(p.error, 2);
     return;
   }
+  round_noise<kSample>(p, sample_smem(s_keys, p.batch), s_list, n, code_stride);
   const int rb0 = (int)(s_list[0] / code_stride), rb1 = (int)(s_list[n - 1] / code_stride);
   if ((size_t)(rb1 - rb0 + 1) * H * 2 <= (size_t)kHStageBytes) {
     if (rb0 < h_lo || rb1 >= h_hi) {
@@ -855,6 +942,7 @@ __device__ __forceinline__ void coop_stream_round(const RowSparseParams& p, cons
   } else {
     stream_rows<T, false, kSample>(p, s_list, n, rbase, code_stride, nullptr, 0, want_top, s_keys);
   }
+  round_stats<kSample>(sample_smem(s_keys, p.batch), s_list, n, code_stride);
 }
 
 // Bounded wait (one polling thread per flag) until *flag != 0; returns the

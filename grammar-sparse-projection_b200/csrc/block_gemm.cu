@@ -11,20 +11,26 @@
 //  * tile_builder_kernel: for every 128-row vocabulary tile, OR of the batch's
 //    mask words (4 words per request); active tile ids are compacted per
 //    builder block of kBuilderTiles tiles. Skipped in dense mode.
-//  * tc_projection_kernel: one persistent CTA per SM, 6 warps.
+//  * tc_projection_kernel: one persistent CTA per SM, 10 warps.
 //      warp 0      one lane issues TMA loads of the W tile (128 rows x 64 K,
 //                  128-byte swizzle) and of h (Npad rows x 64 K) into a ring of
 //                  shared-memory stages;
 //      warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128 vocabulary
 //                  rows, N = batch padded to a multiple of 32, K = 16 per
-//                  instruction) into one of two TMEM accumulators, committing
-//                  each stage back to the producer and each tile to the epilogue;
-//      warps 2-5   epilogue: first -inf over every request's outputs in the
-//                  inactive tiles (block mode; while the first accumulator is
-//                  computed), then per tile tcgen05.ld of the accumulator (one TMEM lane = one
-//                  vocabulary row per thread), mask bit, rounding, -inf, logits
-//                  stores coalesced along the vocabulary, and 64-bit top-1 keys
-//                  reduced across the warp's 32 rows with a transpose-reduce.
+//                  instruction) into one of 4 TMEM accumulators (2 when
+//                  N > 128), committing each stage back to the producer and
+//                  each tile to the epilogue;
+//      warps 2-9   epilogue, two warps per TMEM lane quadrant splitting the
+//                  accumulator's columns: first -inf over every request's
+//                  outputs in the inactive tiles (block mode; while the first
+//                  accumulator is computed), then per tile tcgen05.ld of the
+//                  accumulator (one TMEM lane = one vocabulary row per thread),
+//                  mask bit (words loaded before the accumulator wait),
+//                  rounding, -inf, logits stores coalesced along the
+//                  vocabulary, and 32-bit warp-local top-1 keys (16-bit value
+//                  order + row) reduced across the warp's 32 rows with a
+//                  transpose-reduce, widened to 64-bit global keys once per
+//                  request.
 //    Tiles are taken from the compacted list round-robin by CTA. The cross-CTA
 //    top-1 merge is the same last-arrival scheme as the row-sparse kernel.
 //
@@ -50,8 +56,11 @@ namespace {
 
 constexpr int kTileRows = 128;
 constexpr int kTileK = 64;  // K elements per stage: one 128-byte swizzle row
-constexpr int kGemmThreads = 192;
+constexpr int kEpilogueWarps = 8;  // two per TMEM lane quadrant
+constexpr int kGemmThreads = 32 * (2 + kEpilogueWarps);
 constexpr int kMaxNpad = 256;
+constexpr int kMaxAcc = 4;          // TMEM accumulators (4 when npad <= 128, else 2)
+constexpr int kMaxUnits = kMaxNpad / 64;  // 32-column units per epilogue warp
 constexpr int kMaxStages = 8;
 constexpr uint32_t kABytes = kTileRows * kTileK * 2;  // 16 KB
 
@@ -61,6 +70,7 @@ struct GemmConfig {
   int kblocks;   // ceil(H / 64)
   int ntiles;    // ceil(V / 128)
   int nbuild;    // builder blocks (block mode)
+  int acc_shift; // log2 of the accumulator count
   uint32_t tmem_cols;
   uint32_t idesc;
 };
@@ -79,7 +89,7 @@ __host__ __device__ inline GemmLayout gemm_layout(int npad, int stages, int nbui
   l.b = align_to(off, 1024);
   off = l.b + (size_t)stages * npad * kTileK * 2;
   l.bars = align_to(off, 16);
-  off = l.bars + 8 * (2 * (size_t)stages + 4);
+  off = l.bars + 8 * (2 * (size_t)stages + 2 * kMaxAcc);
   l.tmem = align_to(off, 16);
   off = l.tmem + 16;
   l.keys = align_to(off, 16);
@@ -107,9 +117,10 @@ __device__ __forceinline__ int tile_at(const BlockGemmParams& p, const GemmConfi
 }
 
 // -inf over every request's outputs in the inactive 128-row tiles
-// t = cta + G * (ew + 4 j) (block mode): a tile is inactive when no request
-// has a legal token in it, the same test the builder applies. Run by the
-// epilogue warps (ew = 0..3) before their first accumulator arrives.
+// t = cta + G * (ew + kEpilogueWarps j) (block mode): a tile is inactive when
+// no request has a legal token in it, the same test the builder applies. Run
+// by the epilogue warps (ew = 0..kEpilogueWarps-1) before their first
+// accumulator arrives.
 template <typename T>
 __device__ __forceinline__ void fill_inactive_tiles(const BlockGemmParams& p, int ntiles, int cta, int G, int ew,
                                                     int lane) {
@@ -117,7 +128,7 @@ __device__ __forceinline__ void fill_inactive_tiles(const BlockGemmParams& p, in
   const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
   const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 15) == 0) && (p.logits_stride % 8 == 0);
-  for (int t = cta + ew * G; t < ntiles; t += 4 * G) {
+  for (int t = cta + ew * G; t < ntiles; t += kEpilogueWarps * G) {
     uint32_t any = 0u;
     for (int b = lane; b < B; b += 32) {
       const uint32_t* row = p.mask + (int64_t)b * p.mask_stride;
@@ -141,7 +152,90 @@ __device__ __forceinline__ void fill_inactive_tiles(const BlockGemmParams& p, in
   }
 }
 
+// First request column of epilogue unit u of the quadrant's warp `half`.
+__device__ __forceinline__ int unit_col(bool narrow, int half, int u) {
+  return narrow ? 16 * half : 32 * (half + 2 * u);
+}
+
+// Warp-local top-1 key of a rounded 16-bit value at row `lane` of the warp's
+// 32 rows: an order-preserving map of the 16-bit pattern (sign-magnitude to
+// biased, -0 and +0 equal, every legal value >= 0x0001) in the high half, and
+// 0xffff - lane in the low half so that the lower row wins ties. 0 means "no
+// legal token". Ordering equals that of top1_key on the widened value.
+__device__ __forceinline__ uint32_t warp_key16(uint32_t bits, uint32_t low) {
+  const uint32_t o = (bits & 0x8000u) ? 0x8000u - (bits & 0x7fffu) : (bits | 0x8000u);
+  return (o << 16) | low;
+}
+
+// Widen a warp_key16 of the warp whose first row is `row_base` (global
+// vocabulary id) to a global top1_key and keep the larger.
 template <typename T>
+__device__ __forceinline__ unsigned long long merge_unit_key(unsigned long long running, uint32_t k, int64_t row_base) {
+  if (k == 0u) return running;
+  const uint32_t o = k >> 16;
+  const uint32_t bits = o >= 0x8000u ? (o & 0x7fffu) : (0x8000u | (0x8000u - o));
+  const uint32_t r = 0xffffu - (k & 0xffffu);
+  const unsigned long long key =
+      top1_key(DTypeTraits<T>::bits_to_float((uint16_t)bits), (uint64_t)(row_base + (int64_t)r));
+  return key > running ? key : running;
+}
+
+// One epilogue unit: kCols accumulator columns (requests b0 .. b0 + kCols - 1)
+// of this warp's 32 TMEM lanes (one vocabulary row per thread). Rounds to the
+// logits dtype, applies the mask bit (word_l: this lane's mask word for
+// request b0 + lane % kCols), stores the row's logits (-inf where illegal) and
+// returns in lane l < kCols the warp_key16 maximum over the 32 rows for
+// request b0 + l.
+template <typename T, int kCols>
+__device__ __forceinline__ uint32_t epilogue_unit(uint32_t taddr, uint32_t word_l, int b0, int B, bool row_ok,
+                                                  bool store, uint16_t* out, int64_t stride, int lane) {
+  uint32_t v[kCols];
+  if constexpr (kCols == 32) tmem_ld32(taddr, v);
+  else tmem_ld16(taddr, v);
+  tmem_ld_wait();
+  const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
+  const uint32_t lanebit = row_ok ? (1u << lane) : 0u;
+  const uint32_t low = 0xffffu - (uint32_t)lane;
+  uint32_t key[kCols];
+  if (b0 + kCols <= B) {
+#pragma unroll
+    for (int jj = 0; jj < kCols; ++jj) {
+      const bool legal = (__shfl_sync(FULL_MASK, word_l, jj) & lanebit) != 0u;
+      const uint16_t bits = legal ? DTypeTraits<T>::round_bits(__uint_as_float(v[jj])) : ninf;
+      if (store) out[jj * stride] = bits;
+      key[jj] = legal ? warp_key16(bits, low) : 0u;
+    }
+  } else {
+#pragma unroll
+    for (int jj = 0; jj < kCols; ++jj) {
+      const bool legal = (__shfl_sync(FULL_MASK, word_l, jj) & lanebit) != 0u;  // word is 0 past B
+      const uint16_t bits = legal ? DTypeTraits<T>::round_bits(__uint_as_float(v[jj])) : ninf;
+      if (store && b0 + jj < B) out[jj * stride] = bits;
+      key[jj] = legal ? warp_key16(bits, low) : 0u;
+    }
+  }
+  // transpose-reduce: lane l ends with the maximum over the 32 rows of
+  // column l % kCols
+#pragma unroll
+  for (int h = kCols / 2; h >= 1; h >>= 1) {
+    const bool upper = (lane & h) != 0;
+#pragma unroll
+    for (int j = 0; j < h; ++j) {
+      const uint32_t send = upper ? key[j] : key[j + h];
+      const uint32_t keep = upper ? key[j + h] : key[j];
+      const uint32_t recv = __shfl_xor_sync(FULL_MASK, send, h);
+      key[j] = keep > recv ? keep : recv;
+    }
+  }
+  if constexpr (kCols == 16) {
+    const uint32_t other = __shfl_xor_sync(FULL_MASK, key[0], 16);
+    key[0] = key[0] > other ? key[0] : other;
+  }
+  return key[0];
+}
+
+// kNarrow: the batch pads to 32 columns (one 16-column unit per epilogue warp).
+template <typename T, bool kNarrow>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_projection_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_h,
                          const BlockGemmParams p, const GemmConfig c) {
@@ -154,8 +248,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   unsigned char* s_b = smem + L.b;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + c.stages;
-  uint64_t* tfull = empty + c.stages;  // [2]
-  uint64_t* tempty = tfull + 2;        // [2]
+  uint64_t* tfull = empty + c.stages;  // [kMaxAcc]
+  uint64_t* tempty = tfull + kMaxAcc;  // [kMaxAcc]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.tmem);
   unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
   int* s_pref = reinterpret_cast<int*>(smem + L.pref);
@@ -175,9 +269,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kMaxAcc; ++a) {
       mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, 4);  // one arrival per epilogue warp
+      mbar_init(tempty + a, kEpilogueWarps);  // one arrival per epilogue warp
     }
     fence_mbar_init();
     s_misc[0] = 0;
@@ -249,8 +343,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t last_use = 0;
       int i = 0;
       for (int pos = cta; pos < total && !*abort_flag; pos += G, ++i) {
-        const int acc = i & 1;
-        const uint32_t ause = (uint32_t)(i >> 1);
+        const int acc = i & ((1 << c.acc_shift) - 1);
+        const uint32_t ause = (uint32_t)(i >> c.acc_shift);
         if (ause > 0 && !mbar_wait(tempty + acc, (ause - 1) & 1u, abort_flag)) {
           *abort_flag = 1;
           break;
@@ -284,18 +378,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (last_stage >= 0) mbar_wait(empty + last_stage, last_use & 1u, nullptr);
     }
   } else {
-    // ---- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4) -----------
+    // ---- epilogue: warps 2..9; warp w reads TMEM lane quadrant w % 4 -------
+    // The quadrant's two warps split the accumulator's columns: 16 each when
+    // the batch pads to 32, else alternating 32-column units.
+    const int ew = warp - 2;
     const int q = warp & 3;
-    const int nchunks = c.npad / 32;
-    const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
-    if (!p.dense && p.logits) fill_inactive_tiles<T>(p, c.ntiles, cta, G, warp - 2, lane);
-    unsigned long long running[kMaxNpad / 32];
+    const int half = ew >> 2;
+    constexpr bool narrow = kNarrow;
+    const int nunits = narrow ? 1 : (c.npad / 32 - half + 1) / 2;
+    if (!p.dense && p.logits) fill_inactive_tiles<T>(p, c.ntiles, cta, G, ew, lane);
+    unsigned long long running[kMaxUnits];  // lane l: best key of the unit's request l
 #pragma unroll
-    for (int j = 0; j < kMaxNpad / 32; ++j) running[j] = 0ull;
+    for (int u = 0; u < kMaxUnits; ++u) running[u] = 0ull;
+    const int ulane = narrow ? (lane & 15) : lane;  // request column a lane's mask word serves
     int i = 0;
     for (int pos = cta; pos < total; pos += G, ++i) {
-      const int acc = i & 1;
-      const uint32_t ause = (uint32_t)(i >> 1);
+      const int acc = i & ((1 << c.acc_shift) - 1);
+      const uint32_t ause = (uint32_t)(i >> c.acc_shift);
+      const int tile = tile_at(p, c, s_pref, pos);
+      const int row0 = tile * kTileRows + q * 32;
+      const int word_idx = tile * 4 + q;  // mask word holding this warp's 32 rows
+      // mask words first: their loads overlap the wait for the accumulator
+      uint32_t words[kMaxUnits];
+#pragma unroll
+      for (int u = 0; u < kMaxUnits; ++u) {
+        words[u] = 0u;
+        const int b = unit_col(narrow, half, u) + ulane;
+        if (u < nunits && b < B) {
+          if (!p.mask) words[u] = 0xffffffffu;
+          else if (word_idx < p.nw) words[u] = __ldg(p.mask + (int64_t)b * p.mask_stride + word_idx);
+        }
+      }
       const bool ok = mbar_wait(tfull + acc, ause & 1u, abort_flag);
       __syncwarp();
       if (!ok) {
@@ -303,46 +416,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      const int tile = tile_at(p, c, s_pref, pos);
-      const int row = tile * kTileRows + q * 32 + lane;
-      const int word_idx = tile * 4 + q;  // mask word holding this warp's 32 rows
+      const int row = row0 + lane;
+      const bool row_ok = row < V;
+      const bool store = row_ok && p.logits != nullptr;
+      const uint32_t tcol = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * c.npad);
+      uint16_t* out = static_cast<uint16_t*>(p.logits) + row;
+      if constexpr (narrow) {
+        const int b0 = 16 * half;
+        const uint32_t k = epilogue_unit<T, 16>(tcol + (uint32_t)b0, words[0], b0, B, row_ok, store,
+                                                 out + (int64_t)b0 * p.logits_stride, p.logits_stride, lane);
+        running[0] = merge_unit_key<T>(running[0], k, p.vocab_offset + row0);
+      } else {
 #pragma unroll
-      for (int ch = 0; ch < kMaxNpad / 32; ++ch) {
-        if (ch < nchunks) {
-          uint32_t v[32];
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * c.npad + ch * 32), v);
-          tmem_ld_wait();
-          const int b0 = ch * 32;
-          uint32_t my_word = 0u;
-          if (b0 + lane < B) {
-            if (!p.mask) my_word = 0xffffffffu;
-            else if (word_idx < p.nw) my_word = __ldg(p.mask + (int64_t)(b0 + lane) * p.mask_stride + word_idx);
+        for (int u = 0; u < kMaxUnits; ++u) {
+          if (u < nunits) {
+            const int b0 = unit_col(false, half, u);
+            const uint32_t k = epilogue_unit<T, 32>(tcol + (uint32_t)b0, words[u], b0, B, row_ok, store,
+                                                     out + (int64_t)b0 * p.logits_stride, p.logits_stride, lane);
+            running[u] = merge_unit_key<T>(running[u], k, p.vocab_offset + row0);
           }
-          unsigned long long key[32];
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int b = b0 + jj;
-            const uint32_t word = __shfl_sync(FULL_MASK, my_word, jj);
-            const bool in = (b < B) && (row < V);
-            const bool legal = in && ((word >> lane) & 1u);
-            const uint16_t bits = legal ? DTypeTraits<T>::round_bits(__uint_as_float(v[jj])) : ninf;
-            if (in && p.logits) static_cast<uint16_t*>(p.logits)[(int64_t)b * p.logits_stride + row] = bits;
-            key[jj] = legal ? top1_key(DTypeTraits<T>::bits_to_float(bits), (uint64_t)(p.vocab_offset + row)) : 0ull;
-          }
-          // transpose-reduce: lane l ends with the max over the warp's 32 rows
-          // of request b0 + l
-#pragma unroll
-          for (int half = 16; half >= 1; half >>= 1) {
-            const bool upper = (lane & half) != 0;
-#pragma unroll
-            for (int j = 0; j < half; ++j) {
-              const unsigned long long send = upper ? key[j] : key[j + half];
-              const unsigned long long keep = upper ? key[j + half] : key[j];
-              const unsigned long long recv = shfl_xor_u64(send, half);
-              key[j] = keep > recv ? keep : recv;
-            }
-          }
-          running[ch] = key[0] > running[ch] ? key[0] : running[ch];
         }
       }
       tc_fence_before_sync();
@@ -351,9 +443,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     if (want_top) {
 #pragma unroll
-      for (int ch = 0; ch < kMaxNpad / 32; ++ch) {
-        const int b = ch * 32 + lane;
-        if (ch < nchunks && b < B && running[ch] != 0ull) atomicMax(&s_keys[b], running[ch]);
+      for (int u = 0; u < kMaxUnits; ++u) {
+        const int b = unit_col(narrow, half, u) + lane;
+        if (u < nunits && lane < (narrow ? 16 : 32) && b < B && running[u] != 0ull) atomicMax(&s_keys[b], running[u]);
       }
     }
   }
@@ -512,8 +604,11 @@ cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream)
   c.kblocks = (p.hidden_dim + kTileK - 1) / kTileK;
   c.ntiles = (p.vocab + kTileRows - 1) / kTileRows;
   c.nbuild = (c.ntiles + kBuilderTiles - 1) / kBuilderTiles;
+  // 4 accumulators let the MMA run up to 3 tiles ahead of the epilogue; TMEM
+  // holds 512 fp32 columns per SM
+  c.acc_shift = c.npad <= 128 ? 2 : 1;
   uint32_t cols = 32;
-  while (cols < 2u * (uint32_t)c.npad) cols <<= 1;
+  while (cols < ((uint32_t)c.npad << c.acc_shift)) cols <<= 1;
   c.tmem_cols = cols;
   c.idesc = tc_idesc_f16((uint32_t)c.npad, sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value);
   const size_t stage_bytes = kABytes + (size_t)c.npad * kTileK * 2;
@@ -534,7 +629,7 @@ cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream)
     tile_builder_kernel<T><<<c.nbuild, kBuilderThreads, 0, stream>>>(p, c.ntiles);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
   }
-  auto k = tc_projection_kernel<T>;
+  auto k = c.npad == 32 ? tc_projection_kernel<T, true> : tc_projection_kernel<T, false>;
   const size_t smem_bytes = L.total + 1024;
   if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), smem_bytes, dev)) != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};

@@ -66,7 +66,7 @@ def parse_args():
     ap.add_argument("--sweep-steps", type=int, default=100)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-vp", action="store_true", help="skip the vocabulary-parallel head section")
-    ap.add_argument("--only", choices=("batched", "mixed", "vp", "sampler"), default=None,
+    ap.add_argument("--only", choices=("batched", "mixed", "vp", "sampler", "graphed"), default=None,
                     help="run one extra section alone (small; for profiling)")
     ap.add_argument("--batch", type=int, default=32, help="batch of --only batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -265,6 +265,8 @@ def main():
             g = torch.Generator(device=dev).manual_seed(1234)
             weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(4)]
             res = sampler_section(dev, weights, steps=max(args.steps, 1), batches=(1, args.batch))
+        elif args.only == "graphed":
+            res = graphed_head_section(dev, steps=max(args.steps, 1))
         else:
             res = mixed_section(dev, peak, steps=max(args.steps, 1))
         print(json.dumps({"only": args.only, "result": res}), flush=True)
@@ -360,8 +362,8 @@ def main():
     for i in range(max(args.warmup, 3)):
         step(i)
     barrier()
-    sampler = ClockSampler(local_rank)
-    with sampler:
+    clocks = ClockSampler(local_rank)
+    with clocks:
         t_wall = time.perf_counter()
         total_us = graph_total_us(args.steps, step)
         barrier()
@@ -441,7 +443,8 @@ def main():
     sweep = None
     batched = None
     mixed = None
-    sampler = None
+    sampler_res = None
+    graphed = None
     same_gpu_dense = None
     cpu_base = None
     if world == 1 and not args.no_sweep:
@@ -462,7 +465,8 @@ def main():
         same_gpu_dense = time_dense_baseline(dev, weight, hidden, masks, args)
         batched = batched_section(dev, weights[:8], peak)
         mixed = mixed_section(dev, peak)
-        sampler = sampler_section(dev, weights[:8])
+        sampler_res = sampler_section(dev, weights[:8])
+        graphed = graphed_head_section(dev)
     vp_head = None if args.no_vp else vocab_parallel_section(dev, world, rank, peak)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         w_cpu = weight.cpu().numpy()
@@ -487,7 +491,7 @@ def main():
             "gpu_launches": args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu_base,
-            "clocks": sampler.summary(),
+            "clocks": clocks.summary(),
             "cold": cold,
             "timed_region_wall_s": t_wall,
             "sweep": sweep,
@@ -495,7 +499,8 @@ def main():
             "mixed": mixed,
             "same_gpu_dense_mask": same_gpu_dense,
             "vocab_parallel_head": vp_head,
-            "sampler": sampler,
+            "sampler": sampler_res,
+            "graphed_head": graphed,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -792,6 +797,97 @@ def mixed_section(dev, peak, steps=10):
                     "tokens_per_s_best": batch / (times[best] * 1e-6)})
     del weights
     return out
+
+
+def graphed_head_section(dev, steps=20):
+    """Device-side mask path at the mixed shape (V=151,936, H=1,024 bf16,
+    batch 64), one mask per constrained fraction. GraphedGrammarHead: the head
+    as one CUDA graph (device route selector, SWITCH node, chosen projection
+    with fused top-1), timed with CUDA events over `steps` back-to-back
+    replays; the pinned-mask host-to-device copy (1.2 MB) timed alone on the
+    copy stream (in a decode loop it overlaps the transformer layers), and
+    staged copy + replay back to back (nothing to overlap with here). Against
+    the host-decided dispatch (policy "b200": device statistics read back,
+    route chosen on the host) and the eager device selector (policy "device":
+    4-byte route read back), wall clock over `steps` calls."""
+    import time
+    from gsp import triton_runtime as tr
+    from gsp import workloads as wl
+    from gsp.graphed import GraphedGrammarHead
+    vocab, hidden, batch = 151936, 1024, 64
+    g = torch.Generator(device=dev).manual_seed(7)
+    w = (torch.randn(vocab, hidden, device=dev, generator=g) * 0.02).bfloat16()
+    h = torch.randn(batch, hidden, device=dev, generator=g).bfloat16()
+    head = GraphedGrammarHead(w, batch)
+    head.hidden.copy_(h)
+
+    def events_us(fn, stream=None):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s = stream or torch.cuda.current_stream(dev)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(steps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / steps
+
+    out = []
+    for frac in (0.0, 0.5, 1.0):
+        rng = np.random.default_rng(int(frac * 100) + 11)
+        n_con = int(round(frac * batch))
+        legal = np.zeros((batch, vocab), dtype=bool)
+        for b in range(batch):
+            ids = (wl.clustered_legal_ids(rng, vocab, int(0.002 * vocab), 16) if b < n_con
+                   else wl.uniform_legal_ids(rng, vocab, int(0.95 * vocab)))
+            legal[b, ids] = True
+        mask_np = wl.pack_bitmask(legal)
+        head.wait_mask_copied()
+        head.mask_host.copy_(torch.from_numpy(mask_np))
+        head.stage_mask()
+        head.step()
+        torch.cuda.synchronize()
+        route = head.route_names()[0]
+        graph_us = events_us(head.step)
+
+        def copy_only():
+            head.mask.copy_(head.mask_host, non_blocking=True)
+        with torch.cuda.stream(head.copy_stream):
+            copy_us = events_us(copy_only, head.copy_stream)
+
+        def staged():
+            head.stage_mask()
+            head.step()
+        staged_us = events_us(staged)
+        mask_dev = torch.from_numpy(mask_np).to(dev)
+        eager = {}
+        for policy in ("b200", "device"):
+            for _ in range(3):
+                tr.adaptive_grammar_logits(h, w, mask_dev, policy=policy)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                _, r = tr.adaptive_grammar_logits(h, w, mask_dev, policy=policy)
+            torch.cuda.synchronize()
+            eager[policy] = {"us_per_step": (time.perf_counter() - t0) * 1e6 / steps, "route": r}
+        fn = {"row-sparse": _native_fn("row_sparse"), "block-sparse": _native_fn("block_gemm"),
+              "dense-mask": _native_fn("dense_masked")}[route]
+        direct_us = graph_time_us(dev, steps, lambda i: fn(h, w, mask_dev, logits=head.out.logits,
+                                                            top_value=head.out.top_value,
+                                                            top_index=head.out.top_index)) / steps
+        out.append({"constrained_fraction": frac, "route": route, "graphed_head_us": graph_us,
+                    "chosen_route_alone_us": direct_us, "mask_h2d_copy_us": copy_us,
+                    "staged_copy_then_head_us": staged_us, "mask_bytes": int(mask_np.nbytes),
+                    "host_b200_policy": eager["b200"], "eager_device_policy": eager["device"]})
+    del head, w
+    return out
+
+
+def _native_fn(name):
+    from gsp import _native
+    return getattr(_native, name)
 
 
 def time_dense_baseline(dev, weight, hidden, masks, args):

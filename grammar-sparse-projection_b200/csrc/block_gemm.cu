@@ -517,6 +517,10 @@ __global__ void __launch_bounds__(kBuilderThreads) tile_builder_kernel(const Blo
   const int tid = threadIdx.x;
   const int t0 = blockIdx.x * kBuilderTiles;
   const int V = p.vocab, nw = p.nw, B = p.batch;
+  // The projection kernel may start its set-up now (programmatic dependent
+  // launch): its CTAs fit beside these blocks, and its griddepcontrol.wait
+  // still waits for this grid to finish and its writes to be visible.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid < kBuilderTiles) s_act[tid] = 0u;
   __syncthreads();
 
@@ -550,9 +554,6 @@ __global__ void __launch_bounds__(kBuilderThreads) tile_builder_kernel(const Blo
     if (act) p.tile_list[t0 + __popc(am & below)] = t;
     if (tid == 0) p.tile_counts[blockIdx.x] = __popc(am);
   }
-  // The projection kernel may start its set-up now (programmatic dependent
-  // launch); its griddepcontrol.wait still waits for this grid to finish.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -639,7 +640,7 @@ cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream)
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = p.dense ? 0 : 1;
+  attr[0].val.programmaticStreamSerializationAllowed = (p.dense || p.no_pdl) ? 0 : 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k, tw, th, p, c);

@@ -14,6 +14,8 @@ namespace gsp {
 namespace {
 
 thread_local char g_last_error[512] = "";
+// Set while this thread records a conditional node's body (see kConditionalBodyPdl).
+thread_local bool tl_no_pdl = false;
 
 int32_t fail(int32_t code, const char* fmt, ...) {
   va_list ap;
@@ -48,8 +50,12 @@ Workspace carve_workspace(void* base, int batch, int vocab) {
   Workspace w;
   w.ticket = reinterpret_cast<unsigned int*>(p);
   w.error = reinterpret_cast<int*>(p + 4);
-  w.keys = reinterpret_cast<unsigned long long*>(p + 16);
-  p += align256(16 + sizeof(unsigned long long) * (size_t)batch);
+  w.route_ticket = reinterpret_cast<unsigned int*>(p + 8);
+  w.route_active = reinterpret_cast<unsigned int*>(p + 12);
+  w.route_legal = reinterpret_cast<unsigned long long*>(p + 16);
+  w.route_word = reinterpret_cast<int*>(p + 24);
+  w.keys = reinterpret_cast<unsigned long long*>(p + kKeysOffset);
+  p += align256(kKeysOffset + sizeof(unsigned long long) * (size_t)batch);
   w.tile_list = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * (size_t)ntiles);
   w.tile_counts = reinterpret_cast<int32_t*>(p);
@@ -239,8 +245,35 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
   p.tile_list = w.tile_list;
   p.tile_counts = w.tile_counts;
   p.dense = dense || bitmask == nullptr;
+  p.no_pdl = tl_no_pdl ? 1 : 0;
   if (peers) p.peers = *peers;
   return cuda_status(launch_block_gemm(p, dtype, s), fn);
+}
+
+// ---- device-side route choice ---------------------------------------------
+// Programmatic dependent launch between the tile builder and the projection
+// inside a conditional node's body.
+constexpr bool kConditionalBodyPdl = true;
+
+int32_t route_call(const char* fn, int route, const void* hidden, int64_t hidden_row_stride, const void* weight,
+                   int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch,
+                   int32_t vocab, int32_t hidden_dim, int32_t dtype, void* logits, int64_t logits_row_stride,
+                   float* top_value, int64_t* top_index, void* workspace, size_t workspace_bytes_, void* stream) {
+  const bool tc = route != GSP_ROUTE_ROW_SPARSE;
+  return projection_common(fn, tc, route == GSP_ROUTE_DENSE_MASK ? 1 : 0, hidden, hidden_row_stride, weight,
+                           weight_row_stride, bitmask, bitmask_row_stride, batch, vocab, hidden_dim, dtype, 0, logits,
+                           logits_row_stride, top_value, top_index, nullptr, workspace, workspace_bytes_, stream);
+}
+
+// One non-blocking stream per device for recording conditional bodies; the
+// mutex also serialises body recording between threads.
+std::mutex g_body_mu;
+cudaStream_t body_stream(int device) {
+  static cudaStream_t streams[128] = {};
+  if (device < 0 || device >= 128) return nullptr;
+  if (!streams[device] && cudaStreamCreateWithFlags(&streams[device], cudaStreamNonBlocking) != cudaSuccess)
+    streams[device] = nullptr;
+  return streams[device];
 }
 
 }  // namespace
@@ -449,6 +482,187 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
                            weight_row_stride, bitmask, bitmask_row_stride, batch, vocab, hidden_dim, dtype, vocab_offset, logits,
                            logits_row_stride, top_value, top_index, top_key, workspace, workspace_bytes_,
                            stream, &x);
+}
+
+void gsp_default_route_cost(gsp_route_cost* cost) {
+  if (!cost) return;
+  cost->hbm_gbs = kB200RouteCost.hbm_gbs;
+  cost->row_sparse_fixed_us = kB200RouteCost.row_sparse_fixed_us;
+  cost->block_floor_us = kB200RouteCost.block_floor_us;
+  cost->block_fixed_us = kB200RouteCost.block_fixed_us;
+  cost->block_gbs = kB200RouteCost.block_gbs;
+  cost->dense_fixed_us = kB200RouteCost.dense_fixed_us;
+  cost->dense_gbs = kB200RouteCost.dense_gbs;
+  cost->group_split_fixed_us = kB200RouteCost.group_split_fixed_us;
+}
+
+static RouteCost to_route_cost(const gsp_route_cost* c) {
+  if (!c) return kB200RouteCost;
+  return RouteCost{c->hbm_gbs, c->row_sparse_fixed_us, c->block_floor_us, c->block_fixed_us,
+                   c->block_gbs, c->dense_fixed_us, c->dense_gbs, c->group_split_fixed_us};
+}
+
+int32_t gsp_choose_route(int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t elem_bytes, int64_t legal_total,
+                         int64_t active_tiles, const gsp_route_cost* cost) {
+  if (batch < 1 || vocab < 1 || hidden_dim < 1 || elem_bytes < 1 || legal_total < 0 || active_tiles < 0)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "gsp_choose_route: sizes and counts must be positive");
+  return choose_route_by_cost(batch, vocab, hidden_dim, elem_bytes, legal_total, active_tiles, to_route_cost(cost));
+}
+
+int32_t gsp_adaptive_logits(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                            int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride,
+                            int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype, void* logits,
+                            int64_t logits_row_stride, float* top_value, int64_t* top_index,
+                            const gsp_route_cost* cost, int32_t* route_out, int32_t* route_host, void* workspace,
+                            size_t workspace_bytes_, void* stream) {
+  const char* fn = "gsp_adaptive_logits";
+  if (route_host) *route_host = -1;
+  int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                   bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
+  if (st != GSP_OK) return st;
+  if (!bitmask) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask is required", fn);
+  st = check_workspace(fn, true, workspace, workspace_bytes_, batch, vocab);
+  if (st != GSP_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err;
+  if (batch == 1) {  // always row-sparse
+    if (route_out && (err = cudaMemsetAsync(route_out, 0, sizeof(int32_t), s)) != cudaSuccess)
+      return cuda_status(err, fn);
+    if (route_host) *route_host = GSP_ROUTE_ROW_SPARSE;
+    return route_call(fn, GSP_ROUTE_ROW_SPARSE, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                      bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride, top_value,
+                      top_index, workspace, workspace_bytes_, stream);
+  }
+  const Workspace w = carve_workspace(workspace, batch, vocab);
+  RouteSelectParams sel;
+  std::memset(&sel, 0, sizeof(sel));
+  sel.mask = reinterpret_cast<const uint32_t*>(bitmask);
+  sel.mask_stride = bitmask_row_stride;
+  sel.batch = batch;
+  sel.vocab = vocab;
+  sel.nw = (vocab + 31) / 32;
+  sel.ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
+  sel.hidden_dim = hidden_dim;
+  sel.elem_bytes = 2;
+  sel.cost = to_route_cost(cost);
+  sel.ticket = w.route_ticket;
+  sel.active = w.route_active;
+  sel.legal = w.route_legal;
+  sel.route_out = route_out;
+
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if ((err = cudaStreamIsCapturing(s, &cs)) != cudaSuccess) return cuda_status(err, fn);
+  if (cs == cudaStreamCaptureStatusInvalidated)
+    return fail(GSP_ERR_CUDA, "%s: the stream's capture has been invalidated", fn);
+
+  if (cs == cudaStreamCaptureStatusNone) {
+    // eager: selector, 4-byte read-back, chosen route
+    sel.route_word = w.route_word;
+    if ((err = launch_route_select(sel, s)) != cudaSuccess) return cuda_status(err, fn);
+    int32_t route = -1;
+    if ((err = cudaMemcpyAsync(&route, w.route_word, sizeof(int32_t), cudaMemcpyDeviceToHost, s)) != cudaSuccess ||
+        (err = cudaMemsetAsync(w.route_word, 0, sizeof(int32_t), s)) != cudaSuccess ||
+        (err = cudaStreamSynchronize(s)) != cudaSuccess)
+      return cuda_status(err, fn);
+    if (route < GSP_ROUTE_ROW_SPARSE || route > GSP_ROUTE_DENSE_MASK)
+      return fail(GSP_ERR_CUDA, "%s: the route selector returned %d", fn, route);
+    if (route_host) *route_host = route;
+    return route_call(fn, route, hidden, hidden_row_stride, weight, weight_row_stride, bitmask, bitmask_row_stride,
+                      batch, vocab, hidden_dim, dtype, logits, logits_row_stride, top_value, top_index, workspace,
+                      workspace_bytes_, stream);
+  }
+
+  // capture: selector kernel -> SWITCH node {row-sparse, block-sparse, dense-mask}
+  int device = 0;
+  if ((err = cudaGetDevice(&device)) != cudaSuccess) return cuda_status(err, fn);
+  cudaGraph_t graph = nullptr;
+  const cudaGraphNode_t* deps = nullptr;
+  size_t ndeps = 0;
+  if ((err = cudaStreamGetCaptureInfo(s, &cs, nullptr, &graph, &deps, &ndeps)) != cudaSuccess)
+    return cuda_status(err, fn);
+  cudaGraphConditionalHandle handle;
+  if ((err = cudaGraphConditionalHandleCreate(&handle, graph, 0, cudaGraphCondAssignDefault)) != cudaSuccess)
+    return cuda_status(err, fn);
+  sel.handle = handle;
+  sel.has_handle = 1;
+  if ((err = launch_route_select(sel, s)) != cudaSuccess) return cuda_status(err, fn);
+  if ((err = cudaStreamGetCaptureInfo(s, &cs, nullptr, &graph, &deps, &ndeps)) != cudaSuccess)
+    return cuda_status(err, fn);
+  // (the struct's union has no default constructor: zero-filled storage)
+  alignas(cudaGraphNodeParams) unsigned char np_storage[sizeof(cudaGraphNodeParams)] = {};
+  cudaGraphNodeParams& np = *reinterpret_cast<cudaGraphNodeParams*>(np_storage);
+  np.type = cudaGraphNodeTypeConditional;
+  np.conditional.handle = handle;
+  np.conditional.type = cudaGraphCondTypeSwitch;
+  np.conditional.size = 3;
+  cudaGraphNode_t node;
+  if ((err = cudaGraphAddNode(&node, graph, deps, ndeps, &np)) != cudaSuccess) return cuda_status(err, fn);
+  {
+    std::lock_guard<std::mutex> lock(g_body_mu);
+    cudaStream_t bs = body_stream(device);
+    if (!bs) return fail(GSP_ERR_CUDA, "%s: could not create the body-recording stream", fn);
+    for (int r = GSP_ROUTE_ROW_SPARSE; r <= GSP_ROUTE_DENSE_MASK; ++r) {
+      if ((err = cudaStreamBeginCaptureToGraph(bs, np.conditional.phGraph_out[r], nullptr, nullptr, 0,
+                                               cudaStreamCaptureModeRelaxed)) != cudaSuccess)
+        return cuda_status(err, fn);
+      tl_no_pdl = !kConditionalBodyPdl;
+      st = route_call(fn, r, hidden, hidden_row_stride, weight, weight_row_stride, bitmask, bitmask_row_stride,
+                      batch, vocab, hidden_dim, dtype, logits, logits_row_stride, top_value, top_index, workspace,
+                      workspace_bytes_, bs);
+      tl_no_pdl = false;
+      cudaGraph_t body = nullptr;
+      err = cudaStreamEndCapture(bs, &body);
+      if (st != GSP_OK) return st;
+      if (err != cudaSuccess) return cuda_status(err, fn);
+    }
+  }
+  if ((err = cudaStreamUpdateCaptureDependencies(s, &node, 1, cudaStreamSetCaptureDependencies)) != cudaSuccess)
+    return cuda_status(err, fn);
+  return GSP_OK;
+}
+
+size_t gsp_group_plan_words(int32_t batch) {
+  if (batch < 1) return 0;
+  return (size_t)kPlanHeader + 6 * (size_t)batch;
+}
+
+int32_t gsp_group_plan(const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                       int32_t hidden_dim, int32_t elem_bytes, int32_t with_logits, const gsp_route_cost* cost,
+                       int32_t* plan, void* stream) {
+  const char* fn = "gsp_group_plan";
+  if (!bitmask || !plan) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask and plan are required", fn);
+  if (batch < 1 || batch > kGroupMaxBatch || vocab < 1 || hidden_dim < 1 || elem_bytes < 1)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: batch must be in [1, %d]; vocab, hidden_dim, elem_bytes positive", fn,
+                kGroupMaxBatch);
+  const int64_t nw = (vocab + 31) / 32;
+  if (batch > 1 && bitmask_row_stride < nw)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask_row_stride must be >= ceil(vocab/32)", fn);
+  GroupPlanParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mask = reinterpret_cast<const uint32_t*>(bitmask);
+  p.mask_stride = batch > 1 ? bitmask_row_stride : 0;
+  p.batch = batch;
+  p.vocab = vocab;
+  p.nw = (int)nw;
+  p.ntiles = (vocab + GSP_TILE_ROWS - 1) / GSP_TILE_ROWS;
+  p.hidden_dim = hidden_dim;
+  p.elem_bytes = elem_bytes;
+  p.with_logits = with_logits ? 1 : 0;
+  p.cost = to_route_cost(cost);
+  p.plan = plan;
+  return cuda_status(launch_group_plan(p, static_cast<cudaStream_t>(stream)), fn);
+}
+
+int32_t gsp_gather_rows(const void* src, int64_t src_row_stride_bytes, const int32_t* rows, int32_t n,
+                        int64_t row_bytes, void* dst, int64_t dst_row_stride_bytes, void* stream) {
+  const char* fn = "gsp_gather_rows";
+  if (n < 0 || row_bytes < 0) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: negative size", fn);
+  if (n == 0 || row_bytes == 0) return GSP_OK;
+  if (!src || !dst || !rows) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: src, rows and dst are required", fn);
+  if (dst_row_stride_bytes < row_bytes)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: dst_row_stride_bytes < row_bytes", fn);
+  return cuda_status(launch_gather_rows(src, src_row_stride_bytes, rows, n, row_bytes, dst, dst_row_stride_bytes,
+                                        static_cast<cudaStream_t>(stream)), fn);
 }
 
 }  // extern "C"

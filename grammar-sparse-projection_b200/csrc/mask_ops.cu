@@ -1,5 +1,5 @@
 // Bitmask utilities: token-id list -> bitmask, per-request density statistics,
-// and top-1 key decoding.
+// the device route selector, and top-1 key decoding.
 #include "gsp_common.cuh"
 #include "gsp_internal.h"
 
@@ -86,6 +86,74 @@ __global__ void active_tile_count_kernel(const uint32_t* __restrict__ mask, int6
   if ((threadIdx.x & 31) == 0 && active) atomicAdd(active_tiles, active);
 }
 
+constexpr int kRouteTiles = 8;      // 128-row tiles per selector block
+constexpr int kRouteThreads = 256;  // 32 request groups x 8 tiles
+
+// Device route selector: each block ORs and counts the mask words of
+// kRouteTiles tiles over every request (thread: tile tid % 8, requests
+// tid / 8, +32, ...: a warp reads 4 requests x 128 contiguous bytes), adds its
+// legal tokens and active tiles to the workspace counters; the last block to
+// arrive applies the cost model, publishes the route and returns the counters
+// to zero. One block per 8 tiles spreads the mask read over every SM.
+__global__ void __launch_bounds__(kRouteThreads) route_select_kernel(const RouteSelectParams p) {
+  __shared__ uint32_t s_act[kRouteThreads / 32][kRouteTiles];
+  __shared__ unsigned int s_legal[kRouteThreads / 32];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lt = tid % kRouteTiles, grp = tid / kRouteTiles;
+  constexpr int kGroups = kRouteThreads / kRouteTiles;
+  const int t = blockIdx.x * kRouteTiles + lt;
+  uint32_t any = 0u;
+  unsigned int legal = 0u;
+  if (t < p.ntiles) {
+#pragma unroll 2
+    for (int b = grp; b < p.batch; b += kGroups) {
+      const uint32_t* row = p.mask + (int64_t)b * p.mask_stride;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int w = t * 4 + j;
+        if (w < p.nw) {
+          const uint32_t x = tail_clip(__ldg(row + w), w, p.vocab);
+          any |= x;
+          legal += __popc(x);
+        }
+      }
+    }
+  }
+  // a warp holds 4 request groups of the same 8 tiles: OR them by tile
+  any |= __shfl_xor_sync(FULL_MASK, any, 8);
+  any |= __shfl_xor_sync(FULL_MASK, any, 16);
+  legal = __reduce_add_sync(FULL_MASK, legal);
+  if (lane < kRouteTiles) s_act[warp][lane] = any;
+  if (lane == 0) s_legal[warp] = legal;
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long sum = 0;
+    for (int i = 0; i < kRouteThreads / 32; ++i) sum += s_legal[i];
+    unsigned int act = 0;
+    for (int j = 0; j < kRouteTiles; ++j) {
+      uint32_t a = 0u;
+      for (int i = 0; i < kRouteThreads / 32; ++i) a |= s_act[i][j];
+      act += a != 0u;
+    }
+    if (sum) atomicAdd(p.legal, sum);
+    if (act) atomicAdd(p.active, act);
+    __threadfence();
+    s_last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last || tid != 0) return;
+  __threadfence();
+  const unsigned long long legal_total = atomicExch(p.legal, 0ull);
+  const unsigned int active = atomicExch(p.active, 0u);
+  atomicExch(p.ticket, 0u);
+  const int route = choose_route_by_cost(p.batch, p.vocab, p.hidden_dim, p.elem_bytes, (long long)legal_total,
+                                         (long long)active, p.cost);
+  if (p.has_handle) cudaGraphSetConditional(p.handle, (unsigned int)route);
+  if (p.route_out) *p.route_out = route;
+  if (p.route_word) *p.route_word = route;
+}
+
 __global__ void top1_from_keys_kernel(const int64_t* __restrict__ keys, int batch,
                                       float* top_value, int64_t* top_index) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -141,6 +209,12 @@ cudaError_t launch_mask_stats(const uint32_t* mask, int64_t stride, int batch, i
     if (err != cudaSuccess) return err;
   }
   return cudaSuccess;
+}
+
+cudaError_t launch_route_select(const RouteSelectParams& p, cudaStream_t stream) {
+  const int blocks = (p.ntiles + kRouteTiles - 1) / kRouteTiles;
+  route_select_kernel<<<blocks, kRouteThreads, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_top1_from_keys(const int64_t* keys, int batch, float* top_value,

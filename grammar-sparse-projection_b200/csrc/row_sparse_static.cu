@@ -83,7 +83,7 @@ extern "C" int32_t gsp_row_sparse_logits_static(const void* hidden, int64_t hidd
   }
   if (batch >= 1) {
     // ticket, error word and this call's keys must start at zero
-    err = cudaMemsetAsync(scratch, 0, 16 + 8 * (size_t)batch, static_cast<cudaStream_t>(stream));
+    err = cudaMemsetAsync(scratch, 0, kKeysOffset + 8 * (size_t)batch, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) {
       return record_error(GSP_ERR_CUDA, "gsp_row_sparse_logits_static: clearing the static scratch failed: %s",
                           cudaGetErrorString(err));

@@ -41,6 +41,13 @@ _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
 _sz = ctypes.c_size_t
 
+class RouteCost(ctypes.Structure):
+    """gsp_route_cost: the device route selector's cost model (us, GB/s)."""
+    _fields_ = [(name, ctypes.c_double) for name in (
+        "hbm_gbs", "row_sparse_fixed_us", "block_floor_us", "block_fixed_us", "block_gbs",
+        "dense_fixed_us", "dense_gbs", "group_split_fixed_us")]
+
+
 _PROJECTION_ARGS = [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
                     _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]
 
@@ -68,6 +75,13 @@ SIGNATURES = {
     "gsp_peer_exchange_free": ([_vp], _i32),
     "gsp_vocab_parallel_logits": ([_i32] + _PROJECTION_ARGS[:-1] + [ctypes.POINTER(_vp), _i32, _i32, _i32, _i64,
                                                                _vp], _i32),
+    "gsp_default_route_cost": ([ctypes.POINTER(RouteCost)], None),
+    "gsp_choose_route": ([_i32, _i32, _i32, _i32, _i64, _i64, ctypes.POINTER(RouteCost)], _i32),
+    "gsp_adaptive_logits": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _vp,
+                             ctypes.POINTER(RouteCost), _vp, ctypes.POINTER(_i32), _vp, _sz, _vp], _i32),
+    "gsp_group_plan_words": ([_i32], _sz),
+    "gsp_group_plan": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(RouteCost), _vp, _vp], _i32),
+    "gsp_gather_rows": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp], _i32),
 }
 
 ROUTE_CODES = {"row-sparse": 0, "block-sparse": 1, "dense-mask": 2}
@@ -350,3 +364,90 @@ def top1_from_keys(keys: torch.Tensor, top_value=None, top_index=None) -> None:
     status = load().gsp_top1_from_keys(_ptr(keys), keys.numel(), _ptr(top_value), _ptr(top_index),
                                        _stream(keys.device))
     _check(status, "gsp_top1_from_keys")
+
+
+# ---------------------------------------------------------------------------
+# device-side route choice
+# ---------------------------------------------------------------------------
+def route_cost(cost: dict | None) -> RouteCost | None:
+    """RouteCost from a dict of gsp_route_cost fields (missing fields take the
+    library defaults); None stays None (the library's B200 defaults)."""
+    if cost is None:
+        return None
+    c = RouteCost()
+    load().gsp_default_route_cost(ctypes.byref(c))
+    for name, value in cost.items():
+        if name not in dict(RouteCost._fields_):
+            raise ValueError(f"unknown route cost field {name!r}")
+        setattr(c, name, float(value))
+    return c
+
+
+def default_route_cost() -> dict:
+    """The library's built-in B200 route cost model (gsp_default_route_cost)."""
+    c = RouteCost()
+    load().gsp_default_route_cost(ctypes.byref(c))
+    return {name: getattr(c, name) for name, _ in RouteCost._fields_}
+
+
+def choose_route_code(batch: int, vocab: int, hidden_dim: int, elem_bytes: int, legal_total: int,
+                      active_tiles: int, cost: dict | None = None) -> int:
+    """The library's route choice for given statistics (gsp_choose_route, host)."""
+    c = route_cost(cost)
+    status = load().gsp_choose_route(batch, vocab, hidden_dim, elem_bytes, legal_total, active_tiles,
+                                     None if c is None else ctypes.byref(c))
+    if status < 0:
+        _check(status, "gsp_choose_route")
+    return status
+
+
+def adaptive(hidden, weight, mask, logits=None, top_value=None, top_index=None, route_out=None,
+             cost: dict | None = None) -> int:
+    """gsp_adaptive_logits: route chosen on the device. Returns the route code
+    (eager calls) or -1 (stream being captured: a conditional node chooses at
+    every replay; route_out, an int32 CUDA tensor, then holds it)."""
+    _require_cuda(hidden, weight, mask, logits)
+    lib = load()
+    batch, hdim = hidden.shape
+    vocab = weight.shape[0]
+    ws = workspace(hidden.device, batch, vocab)
+    c = route_cost(cost)
+    host_route = ctypes.c_int32(-1)
+    status = lib.gsp_adaptive_logits(
+        _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0), _ptr(mask),
+        0 if mask is None else mask.stride(0), batch, vocab, hdim, dtype_code(hidden.dtype),
+        _ptr(logits), 0 if logits is None else logits.stride(0), _ptr(top_value), _ptr(top_index),
+        None if c is None else ctypes.byref(c), _ptr(route_out), ctypes.byref(host_route),
+        _ptr(ws), ws.numel(), _stream(hidden.device))
+    _check(status, "gsp_adaptive_logits")
+    return host_route.value
+
+
+# ---------------------------------------------------------------------------
+# lane grouping by density class
+# ---------------------------------------------------------------------------
+GROUP_PLAN_HEADER = 16
+GROUP_MAX_BATCH = 256
+
+
+def group_plan(mask, vocab: int, hidden_dim: int, elem_bytes: int, with_logits: bool, plan,
+               cost: dict | None = None) -> None:
+    """gsp_group_plan into `plan` (CUDA int32, gsp_group_plan_words(batch))."""
+    _require_cuda(mask, plan)
+    c = route_cost(cost)
+    batch = mask.shape[0]
+    status = load().gsp_group_plan(_ptr(mask), mask.stride(0), batch, vocab, hidden_dim, elem_bytes,
+                                   1 if with_logits else 0, None if c is None else ctypes.byref(c), _ptr(plan),
+                                   _stream(mask.device))
+    _check(status, "gsp_group_plan")
+
+
+def gather_rows(src, rows, dst, n: int | None = None) -> None:
+    """dst[i] = src[rows[i]] for i < n (rows: CUDA int32; 2-D src/dst, or 1-D
+    for one element per row)."""
+    _require_cuda(src, rows, dst)
+    n = rows.numel() if n is None else n
+    row_bytes = (src.shape[1] if src.ndim == 2 else 1) * src.element_size()
+    status = load().gsp_gather_rows(_ptr(src), src.stride(0) * src.element_size(), _ptr(rows), n, row_bytes,
+                                    _ptr(dst), dst.stride(0) * dst.element_size(), _stream(src.device))
+    _check(status, "gsp_gather_rows")

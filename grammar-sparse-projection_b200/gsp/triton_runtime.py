@@ -46,6 +46,10 @@ __all__ = [
     "mask_stats",
     "choose_route",
     "ROUTES",
+    "HeadResult",
+    "grammar_head",
+    "GroupedResult",
+    "grouped_grammar_logits",
 ]
 
 ROUTES = ("row-sparse", "block-sparse", "dense-mask")
@@ -255,6 +259,7 @@ B200_COST = {
     "block_gbs": 3800.0,           # effective rate over the active tiles
     "dense_fixed_us": 5.0,
     "dense_gbs": 6000.0,
+    "group_split_fixed_us": 10.0,  # lane-group split: row gathers, second route launch, un-permute
 }
 
 
@@ -314,8 +319,29 @@ def adaptive_grammar_logits(
     full_word_fraction (gsp/triton_runtime.py:324-353), so routes match the
     reference for the same inputs. policy="b200" measures the mask on the
     device (exact legal counts and active tiles) and applies choose_route.
+    policy="device" lets the library's route selector kernel do both on the
+    device (gsp_adaptive_logits; the same cost model), reading back only the
+    chosen route (under CUDA-graph capture use grammar_head instead, whose
+    route stays on the device). policy="grouped" also considers splitting the
+    batch into two lane groups on different routes (grouped_grammar_logits);
+    a split reports its routes joined by "+", e.g. "row-sparse+block-sparse".
     """
     batch = 1 if hidden.ndim == 1 else hidden.shape[0]
+    if policy == "grouped":
+        if full_word_fraction is not None and len(full_word_fraction) != batch:
+            raise ValueError("full_word_fraction length must equal batch")
+        _, _, squeeze, _, _ = _sparse_inputs(hidden, weight, bitmask_gpu)
+        res = grouped_grammar_logits(hidden, weight, bitmask_gpu)
+        return (res.logits[0] if squeeze else res.logits), "+".join(res.plan["routes"])
+    if policy == "device":
+        if full_word_fraction is not None and len(full_word_fraction) != batch:
+            raise ValueError("full_word_fraction length must equal batch")
+        hidden_2d, mask_2d, squeeze, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
+        out = torch.empty((batch, vocab), device=hidden.device, dtype=hidden.dtype)
+        code = _native.adaptive(hidden_2d, weight, mask_2d, logits=out)
+        if code < 0:
+            raise ValueError("policy='device' reads the route back; under CUDA-graph capture use grammar_head")
+        return (out[0] if squeeze else out), ROUTES[code]
     if policy == "reference":
         route = _reference_route(batch, full_word_fraction, dense_full_word_threshold)
     elif policy == "b200":
@@ -373,6 +399,106 @@ def grammar_logits_with_top1(
     top_index = torch.empty(batch, device=dev, dtype=torch.int64)
     fn(hidden_2d, weight, mask_2d, logits=logits, top_value=top_value, top_index=top_index)
     return logits, top_value, top_index
+
+
+class HeadResult(NamedTuple):
+    logits: torch.Tensor | None  # [B, V] masked logits (None when not asked for)
+    top_value: torch.Tensor      # float32 [B]: greedy top-1 logit
+    top_index: torch.Tensor      # int64 [B]: greedy top-1 token
+    route: torch.Tensor          # int32 [1] on the device: index into ROUTES
+
+
+def grammar_head(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torch.Tensor, *,
+                 return_logits: bool = True, cost: dict | None = None,
+                 out: HeadResult | None = None) -> HeadResult:
+    """The whole grammar-conditioned head with the route chosen on the device.
+
+    A selector kernel counts the batch's legal tokens and active 128-row tiles
+    and applies the B200 cost model (choose_route's, with `cost` overriding
+    fields of B200_COST); the chosen route computes the masked logits and
+    fused greedy top-1. Nothing waits on the host when the call is captured
+    in a CUDA graph (torch.cuda.graph): the capture holds a conditional node
+    whose branches are the three routes, and each replay runs the one the
+    selector picks for that replay's mask. Eager calls read the 4-byte route
+    back. `out` reuses output tensors (for graph capture: allocate them before
+    capturing). Warm up once outside capture on the capturing stream.
+    """
+    hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
+    dev = hidden.device
+    if out is None:
+        out = HeadResult(
+            torch.empty((batch, vocab), device=dev, dtype=hidden.dtype) if return_logits else None,
+            torch.empty(batch, device=dev, dtype=torch.float32),
+            torch.empty(batch, device=dev, dtype=torch.int64),
+            torch.zeros(1, device=dev, dtype=torch.int32))
+    _native.adaptive(hidden_2d, weight, mask_2d, logits=out.logits, top_value=out.top_value,
+                     top_index=out.top_index, route_out=out.route, cost=cost)
+    return out
+
+
+class GroupedResult(NamedTuple):
+    logits: torch.Tensor | None  # [B, V] in the caller's request order
+    top_value: torch.Tensor      # float32 [B]
+    top_index: torch.Tensor      # int64 [B]
+    plan: dict                   # split, routes, order and the modelled times
+
+
+_ROUTE_FNS = {0: "row_sparse", 1: "block_gemm", 2: "dense_masked"}
+
+
+def grouped_grammar_logits(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torch.Tensor, *,
+                           return_logits: bool = True, cost: dict | None = None) -> GroupedResult:
+    """Masked logits and greedy top-1 with the batch split into two lane
+    groups when that is cheaper (the reference's proposed lane grouping by
+    density class, paper/draft.md:264-270).
+
+    gsp_group_plan profiles every request on the device, orders the requests
+    by the fill of their active 128-row tiles (scattered lanes first) and
+    costs every split "first k | rest", each group on its cheapest route,
+    against the best single route. The plan (a few hundred int32) is read
+    back; a split permutes the hidden and mask rows into group order, runs
+    the two routes and permutes the outputs back. Results equal the chosen
+    routes' own (bit for bit); at most GSP_GROUP_MAX_BATCH (256) requests.
+    """
+    hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
+    if batch > _native.GROUP_MAX_BATCH:
+        raise ValueError(f"grouped_grammar_logits takes at most {_native.GROUP_MAX_BATCH} requests")
+    dev = hidden.device
+    plan_dev = torch.empty(_native.GROUP_PLAN_HEADER + 6 * batch, dtype=torch.int32, device=dev)
+    _native.group_plan(mask_2d, vocab, weight.shape[1], weight.element_size(), return_logits, plan_dev, cost)
+    plan_host = plan_dev[:_native.GROUP_PLAN_HEADER + batch].cpu()
+    hdr = plan_host[:8].tolist()
+    k, route_a, route_b, single = hdr[0], hdr[1], hdr[2], hdr[3]
+    info = {"split": k, "single_route": ROUTES[single], "single_us": hdr[4] / 1e3,
+            "split_us": hdr[5] / 1e3 if hdr[5] >= 0 else None,
+            "order": plan_host[_native.GROUP_PLAN_HEADER:].tolist()}
+    logits = torch.empty((batch, vocab), device=dev, dtype=hidden.dtype) if return_logits else None
+    top_value = torch.empty(batch, device=dev, dtype=torch.float32)
+    top_index = torch.empty(batch, device=dev, dtype=torch.int64)
+    if k == 0:
+        info["routes"] = (ROUTES[single],)
+        getattr(_native, _ROUTE_FNS[single])(hidden_2d, weight, mask_2d, logits=logits, top_value=top_value,
+                                             top_index=top_index)
+        return GroupedResult(logits, top_value, top_index, info)
+    info["routes"] = (ROUTES[route_a], ROUTES[route_b])
+    order = plan_dev[_native.GROUP_PLAN_HEADER:_native.GROUP_PLAN_HEADER + batch]
+    inverse = plan_dev[_native.GROUP_PLAN_HEADER + batch:_native.GROUP_PLAN_HEADER + 2 * batch]
+    h_p = torch.empty_like(hidden_2d)
+    m_p = torch.empty((batch, mask_2d.shape[1]), dtype=torch.int32, device=dev)
+    _native.gather_rows(hidden_2d, order, h_p)
+    _native.gather_rows(mask_2d, order, m_p)
+    lg_p = torch.empty((batch, vocab), device=dev, dtype=hidden.dtype) if return_logits else None
+    tv_p = torch.empty(batch, device=dev, dtype=torch.float32)
+    ti_p = torch.empty(batch, device=dev, dtype=torch.int64)
+    for lo, hi, route in ((0, k, route_a), (k, batch, route_b)):
+        getattr(_native, _ROUTE_FNS[route])(h_p[lo:hi], weight, m_p[lo:hi],
+                                            logits=None if lg_p is None else lg_p[lo:hi],
+                                            top_value=tv_p[lo:hi], top_index=ti_p[lo:hi])
+    if logits is not None:
+        _native.gather_rows(lg_p, inverse, logits)
+    _native.gather_rows(tv_p, inverse, top_value)
+    _native.gather_rows(ti_p, inverse, top_index)
+    return GroupedResult(logits, top_value, top_index, info)
 
 
 class SampleResult(NamedTuple):

@@ -271,6 +271,90 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
                                   int32_t rank, int32_t world_size, int32_t max_batch,
                                   int64_t total_vocab, void* stream);
 
+/* ---- Device-side route choice (adaptive_grammar_logits without a host
+ * round trip) ----------------------------------------------------------------
+ * Route cost model (the reference's dispatcher, gsp/triton_runtime.py:324-353,
+ * chooses from a host-side full-word fraction; this model costs each route as
+ * a fixed latency plus its bytes at that kernel's measured B200 rate):
+ *   row   = row_sparse_fixed_us + (legal_total * H * e + B * V * e) / (hbm_gbs * 1e3)
+ *   block = max(block_floor_us, block_fixed_us + min(128 * active_tiles, V) * H * e / (block_gbs * 1e3))
+ *   dense = dense_fixed_us + V * H * e / (dense_gbs * 1e3)
+ * (us; e = element bytes). The cheapest wins; on equal cost block-sparse,
+ * then dense-mask, then row-sparse. Batch 1 is always row-sparse.
+ * gsp_default_route_cost fills the B200 calibration; gsp_choose_route applies
+ * the model on the host (the device selector runs the same code).
+ */
+typedef struct gsp_route_cost {
+  double hbm_gbs;
+  double row_sparse_fixed_us;
+  double block_floor_us;
+  double block_fixed_us;
+  double block_gbs;
+  double dense_fixed_us;
+  double dense_gbs;
+  double group_split_fixed_us; /* lane-group split overhead (gsp_group_plan) */
+} gsp_route_cost;
+
+void gsp_default_route_cost(gsp_route_cost* cost);
+int32_t gsp_choose_route(int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t elem_bytes,
+                         int64_t legal_total, int64_t active_tiles, const gsp_route_cost* cost);
+
+/* Masked logits and fused top-1 with the route chosen ON THE DEVICE from the
+ * mask: one selector kernel counts the batch's legal tokens and active
+ * 128-row tiles, applies the cost model (cost NULL = defaults) and picks
+ * GSP_ROUTE_ROW_SPARSE / _BLOCK_SPARSE / _DENSE_MASK.
+ *  - Stream being captured into a CUDA graph: the call adds the selector
+ *    kernel and a SWITCH conditional node whose three bodies hold the three
+ *    routes' launches; the selector sets the switch with
+ *    cudaGraphSetConditional, so every replay runs only the chosen route and
+ *    the host never waits. Body launches are recorded from this call's
+ *    pointers. Restrictions of conditional nodes apply to the enclosing graph
+ *    (it cannot be cloned or nested as a child graph). Run each route's first
+ *    call (or this call once) outside capture so that kernel attributes are
+ *    set.
+ *  - Otherwise (eager): the selector runs, the route is read back (one 4-byte
+ *    device-to-host copy and a stream synchronisation) and the chosen route
+ *    is launched.
+ * route_out (device int32, optional) receives the route of each call;
+ * route_host (host, optional) receives it in eager mode and -1 under
+ * capture. bitmask is required; batch >= 1; the workspace must hold
+ * gsp_workspace_bytes(batch, vocab) bytes. Extension beyond the reference.
+ */
+int32_t gsp_adaptive_logits(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                            int64_t weight_row_stride, const int32_t* bitmask,
+                            int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                            int32_t hidden_dim, int32_t dtype, void* logits,
+                            int64_t logits_row_stride, float* top_value, int64_t* top_index,
+                            const gsp_route_cost* cost, int32_t* route_out, int32_t* route_host,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Lane grouping by density class -----------------------------------------
+ * The reference's roadmap (paper/draft.md:264-270) proposes grouping requests
+ * so that permissive lanes do not activate tiles for constrained ones.
+ * gsp_group_plan profiles every request on the device (legal tokens, active
+ * 128-row tiles), orders the requests by the fill of their active tiles
+ * (legal / (128 x tiles); scattered lanes first), finds for every tile the
+ * first and last position in that order of a request that touches it, and
+ * costs every split "first k positions | the rest" with each group on its
+ * cheapest route (the cost model above, plus group_split_fixed_us and, with
+ * logits, the un-permute of the logits rows at hbm_gbs) against the best
+ * single route. plan: device int32 [gsp_group_plan_words(batch)], layout
+ *   [0] k (0: no split), [1] route of positions [0, k), [2] route of [k, B),
+ *   [3] best single route, [4] its modelled ns, [5] the split's modelled ns
+ *   (-1: none), [6..16) reserved, then order[B] (position -> request) and
+ *   inverse[B] (request -> position), then per-request and per-position
+ *   statistics. batch <= GSP_GROUP_MAX_BATCH. No workspace; asynchronous.
+ * gsp_gather_rows copies dst row i = src row rows[i] (device int32 rows) for
+ * permuting hidden states, masks, logits and top-1 rows.
+ */
+#define GSP_GROUP_MAX_BATCH 256
+size_t gsp_group_plan_words(int32_t batch);
+int32_t gsp_group_plan(const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                       int32_t hidden_dim, int32_t elem_bytes, int32_t with_logits, const gsp_route_cost* cost,
+                       int32_t* plan, void* stream);
+int32_t gsp_gather_rows(const void* src, int64_t src_row_stride_bytes, const int32_t* rows, int32_t n,
+                        int64_t row_bytes, void* dst, int64_t dst_row_stride_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

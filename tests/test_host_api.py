@@ -19,7 +19,7 @@ HEADER = os.path.join(REPO, "include", "gsp_b200.h")
 
 def declared_symbols():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int32_t|size_t|const char\s*\*)\s*(gsp_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int32_t|size_t|void|const char\s*\*)\s*(gsp_\w+)\s*\(", text, re.M)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -153,3 +153,50 @@ def test_b200_cost_model_prefers_the_cheapest_bytes():
     assert tr.choose_route(32, V, H, e, [1242] * 32, 700) == "row-sparse"
     # everything legal: dense
     assert tr.choose_route(8, V, H, e, [V] * 8, 1940) == "dense-mask"
+
+
+def test_route_cost_defaults_match_python_model():
+    """The device selector's built-in cost model is the Python B200_COST."""
+    assert _native.default_route_cost() == tr.B200_COST
+
+
+STEERED_COST = {"row_sparse_fixed_us": 0.5, "block_floor_us": 0.0, "block_fixed_us": 1.0, "dense_fixed_us": 0.0}
+
+
+def test_native_route_choice_matches_python_model():
+    """gsp_choose_route (the code the device selector runs) picks the route
+    choose_route picks, on random statistics and on exact cost ties."""
+    import numpy as np
+    rng = np.random.default_rng(0)
+    for cost in (None, STEERED_COST):
+        for _ in range(1500):
+            batch = int(rng.integers(1, 300))
+            vocab = int(rng.integers(1000, 300000))
+            hidden = int(rng.integers(64, 8192))
+            ntiles = (vocab + 127) // 128
+            legal = [int(x) for x in rng.integers(0, vocab + 1, size=batch) * rng.random(batch) ** 4]
+            active = int(rng.integers(0, ntiles + 1))
+            got = _native.choose_route_code(batch, vocab, hidden, 2, sum(legal), active, cost)
+            assert tr.ROUTES[got] == tr.choose_route(batch, vocab, hidden, 2, legal, active, cost), \
+                (batch, vocab, hidden, sum(legal), active, cost)
+    # equal block and dense costs: block first, as in choose_route's tuple order
+    tie = {"block_floor_us": 0.0, "block_fixed_us": 5.0, "block_gbs": 6000.0, "dense_fixed_us": 5.0,
+           "dense_gbs": 6000.0, "row_sparse_fixed_us": 1e9}
+    assert tr.choose_route(8, 4096, 256, 2, [4096] * 8, 32, tie) == "block-sparse"
+    assert _native.choose_route_code(8, 4096, 256, 2, 8 * 4096, 32, tie) == 1
+    assert _native.choose_route_code(1, 4096, 256, 2, 10, 1, tie) == 0  # batch 1: row-sparse
+
+
+def test_adaptive_entry_validation():
+    lib = _native.load()
+    route = ctypes.c_int32(7)
+    args = [FAKE, 8, FAKE, 8, None, 0, 2, 64, 8, 0, None, 64, None, None, None, None, ctypes.byref(route), None, 0,
+            None]
+    assert lib.gsp_adaptive_logits(*args) == -1  # bitmask required
+    assert route.value == -1 and b"bitmask" in lib.gsp_last_error()
+    args[4] = FAKE
+    assert lib.gsp_adaptive_logits(*args) == -3  # workspace required
+    args[9] = 5
+    assert lib.gsp_adaptive_logits(*args) == -2  # dtype
+    with pytest.raises(ValueError):
+        _native.route_cost({"no_such_field": 1.0})

@@ -66,7 +66,7 @@ def parse_args():
     ap.add_argument("--sweep-steps", type=int, default=100)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-vp", action="store_true", help="skip the vocabulary-parallel head section")
-    ap.add_argument("--only", choices=("batched", "mixed", "vp", "sampler", "graphed"), default=None,
+    ap.add_argument("--only", choices=("batched", "mixed", "vp", "sampler", "graphed", "groups"), default=None,
                     help="run one extra section alone (small; for profiling)")
     ap.add_argument("--batch", type=int, default=32, help="batch of --only batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -265,6 +265,10 @@ def main():
             g = torch.Generator(device=dev).manual_seed(1234)
             weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(4)]
             res = sampler_section(dev, weights, steps=max(args.steps, 1), batches=(1, args.batch))
+        elif args.only == "groups":
+            g = torch.Generator(device=dev).manual_seed(1234)
+            weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(2)]
+            res = lane_groups_section(dev, weights, steps=max(args.steps, 1))
         elif args.only == "graphed":
             res = graphed_head_section(dev, steps=max(args.steps, 1))
         else:
@@ -445,6 +449,7 @@ def main():
     mixed = None
     sampler_res = None
     graphed = None
+    groups = None
     same_gpu_dense = None
     cpu_base = None
     if world == 1 and not args.no_sweep:
@@ -467,6 +472,7 @@ def main():
         mixed = mixed_section(dev, peak)
         sampler_res = sampler_section(dev, weights[:8])
         graphed = graphed_head_section(dev)
+        groups = lane_groups_section(dev, weights[:8])
     vp_head = None if args.no_vp else vocab_parallel_section(dev, world, rank, peak)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         w_cpu = weight.cpu().numpy()
@@ -501,6 +507,7 @@ def main():
             "vocab_parallel_head": vp_head,
             "sampler": sampler_res,
             "graphed_head": graphed,
+            "lane_groups": groups,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -882,6 +889,59 @@ def graphed_head_section(dev, steps=20):
                     "staged_copy_then_head_us": staged_us, "mask_bytes": int(mask_np.nbytes),
                     "host_b200_policy": eager["b200"], "eager_device_policy": eager["device"]})
     del head, w
+    return out
+
+
+def lane_groups_section(dev, weights, steps=10):
+    """Lane grouping (grouped_grammar_logits) at V=248,320, H=2,048 fp16, batch
+    32: `n_clustered` requests with 20% of the vocabulary in one run (the same
+    region) batched with scattered requests (0.5% uniform), and the uniform
+    batch of the batched section (0.5% in <= 16 runs) where a split does not
+    pay. Grouped path (plan, read-back, gathers, two routes, un-permute) and
+    each single route, wall clock per call with the result synchronised;
+    greedy top-1 only (no logits), weight copy i % len(weights)."""
+    import time
+    from gsp import _native, triton_runtime as tr
+    from gsp import workloads as wl
+    batch = 32
+    out = []
+    cases = []
+    for n_cl in (4, 8):
+        rng = np.random.default_rng(900 + n_cl)
+        sc = wl.make_batch_mask(rng, batch - n_cl, VOCAB, [1242] * (batch - n_cl))
+        cl = np.repeat(wl.make_batch_mask(rng, 1, VOCAB, [VOCAB // 5], clustered=True, max_runs=1), n_cl, axis=0)
+        m = np.concatenate([sc, cl])
+        cases.append((f"{batch - n_cl} scattered 0.5% + {n_cl} clustered 20%", m[rng.permutation(batch)]))
+    rng = np.random.default_rng(332)
+    cases.append(("32 x 0.5% in <= 16 runs", wl.make_batch_mask(rng, batch, VOCAB, [1242] * batch, clustered=True,
+                                                                 max_runs=16)))
+    h = torch.randn(batch, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(3)).half()
+    tv = torch.empty(batch, device=dev)
+    ti = torch.empty(batch, device=dev, dtype=torch.int64)
+
+    def wall_us(fn):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(steps):
+            fn(i)
+            torch.cuda.synchronize()
+        return (time.perf_counter() - t0) * 1e6 / steps
+
+    for name, mask_np in cases:
+        md = torch.from_numpy(mask_np).to(dev)
+        res = tr.grouped_grammar_logits(h, weights[0], md, return_logits=False)
+        t = {"grouped": wall_us(lambda i: tr.grouped_grammar_logits(h, weights[i % len(weights)], md,
+                                                                    return_logits=False))}
+        for route, fn in (("row-sparse", _native.row_sparse), ("block-sparse", _native.block_gemm),
+                          ("dense-mask", _native.dense_masked)):
+            t[route] = wall_us(lambda i, fn=fn: fn(h, weights[i % len(weights)], md, top_value=tv, top_index=ti))
+        best_single = min(("row-sparse", "block-sparse", "dense-mask"), key=lambda r: t[r])
+        out.append({"case": name, "plan_routes": list(res.plan["routes"]), "split": res.plan["split"],
+                    "modelled_us": {"single": res.plan["single_us"], "split": res.plan["split_us"]},
+                    "us_per_call": t, "best_single_route": best_single,
+                    "speedup_vs_best_single": t[best_single] / t["grouped"]})
     return out
 
 

@@ -665,4 +665,106 @@ int32_t gsp_gather_rows(const void* src, int64_t src_row_stride_bytes, const int
                                         static_cast<cudaStream_t>(stream)), fn);
 }
 
+struct GroupedScratch {
+  int32_t* plan;
+  void* hidden;
+  uint32_t* mask;
+  void* logits;
+  float* top_value;
+  int64_t* top_index;
+  size_t total;
+};
+
+static GroupedScratch carve_grouped(void* base, int batch, int vocab, int hidden_dim, bool with_logits) {
+  char* p = static_cast<char*>(base);
+  GroupedScratch g;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t at = off; off += align256(bytes); return p ? p + at : nullptr; };
+  g.plan = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * ((size_t)kPlanHeader + 6 * (size_t)batch)));
+  g.hidden = take(2 * (size_t)batch * hidden_dim);
+  g.mask = reinterpret_cast<uint32_t*>(take(4 * (size_t)batch * ((vocab + 31) / 32)));
+  g.logits = with_logits ? take(2 * (size_t)batch * vocab) : nullptr;
+  g.top_value = reinterpret_cast<float*>(take(4 * (size_t)batch));
+  g.top_index = reinterpret_cast<int64_t*>(take(8 * (size_t)batch));
+  g.total = off;
+  return g;
+}
+
+size_t gsp_grouped_scratch_bytes(int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t with_logits) {
+  if (batch < 1 || vocab < 1 || hidden_dim < 1) return 0;
+  return carve_grouped(nullptr, batch, vocab, hidden_dim, with_logits != 0).total;
+}
+
+int32_t gsp_grouped_logits(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                           int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride,
+                           int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype, void* logits,
+                           int64_t logits_row_stride, float* top_value, int64_t* top_index,
+                           const gsp_route_cost* cost, int32_t* plan_header, void* scratch, size_t scratch_bytes,
+                           void* workspace, size_t workspace_bytes_, void* stream) {
+  const char* fn = "gsp_grouped_logits";
+  int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                   bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
+  if (st != GSP_OK) return st;
+  if (!bitmask) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask is required", fn);
+  if (batch > kGroupMaxBatch) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: batch %d > %d", fn, batch, kGroupMaxBatch);
+  st = check_workspace(fn, true, workspace, workspace_bytes_, batch, vocab);
+  if (st != GSP_OK) return st;
+  const GroupedScratch g = carve_grouped(scratch, batch, vocab, hidden_dim, logits != nullptr);
+  if (!scratch || (reinterpret_cast<uintptr_t>(scratch) & 255) != 0 || scratch_bytes < g.total)
+    return fail(GSP_ERR_WORKSPACE, "%s: scratch must be 256-byte aligned with %zu bytes", fn, g.total);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if ((err = cudaStreamIsCapturing(s, &cs)) != cudaSuccess) return cuda_status(err, fn);
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(GSP_ERR_UNSUPPORTED, "%s: reads its plan back, so it cannot be captured in a graph", fn);
+  // plan
+  const int32_t with_logits = logits != nullptr;
+  st = gsp_group_plan(bitmask, bitmask_row_stride, batch, vocab, hidden_dim, 2, with_logits, cost, g.plan, stream);
+  if (st != GSP_OK) return st;
+  static thread_local int32_t* hdr = nullptr;  // pinned, one per host thread
+  if (!hdr && (err = cudaMallocHost(&hdr, 8 * sizeof(int32_t))) != cudaSuccess) {
+    hdr = nullptr;
+    return cuda_status(err, fn);
+  }
+  if ((err = cudaMemcpyAsync(hdr, g.plan, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, s)) != cudaSuccess ||
+      (err = cudaStreamSynchronize(s)) != cudaSuccess)
+    return cuda_status(err, fn);
+  if (plan_header) std::memcpy(plan_header, hdr, 8 * sizeof(int32_t));
+  const int k = hdr[0];
+  if (k <= 0 || k >= batch)  // one route on the caller's buffers
+    return route_call(fn, hdr[3], hidden, hidden_row_stride, weight, weight_row_stride, bitmask, bitmask_row_stride,
+                      batch, vocab, hidden_dim, dtype, logits, logits_row_stride, top_value, top_index, workspace,
+                      workspace_bytes_, stream);
+  // split: rows into group order, two routes, rows back
+  const int32_t* order = g.plan + kPlanHeader;
+  const int32_t* inverse = order + batch;
+  const int64_t nw = (vocab + 31) / 32;
+  const int64_t hbytes = 2 * (int64_t)hidden_dim;
+  if ((err = launch_gather_rows(hidden, 2 * hidden_row_stride, order, batch, hbytes, g.hidden, hbytes, s)) !=
+          cudaSuccess ||
+      (err = launch_gather_rows(bitmask, 4 * bitmask_row_stride, order, batch, 4 * nw, g.mask, 4 * nw, s)) !=
+          cudaSuccess)
+    return cuda_status(err, fn);
+  const int lo[2] = {0, k}, hi[2] = {k, batch}, route[2] = {hdr[1], hdr[2]};
+  for (int i = 0; i < 2; ++i) {
+    const int n = hi[i] - lo[i];
+    st = route_call(fn, route[i], static_cast<const char*>(g.hidden) + (size_t)lo[i] * hbytes, hidden_dim, weight,
+                    weight_row_stride, reinterpret_cast<const int32_t*>(g.mask + (size_t)lo[i] * nw), nw, n, vocab,
+                    hidden_dim, dtype,
+                    g.logits ? static_cast<char*>(g.logits) + (size_t)lo[i] * vocab * 2 : nullptr, vocab,
+                    g.top_value + lo[i], g.top_index + lo[i], workspace, workspace_bytes_, stream);
+    if (st != GSP_OK) return st;
+  }
+  if (logits &&
+      (err = launch_gather_rows(g.logits, 2 * (int64_t)vocab, inverse, batch, 2 * (int64_t)vocab, logits,
+                                2 * (batch > 1 ? logits_row_stride : vocab), s)) != cudaSuccess)
+    return cuda_status(err, fn);
+  if (top_value && (err = launch_gather_rows(g.top_value, 4, inverse, batch, 4, top_value, 4, s)) != cudaSuccess)
+    return cuda_status(err, fn);
+  if (top_index && (err = launch_gather_rows(g.top_index, 8, inverse, batch, 8, top_index, 8, s)) != cudaSuccess)
+    return cuda_status(err, fn);
+  return GSP_OK;
+}
+
 }  // extern "C"

@@ -112,15 +112,16 @@ __global__ void __launch_bounds__(kPlanThreads) request_profile_kernel(const Gro
   if (!s_last) return;
   __threadfence();
   // order by fill (legal / (128 tiles)), ascending; ties by request index
+  __shared__ double s_fill[kGroupMaxBatch];
   for (int b = tid; b < p.batch; b += kPlanThreads) {
     const int lb = __ldcg(v.legal + b), tb = __ldcg(v.tiles + b);
-    const double fb = tb ? (double)lb / (128.0 * tb) : -1.0;
+    s_fill[b] = tb ? (double)lb / (128.0 * tb) : -1.0;
+  }
+  __syncthreads();
+  for (int b = tid; b < p.batch; b += kPlanThreads) {
+    const double fb = s_fill[b];
     int rank = 0;
-    for (int j = 0; j < p.batch; ++j) {
-      const int lj = __ldcg(v.legal + j), tj = __ldcg(v.tiles + j);
-      const double fj = tj ? (double)lj / (128.0 * tj) : -1.0;
-      rank += (fj < fb) || (fj == fb && j < b);
-    }
+    for (int j = 0; j < p.batch; ++j) rank += (s_fill[j] < fb) || (s_fill[j] == fb && j < b);
     v.order[rank] = b;
     v.inverse[b] = rank;
   }
@@ -167,37 +168,55 @@ __global__ void __launch_bounds__(kPlanThreads) group_footprint_kernel(const Gro
   __syncthreads();
   if (tid == 0) s_last = atomicAdd(reinterpret_cast<unsigned int*>(v.hdr + 7), 1u) == gridDim.x - 1;
   __syncthreads();
-  if (!s_last || tid != 0) return;
+  if (!s_last) return;
   __threadfence();
-  // cost every split k: positions [0, k) | [k, B)
+  // cost every split k (positions [0, k) | [k, B)): prefix sums in shared
+  // memory, one thread per k, then the first k of least cost
+  __shared__ long long s_legal_pre[kGroupMaxBatch + 1];
+  __shared__ int s_amin_pre[kGroupMaxBatch + 1], s_amax_pre[kGroupMaxBatch + 1];
+  __shared__ double s_cost[kGroupMaxBatch];
+  __shared__ int s_ra[kGroupMaxBatch], s_rb[kGroupMaxBatch];
   const int B = p.batch;
-  long long legal_total = 0, active_total = 0;
-  for (int i = 0; i < B; ++i) {
-    legal_total += __ldcg(v.legal + i);
-    active_total += __ldcg(v.hist_max + i);
+  for (int i = tid; i < B; i += kPlanThreads) {
+    s_legal_pre[i + 1] = __ldcg(v.legal + __ldcg(v.order + i));
+    s_amin_pre[i + 1] = __ldcg(v.hist_min + i);
+    s_amax_pre[i + 1] = __ldcg(v.hist_max + i);
   }
+  __syncthreads();
+  if (tid == 0) {
+    s_legal_pre[0] = 0;
+    s_amin_pre[0] = s_amax_pre[0] = 0;
+    for (int i = 1; i <= B; ++i) {
+      s_legal_pre[i] += s_legal_pre[i - 1];
+      s_amin_pre[i] += s_amin_pre[i - 1];
+      s_amax_pre[i] += s_amax_pre[i - 1];
+    }
+  }
+  __syncthreads();
+  const long long legal_total = s_legal_pre[B], active_total = s_amax_pre[B];
+  const double unpermute = p.with_logits
+      ? 2.0 * (double)((long long)B * p.vocab * p.elem_bytes) / (p.cost.hbm_gbs * 1e3) : 0.0;
+  for (int k = 1 + tid; k < B; k += kPlanThreads) {
+    const long long la = s_legal_pre[k];
+    double ta, tb;
+    s_ra[k] = best_route_by_cost(k, p.vocab, p.hidden_dim, p.elem_bytes, la, s_amin_pre[k], p.cost, &ta);
+    s_rb[k] = best_route_by_cost(B - k, p.vocab, p.hidden_dim, p.elem_bytes, legal_total - la,
+                                 active_total - s_amax_pre[k], p.cost, &tb);
+    s_cost[k] = ta + tb + p.cost.group_split_fixed_us + unpermute;
+  }
+  __syncthreads();
+  if (tid != 0) return;
   double t_single;
   const int single = best_route_by_cost(B, p.vocab, p.hidden_dim, p.elem_bytes, legal_total, active_total, p.cost,
                                         &t_single);
-  const double unpermute = p.with_logits
-      ? 2.0 * (double)((long long)B * p.vocab * p.elem_bytes) / (p.cost.hbm_gbs * 1e3) : 0.0;
   double best_t = t_single;
   int best_k = 0, best_a = single, best_b = single;
-  long long legal_a = 0, active_a = 0, active_b = active_total;
   for (int k = 1; k < B; ++k) {
-    legal_a += __ldcg(v.legal + __ldcg(v.order + k - 1));
-    active_a += __ldcg(v.hist_min + k - 1);
-    active_b -= __ldcg(v.hist_max + k - 1);
-    double ta, tb;
-    const int ra = best_route_by_cost(k, p.vocab, p.hidden_dim, p.elem_bytes, legal_a, active_a, p.cost, &ta);
-    const int rb = best_route_by_cost(B - k, p.vocab, p.hidden_dim, p.elem_bytes, legal_total - legal_a, active_b,
-                                      p.cost, &tb);
-    const double tt = ta + tb + p.cost.group_split_fixed_us + unpermute;
-    if (tt < best_t) {
-      best_t = tt;
+    if (s_cost[k] < best_t) {
+      best_t = s_cost[k];
       best_k = k;
-      best_a = ra;
-      best_b = rb;
+      best_a = s_ra[k];
+      best_b = s_rb[k];
     }
   }
   v.hdr[0] = best_k;

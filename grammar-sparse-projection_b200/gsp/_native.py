@@ -82,6 +82,9 @@ SIGNATURES = {
     "gsp_group_plan_words": ([_i32], _sz),
     "gsp_group_plan": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(RouteCost), _vp, _vp], _i32),
     "gsp_gather_rows": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp], _i32),
+    "gsp_grouped_scratch_bytes": ([_i32, _i32, _i32, _i32], _sz),
+    "gsp_grouped_logits": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _vp,
+                            ctypes.POINTER(RouteCost), ctypes.POINTER(_i32), _vp, _sz, _vp, _sz, _vp], _i32),
 }
 
 ROUTE_CODES = {"row-sparse": 0, "block-sparse": 1, "dense-mask": 2}
@@ -451,3 +454,38 @@ def gather_rows(src, rows, dst, n: int | None = None) -> None:
     status = load().gsp_gather_rows(_ptr(src), src.stride(0) * src.element_size(), _ptr(rows), n, row_bytes,
                                     _ptr(dst), dst.stride(0) * dst.element_size(), _stream(src.device))
     _check(status, "gsp_gather_rows")
+
+
+_scratch: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _grouped_scratch(device: torch.device, need: int) -> torch.Tensor:
+    dev_index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (dev_index, torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        buf = _scratch.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(max(need, 2 * (0 if buf is None else buf.numel())), dtype=torch.uint8, device=device)
+            _scratch[key] = buf
+        return buf
+
+
+def grouped(hidden, weight, mask, logits=None, top_value=None, top_index=None, cost: dict | None = None) -> list[int]:
+    """gsp_grouped_logits; returns the plan header [k, route A, route B, best
+    single route, single ns, split ns, 0, 0] (waits for the plan)."""
+    _require_cuda(hidden, weight, mask, logits)
+    lib = load()
+    batch, hdim = hidden.shape
+    vocab = weight.shape[0]
+    ws = workspace(hidden.device, batch, vocab)
+    scratch = _grouped_scratch(hidden.device, int(lib.gsp_grouped_scratch_bytes(batch, vocab, hdim,
+                                                                                 1 if logits is not None else 0)))
+    c = route_cost(cost)
+    hdr = (_i32 * 8)()
+    status = lib.gsp_grouped_logits(
+        _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0), _ptr(mask), mask.stride(0),
+        batch, vocab, hdim, dtype_code(hidden.dtype), _ptr(logits), 0 if logits is None else logits.stride(0),
+        _ptr(top_value), _ptr(top_index), None if c is None else ctypes.byref(c), hdr,
+        _ptr(scratch), scratch.numel(), _ptr(ws), ws.numel(), _stream(hidden.device))
+    _check(status, "gsp_grouped_logits")
+    return list(hdr)

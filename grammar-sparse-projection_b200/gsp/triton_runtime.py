@@ -452,52 +452,28 @@ def grouped_grammar_logits(hidden: torch.Tensor, weight: torch.Tensor, bitmask_g
     groups when that is cheaper (the reference's proposed lane grouping by
     density class, paper/draft.md:264-270).
 
-    gsp_group_plan profiles every request on the device, orders the requests
-    by the fill of their active 128-row tiles (scattered lanes first) and
-    costs every split "first k | rest", each group on its cheapest route,
-    against the best single route. The plan (a few hundred int32) is read
-    back; a split permutes the hidden and mask rows into group order, runs
-    the two routes and permutes the outputs back. Results equal the chosen
-    routes' own (bit for bit); at most GSP_GROUP_MAX_BATCH (256) requests.
+    One native call (gsp_grouped_logits): the device profiles every request,
+    orders the requests by the fill of their active 128-row tiles (scattered
+    lanes first) and costs every split "first k | rest", each group on its
+    cheapest route, against the best single route; the 32-byte plan header is
+    read back; a split gathers the hidden and mask rows into group order,
+    runs the two routes and permutes logits and top-1 back. Results equal
+    the chosen routes' own (bit for bit); at most 256 requests; not
+    capturable in a CUDA graph (grammar_head is).
     """
     hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
     if batch > _native.GROUP_MAX_BATCH:
         raise ValueError(f"grouped_grammar_logits takes at most {_native.GROUP_MAX_BATCH} requests")
     dev = hidden.device
-    plan_dev = torch.empty(_native.GROUP_PLAN_HEADER + 6 * batch, dtype=torch.int32, device=dev)
-    _native.group_plan(mask_2d, vocab, weight.shape[1], weight.element_size(), return_logits, plan_dev, cost)
-    plan_host = plan_dev[:_native.GROUP_PLAN_HEADER + batch].cpu()
-    hdr = plan_host[:8].tolist()
-    k, route_a, route_b, single = hdr[0], hdr[1], hdr[2], hdr[3]
-    info = {"split": k, "single_route": ROUTES[single], "single_us": hdr[4] / 1e3,
-            "split_us": hdr[5] / 1e3 if hdr[5] >= 0 else None,
-            "order": plan_host[_native.GROUP_PLAN_HEADER:].tolist()}
     logits = torch.empty((batch, vocab), device=dev, dtype=hidden.dtype) if return_logits else None
     top_value = torch.empty(batch, device=dev, dtype=torch.float32)
     top_index = torch.empty(batch, device=dev, dtype=torch.int64)
-    if k == 0:
-        info["routes"] = (ROUTES[single],)
-        getattr(_native, _ROUTE_FNS[single])(hidden_2d, weight, mask_2d, logits=logits, top_value=top_value,
-                                             top_index=top_index)
-        return GroupedResult(logits, top_value, top_index, info)
-    info["routes"] = (ROUTES[route_a], ROUTES[route_b])
-    order = plan_dev[_native.GROUP_PLAN_HEADER:_native.GROUP_PLAN_HEADER + batch]
-    inverse = plan_dev[_native.GROUP_PLAN_HEADER + batch:_native.GROUP_PLAN_HEADER + 2 * batch]
-    h_p = torch.empty_like(hidden_2d)
-    m_p = torch.empty((batch, mask_2d.shape[1]), dtype=torch.int32, device=dev)
-    _native.gather_rows(hidden_2d, order, h_p)
-    _native.gather_rows(mask_2d, order, m_p)
-    lg_p = torch.empty((batch, vocab), device=dev, dtype=hidden.dtype) if return_logits else None
-    tv_p = torch.empty(batch, device=dev, dtype=torch.float32)
-    ti_p = torch.empty(batch, device=dev, dtype=torch.int64)
-    for lo, hi, route in ((0, k, route_a), (k, batch, route_b)):
-        getattr(_native, _ROUTE_FNS[route])(h_p[lo:hi], weight, m_p[lo:hi],
-                                            logits=None if lg_p is None else lg_p[lo:hi],
-                                            top_value=tv_p[lo:hi], top_index=ti_p[lo:hi])
-    if logits is not None:
-        _native.gather_rows(lg_p, inverse, logits)
-    _native.gather_rows(tv_p, inverse, top_value)
-    _native.gather_rows(ti_p, inverse, top_index)
+    hdr = _native.grouped(hidden_2d, weight, mask_2d, logits=logits, top_value=top_value, top_index=top_index,
+                          cost=cost)
+    k = hdr[0]
+    info = {"split": k, "single_route": ROUTES[hdr[3]], "single_us": hdr[4] / 1e3,
+            "split_us": hdr[5] / 1e3 if hdr[5] >= 0 else None,
+            "routes": (ROUTES[hdr[1]], ROUTES[hdr[2]]) if k else (ROUTES[hdr[3]],)}
     return GroupedResult(logits, top_value, top_index, info)
 
 

@@ -355,6 +355,24 @@ int32_t gsp_group_plan(const int32_t* bitmask, int64_t bitmask_row_stride, int32
 int32_t gsp_gather_rows(const void* src, int64_t src_row_stride_bytes, const int32_t* rows, int32_t n,
                         int64_t row_bytes, void* dst, int64_t dst_row_stride_bytes, void* stream);
 
+/* The whole grouped projection in one call: gsp_group_plan, a 32-byte
+ * read-back of the plan header (the call waits for it: not capturable), then
+ * either the best single route on the caller's buffers, or a split: hidden
+ * and mask rows gathered into group order, each group's route, logits and
+ * top-1 rows permuted back. Results equal the chosen routes' outputs.
+ * scratch: gsp_grouped_scratch_bytes(batch, vocab, hidden_dim, logits != NULL)
+ * bytes of device memory, 256-byte aligned (contents not preserved);
+ * workspace as for the other entries; plan_header (host int32 [8], optional)
+ * receives the plan header. batch <= GSP_GROUP_MAX_BATCH.
+ */
+size_t gsp_grouped_scratch_bytes(int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t with_logits);
+int32_t gsp_grouped_logits(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                           int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride,
+                           int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype, void* logits,
+                           int64_t logits_row_stride, float* top_value, int64_t* top_index,
+                           const gsp_route_cost* cost, int32_t* plan_header, void* scratch, size_t scratch_bytes,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

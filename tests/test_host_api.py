@@ -200,3 +200,23 @@ def test_adaptive_entry_validation():
     assert lib.gsp_adaptive_logits(*args) == -2  # dtype
     with pytest.raises(ValueError):
         _native.route_cost({"no_such_field": 1.0})
+
+
+def test_grouped_entry_validation():
+    lib = _native.load()
+    assert lib.gsp_group_plan_words(0) == 0 and lib.gsp_group_plan_words(4) == 16 + 24
+    assert lib.gsp_grouped_scratch_bytes(0, 10, 10, 1) == 0
+    with_l = lib.gsp_grouped_scratch_bytes(32, 248320, 2048, 1)
+    without = lib.gsp_grouped_scratch_bytes(32, 248320, 2048, 0)
+    assert with_l - without >= 32 * 248320 * 2 and with_l % 256 == 0
+    hdr = (ctypes.c_int32 * 8)()
+    args = [FAKE, 8, FAKE, 8, FAKE, 2, 300, 64, 8, 0, None, 64, None, None, None, hdr, FAKE, 1 << 20, FAKE, 1 << 30,
+            None]
+    assert lib.gsp_grouped_logits(*args) == -1  # batch over GSP_GROUP_MAX_BATCH
+    args[6] = 4
+    args[4] = None
+    assert lib.gsp_grouped_logits(*args) == -1 and b"bitmask" in lib.gsp_last_error()
+    assert lib.gsp_group_plan(FAKE, 2, 300, 64, 8, 2, 0, None, FAKE, None) == -1
+    assert lib.gsp_group_plan(FAKE, 2, 4, 64, 8, 2, 0, None, None, None) == -1
+    assert lib.gsp_gather_rows(FAKE, 16, FAKE, 2, 16, FAKE, 8, None) == -1  # dst stride < row bytes
+    assert lib.gsp_gather_rows(None, 16, None, 0, 16, None, 16, None) == 0  # nothing to copy

@@ -384,8 +384,12 @@ def main():
                 "what": "eager steps, 256 MiB L2-flushing write before each, events around each step"}
 
     # e2e through the C ABI with host buffers: each step's mask and hidden state
-    # sit in one pinned staging row (one host-to-device copy) and the top-1
-    # comes back as one 16-byte record (one device-to-host copy)
+    # sit in one pinned staging row, moved to the device by one copy each step;
+    # the top-1 comes back as one 16-byte record in pinned host memory. On one
+    # GPU the copy in is gsp_copy_bytes (an SM-driven copy: a copy-engine
+    # transfer's fixed latency dominates at 35 KB) and the kernel stores the
+    # record straight into pinned host memory; with more ranks, copy-engine
+    # copies both ways.
     local_words = (hi + 31) // 32 - lo // 32
     mask_bytes = local_words * 4
     mask_pad = (mask_bytes + 15) // 16 * 16
@@ -404,19 +408,23 @@ def main():
     out_value = dev_out[1:2].view(torch.float32)[:1]
     host_top = torch.empty(2, dtype=torch.int64).pin_memory()
 
+    host_index = host_top[0:1]
+    host_value = host_top[1:2].view(torch.float32)[:1]
+
     # one prepared C-ABI call per weight copy (arguments converted once)
     calls = [_native.PreparedProjection("gsp_row_sparse_logits", dev_hidden, w, dev_mask, logits=logits,
-                                        top_value=out_value, top_index=out_index) for w in weights] \
+                                        top_value=host_value, top_index=host_index) for w in weights] \
         if world == 1 else None
 
     def e2e_step(i):
-        dev_in.copy_(host_in[i % args.masks], non_blocking=True)
         if world == 1:
+            _native.copy_bytes(dev_in, host_in[i % args.masks])
             calls[i % len(calls)]()
-        else:
-            _native.vocab_parallel("row-sparse", dev_hidden, weights[i % len(weights)], dev_mask, xch.peers, rank,
-                                   xch.max_batch, VOCAB, logits=logits, top_value=out_value,
-                                   top_index=out_index, vocab_offset=lo)
+            return
+        dev_in.copy_(host_in[i % args.masks], non_blocking=True)
+        _native.vocab_parallel("row-sparse", dev_hidden, weights[i % len(weights)], dev_mask, xch.peers, rank,
+                               xch.max_batch, VOCAB, logits=logits, top_value=out_value,
+                               top_index=out_index, vocab_offset=lo)
         host_top.copy_(dev_out, non_blocking=True)
 
     for i in range(3):
@@ -424,6 +432,11 @@ def main():
     barrier()
     e2e_steps = timed(args.steps, e2e_step, 0, flush_l2=False)
     barrier()
+    if world == 1:  # the last step's record on the host equals an eager call on its inputs
+        ref_index = torch.empty(1, dtype=torch.int64, device=dev)
+        _native.row_sparse(dev_hidden, weights[(args.steps - 1) % len(weights)], dev_mask, top_index=ref_index)
+        if int(ref_index.item()) != int(host_top[0]):
+            raise RuntimeError("end-to-end step's host record disagrees with the eager call")
     e2e_total = max_over_ranks(sum(e2e_steps), world)
     e2e_value = legal_bytes / (e2e_total * 1e-6) / 1e9
     h2d = int(in_bytes)
@@ -491,9 +504,13 @@ def main():
             "config": workload_config(args),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": e2e_total / args.steps,
-                    "what": ("eager steps, events around each: one pinned host-to-device copy of the step's mask "
-                             "and hidden state, the prepared C-ABI call on weight copy i % copies, one "
-                             "device-to-host copy of the 16-byte top-1 record")},
+                    "what": (("eager steps, events around each: the step's mask and hidden state copied from one "
+                              "pinned staging row to the device by gsp_copy_bytes (SM-driven copy), the prepared "
+                              "C-ABI call on weight copy i % copies storing the 16-byte top-1 record into pinned "
+                              "host memory") if world == 1 else
+                             ("eager steps, events around each: one pinned host-to-device copy of the step's mask "
+                              "and hidden state, the C-ABI call on weight copy i % copies with the in-kernel "
+                              "cross-rank exchange, one device-to-host copy of the 16-byte top-1 record"))},
             "gpu_launches": args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu_base,

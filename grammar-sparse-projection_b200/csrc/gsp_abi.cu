@@ -621,6 +621,12 @@ int32_t gsp_adaptive_logits(const void* hidden, int64_t hidden_row_stride, const
   return GSP_OK;
 }
 
+int32_t gsp_copy_bytes(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return GSP_OK;
+  if (!dst || !src) return fail(GSP_ERR_INVALID_ARGUMENT, "gsp_copy_bytes: dst and src are required");
+  return cuda_status(launch_copy_bytes(dst, src, bytes, static_cast<cudaStream_t>(stream)), "gsp_copy_bytes");
+}
+
 size_t gsp_group_plan_words(int32_t batch) {
   if (batch < 1) return 0;
   return (size_t)kPlanHeader + 6 * (size_t)batch;

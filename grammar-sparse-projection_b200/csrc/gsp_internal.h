@@ -189,6 +189,7 @@ cudaError_t launch_ids_to_bitmask(const int64_t* ids, int64_t count, int vocab, 
 cudaError_t launch_mask_stats(const uint32_t* mask, int64_t stride, int batch, int vocab,
                               int32_t* legal_counts, int32_t* full_words, int32_t* active_tiles,
                               cudaStream_t stream);
+cudaError_t launch_copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 cudaError_t launch_top1_from_keys(const int64_t* keys, int batch, float* top_value,
                                   int64_t* top_index, cudaStream_t stream);
 cudaError_t launch_block_gemm(const BlockGemmParams& p, int dtype, cudaStream_t stream);

@@ -1,5 +1,7 @@
 // Bitmask utilities: token-id list -> bitmask, per-request density statistics,
 // the device route selector, and top-1 key decoding.
+#include <algorithm>
+
 #include "gsp_common.cuh"
 #include "gsp_internal.h"
 
@@ -163,7 +165,35 @@ __global__ void top1_from_keys_kernel(const int64_t* __restrict__ keys, int batc
   if (top_index) top_index[b] = key_index(k);
 }
 
+// SM-driven copy of `bytes` bytes between device-accessible addresses (device
+// memory, or pinned host memory under unified addressing): each thread moves
+// 16-byte units (bytes past the last whole unit one at a time).
+__global__ void copy_bytes_kernel(unsigned char* __restrict__ dst, const unsigned char* __restrict__ src,
+                                  size_t bytes, int vec16) {
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t done = 0;
+  if (vec16) {
+    const size_t units = bytes / 16;
+    for (size_t i = tid; i < units; i += stride)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+    done = units * 16;
+  }
+  for (size_t i = done + tid; i < bytes; i += stride) dst[i] = src[i];
+}
+
 }  // namespace
+
+cudaError_t launch_copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+  if (bytes == 0) return cudaSuccess;
+  const int vec16 = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0;
+  const size_t units = vec16 ? (bytes + 15) / 16 : bytes;
+  const int threads = 256;
+  const size_t blocks = std::min<size_t>((units + threads - 1) / threads, 1184);
+  copy_bytes_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<unsigned char*>(dst),
+                                                             static_cast<const unsigned char*>(src), bytes, vec16);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ids_to_bitmask(const int64_t* ids, int64_t count, int vocab, uint32_t* mask,
                                   unsigned long long* stats, cudaStream_t stream) {

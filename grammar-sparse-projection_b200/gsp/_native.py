@@ -82,6 +82,7 @@ SIGNATURES = {
     "gsp_group_plan_words": ([_i32], _sz),
     "gsp_group_plan": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(RouteCost), _vp, _vp], _i32),
     "gsp_gather_rows": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp], _i32),
+    "gsp_copy_bytes": ([_vp, _vp, _sz, _vp], _i32),
     "gsp_grouped_scratch_bytes": ([_i32, _i32, _i32, _i32], _sz),
     "gsp_grouped_logits": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _vp,
                             ctypes.POINTER(RouteCost), ctypes.POINTER(_i32), _vp, _sz, _vp, _sz, _vp], _i32),
@@ -489,3 +490,12 @@ def grouped(hidden, weight, mask, logits=None, top_value=None, top_index=None, c
         _ptr(scratch), scratch.numel(), _ptr(ws), ws.numel(), _stream(hidden.device))
     _check(status, "gsp_grouped_logits")
     return list(hdr)
+
+
+def copy_bytes(dst: torch.Tensor, src: torch.Tensor, nbytes: int | None = None) -> None:
+    """gsp_copy_bytes on the current stream of whichever tensor is on a CUDA
+    device: an SM-driven copy (pinned host tensors included)."""
+    n = src.numel() * src.element_size() if nbytes is None else nbytes
+    dev = dst.device if dst.device.type == "cuda" else src.device
+    status = load().gsp_copy_bytes(_ptr(dst), _ptr(src), n, _stream(dev))
+    _check(status, "gsp_copy_bytes")

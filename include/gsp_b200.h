@@ -347,6 +347,16 @@ int32_t gsp_adaptive_logits(const void* hidden, int64_t hidden_row_stride, const
  * gsp_gather_rows copies dst row i = src row rows[i] (device int32 rows) for
  * permuting hidden states, masks, logits and top-1 rows.
  */
+/* SM-driven asynchronous copy of `bytes` bytes between any two addresses the
+ * device can reach: device memory, or pinned host memory (cudaHostAlloc /
+ * cudaMallocHost, which unified addressing maps into the device's address
+ * space). For a decode step's small inputs (a mask row and a hidden state,
+ * tens of KB) it avoids the fixed latency of a copy-engine transfer; the
+ * projection entries can likewise write top_value / top_index straight into
+ * pinned host memory. 16-byte units when both addresses are 16-byte aligned.
+ * No counterpart in the reference (its decode loop copies with torch). */
+int32_t gsp_copy_bytes(void* dst, const void* src, size_t bytes, void* stream);
+
 #define GSP_GROUP_MAX_BATCH 256
 size_t gsp_group_plan_words(int32_t batch);
 int32_t gsp_group_plan(const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch, int32_t vocab,

@@ -262,3 +262,32 @@ def test_full_size_density_sweep(cuda_device, clustered):
 def test_no_bounded_wait_gave_up(cuda_device):
     """Every kernel above completed without giving up a bounded wait."""
     assert _native.workspace_error(cuda_device) == 0
+
+
+def test_copy_bytes_and_top1_into_pinned_memory(cuda_device):
+    """gsp_copy_bytes between pinned host and device memory (16-byte units and
+    ragged tails), and a projection storing its top-1 straight into pinned
+    host memory: the end-to-end step's transfers."""
+    dev = cuda_device
+    rng = np.random.default_rng(21)
+    for nbytes, offset in ((35 * 1024, 0), (35 * 1024 + 3, 0), (1000, 1), (16, 0), (1, 0)):
+        src = torch.from_numpy(rng.integers(0, 256, size=nbytes + offset, dtype=np.uint8)).pin_memory()
+        dst = torch.zeros(nbytes + offset, dtype=torch.uint8, device=dev)
+        _native.copy_bytes(dst[offset:], src[offset:], nbytes)
+        back = torch.zeros(nbytes + offset, dtype=torch.uint8).pin_memory()
+        _native.copy_bytes(back[offset:], dst[offset:], nbytes)
+        torch.cuda.synchronize()
+        assert torch.equal(dst[offset:].cpu(), src[offset:]) and torch.equal(back[offset:], src[offset:]), nbytes
+    vocab, hidden = 20000, 256
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * 0.1).half().to(dev)
+    h = torch.from_numpy(rng.standard_normal((1, hidden), dtype=np.float32)).half().to(dev)
+    mask = torch.from_numpy(O.make_batch_mask(rng, 1, vocab, [200])).to(dev)
+    tv_h = torch.zeros(1, dtype=torch.float32).pin_memory()
+    ti_h = torch.zeros(1, dtype=torch.int64).pin_memory()
+    tv_d = torch.empty(1, device=dev)
+    ti_d = torch.empty(1, dtype=torch.int64, device=dev)
+    for _ in range(2):
+        _native.row_sparse(h, w, mask, top_value=tv_h, top_index=ti_h)
+        _native.row_sparse(h, w, mask, top_value=tv_d, top_index=ti_d)
+        torch.cuda.synchronize()
+        assert ti_h.item() == ti_d.item() and tv_h.item() == tv_d.item()

@@ -220,3 +220,10 @@ def test_grouped_entry_validation():
     assert lib.gsp_group_plan(FAKE, 2, 4, 64, 8, 2, 0, None, None, None) == -1
     assert lib.gsp_gather_rows(FAKE, 16, FAKE, 2, 16, FAKE, 8, None) == -1  # dst stride < row bytes
     assert lib.gsp_gather_rows(None, 16, None, 0, 16, None, 16, None) == 0  # nothing to copy
+
+
+def test_copy_bytes_validation():
+    lib = _native.load()
+    assert lib.gsp_copy_bytes(None, None, 0, None) == 0  # nothing to copy
+    assert lib.gsp_copy_bytes(None, FAKE, 16, None) == -1
+    assert lib.gsp_copy_bytes(FAKE, None, 16, None) == -1

@@ -170,6 +170,9 @@ __global__ void top1_from_keys_kernel(const int64_t* __restrict__ keys, int batc
 // 16-byte units (bytes past the last whole unit one at a time).
 __global__ void copy_bytes_kernel(unsigned char* __restrict__ dst, const unsigned char* __restrict__ src,
                                   size_t bytes, int vec16) {
+  // the next kernel (a projection reading these bytes) may launch now; its
+  // griddepcontrol.wait still waits for this copy to complete
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   size_t done = 0;

@@ -496,6 +496,10 @@ __device__ __forceinline__ int staged_index(int f) {
 template <typename T, int kV, bool kSample>
 __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const RowSparseParams p) {
   constexpr int kWpt = 4 * kV;  // words per thread
+  // Launched with programmatic dependent launch allowed: the CTAs may be
+  // resident while the previous kernel in the stream (an input copy) still
+  // runs; nothing is read or written before that kernel has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(1024) unsigned char smem[];
   const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * kWpt);
   uint32_t* s_list = reinterpret_cast<uint32_t*>(smem + L.list);
@@ -1239,16 +1243,19 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
     const int wpt = F <= kThreads * 16 ? 16 : 32;
     const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * wpt);
     if (L.total <= kStagedSmemMax && F <= kThreads * 32) {
-      if (wpt == 16) {
-        auto k = row_sparse_staged_kernel<T, 4, kSample>;
-        if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
-        k<<<grid, kThreads, L.total, stream>>>(p);
-      } else {
-        auto k = row_sparse_staged_kernel<T, 8, kSample>;
-        if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
-        k<<<grid, kThreads, L.total, stream>>>(p);
-      }
-      return cudaGetLastError();
+      auto k = wpt == 16 ? row_sparse_staged_kernel<T, 4, kSample> : row_sparse_staged_kernel<T, 8, kSample>;
+      if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)grid);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = L.total;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      return cudaLaunchKernelEx(&cfg, k, p);
     }
   }
   const DirectLayout L = direct_layout(p.batch);

@@ -9,8 +9,9 @@ hot path: full -inf-filled logits [V] plus the fused greedy top-1.
   value      legal-row GB/s = legal W bytes (k * H * 2) per step / device time
              per step, summed over ranks' work, timed with CUDA events;
   e2e        the same metric through the C-ABI call with host buffers: the
-             step's mask and hidden state copied from pinned host memory, the
-             top-1 copied back, all inside the timed region;
+             step's mask and hidden state copied from pinned host memory to
+             the device (gsp_copy_bytes), the top-1 record stored by the
+             kernel into pinned host memory, all inside the timed region;
   roofline   the row-sparse kernel's achieved legal-row bandwidth against the
              measured HBM copy bandwidth;
   sweep      every density of the GEMV workload, uniform and clustered;
@@ -21,9 +22,11 @@ with CUDA events around its replay, so host launch overhead and per-step event
 overhead are excluded. Inputs are larger than L2: step i reads weight copy
 i % 32 (32 copies of the 1 GB head) and mask i % 64, so no step finds its legal
 rows in L2. A second, conservative figure ("cold") times every step eagerly
-with its own events after a 256 MiB L2-flushing write. With --gpus N (torchrun, one process per GPU) the head is
-vocabulary-parallel: each rank streams the legal rows of its V/N shard and the
-ranks merge the per-request top-1 with one NCCL integer-MAX all-reduce.
+with its own events after a 256 MiB L2-flushing write. With --gpus N (torchrun,
+one process per GPU) the head is vocabulary-parallel: each rank streams the
+legal rows of its V/N shard and the projection kernel's last CTA merges the
+per-request top-1 with the other ranks over peer memory (NVLink), inside the
+same launch.
 
 `--impl reference` times the reference's CPU algorithm for the same step (the
 oracle port, all host threads) and prints its own line.
@@ -384,12 +387,10 @@ def main():
                 "what": "eager steps, 256 MiB L2-flushing write before each, events around each step"}
 
     # e2e through the C ABI with host buffers: each step's mask and hidden state
-    # sit in one pinned staging row, moved to the device by one copy each step;
-    # the top-1 comes back as one 16-byte record in pinned host memory. On one
-    # GPU the copy in is gsp_copy_bytes (an SM-driven copy: a copy-engine
-    # transfer's fixed latency dominates at 35 KB) and the kernel stores the
-    # record straight into pinned host memory; with more ranks, copy-engine
-    # copies both ways.
+    # sit in one pinned staging row, moved to the device by gsp_copy_bytes (an
+    # SM-driven copy: a copy-engine transfer's fixed latency dominates at
+    # 35 KB); the kernel stores the 16-byte top-1 record straight into pinned
+    # host memory (at N > 1 the global record, after the in-kernel exchange).
     local_words = (hi + 31) // 32 - lo // 32
     mask_bytes = local_words * 4
     mask_pad = (mask_bytes + 15) // 16 * 16
@@ -417,26 +418,28 @@ def main():
         if world == 1 else None
 
     def e2e_step(i):
+        _native.copy_bytes(dev_in, host_in[i % args.masks])
         if world == 1:
-            _native.copy_bytes(dev_in, host_in[i % args.masks])
             calls[i % len(calls)]()
-            return
-        dev_in.copy_(host_in[i % args.masks], non_blocking=True)
-        _native.vocab_parallel("row-sparse", dev_hidden, weights[i % len(weights)], dev_mask, xch.peers, rank,
-                               xch.max_batch, VOCAB, logits=logits, top_value=out_value,
-                               top_index=out_index, vocab_offset=lo)
-        host_top.copy_(dev_out, non_blocking=True)
+        else:
+            _native.vocab_parallel("row-sparse", dev_hidden, weights[i % len(weights)], dev_mask, xch.peers, rank,
+                                   xch.max_batch, VOCAB, logits=logits, top_value=host_value,
+                                   top_index=host_index, vocab_offset=lo)
 
     for i in range(3):
         e2e_step(i)
     barrier()
     e2e_steps = timed(args.steps, e2e_step, 0, flush_l2=False)
     barrier()
-    if world == 1:  # the last step's record on the host equals an eager call on its inputs
-        ref_index = torch.empty(1, dtype=torch.int64, device=dev)
-        _native.row_sparse(dev_hidden, weights[(args.steps - 1) % len(weights)], dev_mask, top_index=ref_index)
-        if int(ref_index.item()) != int(host_top[0]):
-            raise RuntimeError("end-to-end step's host record disagrees with the eager call")
+    # the last step's record on the host equals a call on its inputs with device outputs
+    last = (args.steps - 1) % len(weights)
+    if world == 1:
+        _native.row_sparse(dev_hidden, weights[last], dev_mask, top_index=out_index)
+    else:
+        _native.vocab_parallel("row-sparse", dev_hidden, weights[last], dev_mask, xch.peers, rank, xch.max_batch,
+                               VOCAB, top_value=out_value, top_index=out_index, vocab_offset=lo)
+    if int(out_index.item()) != int(host_top[0]):
+        raise RuntimeError("end-to-end step's host record disagrees with the device-output call")
     e2e_total = max_over_ranks(sum(e2e_steps), world)
     e2e_value = legal_bytes / (e2e_total * 1e-6) / 1e9
     h2d = int(in_bytes)
@@ -504,13 +507,10 @@ def main():
             "config": workload_config(args),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": e2e_total / args.steps,
-                    "what": (("eager steps, events around each: the step's mask and hidden state copied from one "
-                              "pinned staging row to the device by gsp_copy_bytes (SM-driven copy), the prepared "
-                              "C-ABI call on weight copy i % copies storing the 16-byte top-1 record into pinned "
-                              "host memory") if world == 1 else
-                             ("eager steps, events around each: one pinned host-to-device copy of the step's mask "
-                              "and hidden state, the C-ABI call on weight copy i % copies with the in-kernel "
-                              "cross-rank exchange, one device-to-host copy of the 16-byte top-1 record"))},
+                    "what": ("eager steps, events around each: the step's mask and hidden state copied from one "
+                             "pinned staging row to the device by gsp_copy_bytes (SM-driven copy), the C-ABI call "
+                             "on weight copy i % copies (prepared; at N > 1 with the in-kernel cross-rank "
+                             "exchange) storing the 16-byte top-1 record into pinned host memory")},
             "gpu_launches": args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu_base,

@@ -105,9 +105,12 @@ __global__ void __launch_bounds__(kPlanThreads) request_profile_kernel(const Gro
       atomicAdd(v.tiles + b, s_tiles[b]);
     }
   }
-  __threadfence();
+  // the barrier orders every thread's atomics before thread 0's fence and ticket
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(reinterpret_cast<unsigned int*>(v.hdr + 6), 1u) == gridDim.x - 1;
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(reinterpret_cast<unsigned int*>(v.hdr + 6), 1u) == gridDim.x - 1;
+  }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
@@ -164,9 +167,11 @@ __global__ void __launch_bounds__(kPlanThreads) group_footprint_kernel(const Gro
     atomicAdd(v.hist_min + s_min[tid], 1);
     atomicAdd(v.hist_max + s_max[tid], 1);
   }
-  __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(reinterpret_cast<unsigned int*>(v.hdr + 7), 1u) == gridDim.x - 1;
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(reinterpret_cast<unsigned int*>(v.hdr + 7), 1u) == gridDim.x - 1;
+  }
   __syncthreads();
   if (!s_last) return;
   __threadfence();

@@ -610,6 +610,12 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
     if (tid == 0) p.offsets[B] = (int64_t)total;
   }
 
+  // -inf over the illegal entries of this CTA's output slice, issued before
+  // the rows so that the stores drain while the row loads are in flight
+  if (p.logits && has_mask) {
+    __syncthreads();  // staged words complete
+    fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_words[staged_index<kWpt>((int)f)]; });
+  }
   const uint64_t lo = total * (uint64_t)cta / (uint64_t)G;
   const uint64_t hi = total * (uint64_t)(cta + 1) / (uint64_t)G;
   const uint32_t code_stride = (uint32_t)nw * 32u;
@@ -668,9 +674,6 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
     __syncthreads();
   }
 
-  // ---- 6. -inf over the illegal entries of this CTA's output slice ---------
-  if (p.logits && has_mask)
-    fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_words[staged_index<kWpt>((int)f)]; });
   // ---- 7. top-1 ------------------------------------------------------------
   if (want_top || kSample) finalize_top1<kSample>(p, s_keys, s_misc, want_top);
 }

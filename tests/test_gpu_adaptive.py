@@ -139,3 +139,29 @@ def test_batch_one_is_row_sparse_captured(cuda_device, head):
         torch.cuda.synchronize()
         assert gh.route_names() == ["row-sparse"]
         _same(res, _direct("row-sparse", h[:1], w, torch.from_numpy(masks[kind][:1]).to(dev)), kind)
+
+
+@pytest.mark.parametrize("vocab, hidden, batch, dtype", [(30001, 96, 5, torch.float16), (4099, 256, 2, torch.bfloat16)])
+def test_selector_on_ragged_sizes(cuda_device, vocab, hidden, batch, dtype):
+    """Vocabularies that are not multiples of 32 or 128 (tail bits of the last
+    mask word set on purpose): the device's statistics give the host model's
+    route for each cost model, and the outputs equal that route's."""
+    dev = cuda_device
+    rng = np.random.default_rng(vocab)
+    w = (torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32)) * 0.05).to(dtype).to(dev)
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).to(dtype).to(dev)
+    fns = {"row-sparse": _native.row_sparse, "block-sparse": _native.block_gemm, "dense-mask": _native.dense_masked}
+    for ks, cost in (([vocab // 200] * batch, COST), ([int(0.9 * vocab)] * batch, COST),
+                     ([vocab // 50] * batch, {"row_sparse_fixed_us": 50.0, "block_floor_us": 0.0, "dense_fixed_us": 50.0})):
+        mask_np = wl.make_batch_mask(rng, batch, vocab, ks, clustered=True, max_runs=4)
+        mask_np[:, -1] |= np.int32(-1)  # bits past the vocabulary in the last word: ignored
+        legal = wl.unpack_bitmask(mask_np, vocab).sum(axis=1).tolist()
+        want = tr.choose_route(batch, vocab, hidden, 2, legal, wl.active_tiles(mask_np, vocab), cost)
+        md = torch.from_numpy(mask_np).to(dev)
+        res = tr.grammar_head(h, w, md, cost=cost)
+        got = tr.ROUTES[int(res.route.item())]
+        assert got == want, (ks[0], cost, got, want)
+        lg = torch.empty(batch, vocab, dtype=dtype, device=dev)
+        ti = torch.empty(batch, dtype=torch.int64, device=dev)
+        fns[got](h, w, md, logits=lg, top_index=ti)
+        assert torch.equal(res.logits, lg) and torch.equal(res.top_index, ti), (ks[0], got)

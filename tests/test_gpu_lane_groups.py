@@ -160,3 +160,25 @@ def test_no_split_when_it_does_not_pay(cuda_device, weight):
         lg = torch.empty(B, V, dtype=torch.float16, device=dev)
         fn(h, w, torch.from_numpy(mask_np).to(dev), logits=lg)
         assert torch.equal(res.logits, lg)
+
+
+def test_plan_on_ragged_vocabulary(cuda_device):
+    """A vocabulary that is not a multiple of 32 or 128, with the bits past it
+    set in every request's last word: the device plan still equals the
+    restatement's, which never counts those bits."""
+    global V
+    saved = V
+    try:
+        V = 30001
+        rng = np.random.default_rng(17)
+        mask_np = _mixed_mask(rng, 9, 3)
+        mask_np[:, -1] |= np.int32(-1)
+        B = mask_np.shape[0]
+        plan = torch.empty(_native.GROUP_PLAN_HEADER + 6 * B, dtype=torch.int32, device=cuda_device)
+        _native.group_plan(torch.from_numpy(mask_np).to(cuda_device), V, H, 2, True, plan, COST)
+        got = plan.cpu().numpy()
+        ref = plan_reference(mask_np, True, COST)
+        assert got[:6].tolist() == [ref["k"], ref["ra"], ref["rb"], ref["single"], ref["single_ns"], ref["split_ns"]]
+        assert got[16:16 + B].tolist() == ref["order"]
+    finally:
+        V = saved

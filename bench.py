@@ -442,6 +442,8 @@ def main():
         raise RuntimeError("end-to-end step's host record disagrees with the device-output call")
     e2e_total = max_over_ranks(sum(e2e_steps), world)
     e2e_value = legal_bytes / (e2e_total * 1e-6) / 1e9
+    e2e_graph_us = e2e_graph_replay(dev, weights, host_in, dev_in, dev_hidden, dev_mask, logits, host_value,
+                                    host_index, args) if world == 1 else None
     h2d = int(in_bytes)
     d2h = int(dev_out.numel() * 8)
 
@@ -507,10 +509,13 @@ def main():
             "config": workload_config(args),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": e2e_total / args.steps,
+                    "graph_replay_us_per_step": e2e_graph_us,
                     "what": ("eager steps, events around each: the step's mask and hidden state copied from one "
                              "pinned staging row to the device by gsp_copy_bytes (SM-driven copy), the C-ABI call "
                              "on weight copy i % copies (prepared; at N > 1 with the in-kernel cross-rank "
-                             "exchange) storing the 16-byte top-1 record into pinned host memory")},
+                             "exchange) storing the 16-byte top-1 record into pinned host memory; "
+                             "graph_replay_us_per_step: the same step recorded once per weight copy as a CUDA "
+                             "graph and replayed (one GPU)")},
             "gpu_launches": args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu_base,
@@ -532,6 +537,50 @@ def main():
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     return 0
+
+
+def e2e_graph_replay(dev, weights, host_in, dev_in, dev_hidden, dev_mask, logits, host_value, host_index, args):
+    """The end-to-end step as a CUDA graph per weight copy (the SM copy of a
+    pinned staging row and the C-ABI call storing the top-1 record into pinned
+    host memory, recorded once), replayed per step after the step's input is
+    written into that graph's staging row; mean µs per step from events around
+    each replay."""
+    from gsp import _native
+    stages = [torch.zeros(host_in.shape[1], dtype=torch.uint8).pin_memory() for _ in weights]
+    done = [torch.cuda.Event() for _ in weights]
+    cap = torch.cuda.Stream(device=dev)
+    cap.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(cap):
+        calls = [_native.PreparedProjection("gsp_row_sparse_logits", dev_hidden, w, dev_mask, logits=logits,
+                                            top_value=host_value, top_index=host_index) for w in weights]
+        for j, call in enumerate(calls):
+            _native.copy_bytes(dev_in, stages[j])
+            call()
+    cap.synchronize()
+    graphs = []
+    for j, call in enumerate(calls):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            _native.copy_bytes(dev_in, stages[j])
+            call()
+        graphs.append(g)
+    n = args.steps
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    for i in range(-3, n):
+        j = i % len(graphs)
+        done[j].synchronize()  # the staging row's previous copy has run
+        stages[j].copy_(host_in[i % args.masks])
+        if i >= 0:
+            ev0[i].record()
+        graphs[j].replay()
+        if i >= 0:
+            ev1[i].record()
+        done[j].record()
+    torch.cuda.synchronize()
+    us = sum(a.elapsed_time(b) * 1e3 for a, b in zip(ev0, ev1)) / n
+    del graphs
+    return us
 
 
 def legal_counts_local(masks_np: np.ndarray, lo: int, hi: int) -> np.ndarray:

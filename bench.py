@@ -413,18 +413,17 @@ def main():
     host_value = host_top[1:2].view(torch.float32)[:1]
 
     # one prepared C-ABI call per weight copy (arguments converted once)
-    calls = [_native.PreparedProjection("gsp_row_sparse_logits", dev_hidden, w, dev_mask, logits=logits,
-                                        top_value=host_value, top_index=host_index) for w in weights] \
-        if world == 1 else None
+    if world == 1:
+        calls = [_native.PreparedProjection("gsp_row_sparse_logits", dev_hidden, w, dev_mask, logits=logits,
+                                            top_value=host_value, top_index=host_index) for w in weights]
+    else:
+        calls = [_native.PreparedVocabParallel("row-sparse", dev_hidden, w, dev_mask, xch.peers, rank, xch.max_batch,
+                                               VOCAB, logits=logits, top_value=host_value, top_index=host_index,
+                                               vocab_offset=lo) for w in weights]
 
     def e2e_step(i):
         _native.copy_bytes(dev_in, host_in[i % args.masks])
-        if world == 1:
-            calls[i % len(calls)]()
-        else:
-            _native.vocab_parallel("row-sparse", dev_hidden, weights[i % len(weights)], dev_mask, xch.peers, rank,
-                                   xch.max_batch, VOCAB, logits=logits, top_value=host_value,
-                                   top_index=host_index, vocab_offset=lo)
+        calls[i % len(calls)]()
 
     for i in range(3):
         e2e_step(i)
@@ -511,8 +510,8 @@ def main():
                     "us_per_step": e2e_total / args.steps,
                     "graph_replay_us_per_step": e2e_graph_us,
                     "what": ("eager steps, events around each: the step's mask and hidden state copied from one "
-                             "pinned staging row to the device by gsp_copy_bytes (SM-driven copy), the C-ABI call "
-                             "on weight copy i % copies (prepared; at N > 1 with the in-kernel cross-rank "
+                             "pinned staging row to the device by gsp_copy_bytes (SM-driven copy), the prepared "
+                             "C-ABI call on weight copy i % copies (at N > 1 with the in-kernel cross-rank "
                              "exchange) storing the 16-byte top-1 record into pinned host memory; "
                              "graph_replay_us_per_step: the same step recorded once per weight copy as a CUDA "
                              "graph and replayed (one GPU)")},

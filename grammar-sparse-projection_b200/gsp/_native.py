@@ -307,6 +307,36 @@ def vocab_parallel(route: str, hidden, weight, mask, peers: list[int], rank: int
     _check(status, "gsp_vocab_parallel_logits")
 
 
+class PreparedVocabParallel:
+    """One gsp_vocab_parallel_logits call with its arguments converted once
+    (pointers, strides, sizes, the peer-buffer array, workspace and the
+    current stream at construction); each call() only crosses the C ABI."""
+
+    def __init__(self, route: str, hidden, weight, mask, peers: list[int], rank: int, max_batch: int,
+                 total_vocab: int, logits=None, top_value=None, top_index=None, top_key=None,
+                 vocab_offset: int = 0):
+        _require_cuda(hidden, weight, mask, logits)
+        lib = load()
+        batch, hdim = hidden.shape
+        vocab = weight.shape[0]
+        ws = workspace(hidden.device, batch, vocab)
+        arr = (_vp * len(peers))(*[_vp(int(q)) for q in peers])
+        self._keep = (hidden, weight, mask, logits, top_value, top_index, top_key, ws, arr)
+        self._fn = lib.gsp_vocab_parallel_logits
+        self._args = (
+            ROUTE_CODES[route], _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+            _ptr(mask), 0 if mask is None else mask.stride(0),
+            batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+            _ptr(logits), 0 if logits is None else logits.stride(0),
+            _ptr(top_value), _ptr(top_index), _ptr(top_key),
+            _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, total_vocab, _stream(hidden.device))
+
+    def __call__(self) -> None:
+        status = self._fn(*self._args)
+        if status:
+            _check(status, "gsp_vocab_parallel_logits")
+
+
 def row_sparse_sample(hidden, weight, mask, seeds, offset: int, temperature: float, sample_index,
                       sample_logsumexp=None, logits=None, top_value=None, top_index=None,
                       vocab_offset: int = 0) -> None:

@@ -179,3 +179,37 @@ def test_exchange_wait_runs_out_on_one_gpu(cuda_device):
     finally:
         _native.peer_exchange_free(own)
         _native.peer_exchange_free(silent)
+
+
+def test_prepared_vocab_parallel_single_rank(cuda_device):
+    """PreparedVocabParallel (arguments converted once) with world size 1 runs
+    the plain projection: equal to gsp_row_sparse_logits, on repeated calls,
+    with the top-1 record written into pinned host memory."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "..", "grammar-sparse-projection_b200"))
+    from gsp import _native
+    dev = cuda_device
+    rng = np.random.default_rng(9)
+    vocab, hidden = 20000, 128
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * 0.1).half().to(dev)
+    h = torch.from_numpy(rng.standard_normal((1, hidden), dtype=np.float32)).half().to(dev)
+    mask = torch.from_numpy(_case(vocab, hidden, 1, 4, torch.float16)[2]).to(dev)
+    own, _ = _native.peer_exchange_alloc(1, 1)
+    try:
+        lg = torch.empty(1, vocab, dtype=torch.float16, device=dev)
+        host = torch.zeros(2, dtype=torch.int64).pin_memory()
+        call = _native.PreparedVocabParallel("row-sparse", h, w, mask, [own], 0, 1, vocab, logits=lg,
+                                             top_value=host[1:2].view(torch.float32)[:1], top_index=host[0:1])
+        lg_ref = torch.empty(1, vocab, dtype=torch.float16, device=dev)
+        ti_ref = torch.empty(1, dtype=torch.int64, device=dev)
+        tv_ref = torch.empty(1, device=dev)
+        _native.row_sparse(h, w, mask, logits=lg_ref, top_value=tv_ref, top_index=ti_ref)
+        for _ in range(3):
+            host.zero_()
+            call()
+            torch.cuda.synchronize()
+            assert torch.equal(lg, lg_ref)
+            assert int(host[0]) == ti_ref.item() and host[1:2].view(torch.float32)[0].item() == tv_ref.item()
+        assert _native.workspace_error(dev) == 0
+    finally:
+        _native.peer_exchange_free(own)

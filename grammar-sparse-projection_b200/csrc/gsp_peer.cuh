@@ -18,7 +18,7 @@
 // A rank can run at most one call ahead of the slowest peer (it cannot finish
 // call e + 1 before every peer has written its e + 1 keys, which each peer does
 // only after reading its call-e keys), so two key buffers suffice. All ranks
-// must make the same sequence of calls. Nothing here uses multicast.
+// must make the same sequence of calls. Only plain peer loads and stores are used.
 #pragma once
 
 #include <stdint.h>

@@ -417,8 +417,8 @@ int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride, con
                               int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype,
                               int64_t vocab_offset, void* logits, int64_t logits_row_stride, float temperature,
                               const uint64_t* seeds, uint64_t offset, int64_t* sample_index,
-                              float* sample_logsumexp, float* top_value, int64_t* top_index, void* workspace,
-                              size_t workspace_bytes_, void* stream) {
+                              float* sample_logsumexp, int64_t* sample_key, float* top_value, int64_t* top_index,
+                              int64_t* top_key, void* workspace, size_t workspace_bytes_, void* stream) {
   const char* fn = "gsp_row_sparse_sample";
   int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
                                    bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
@@ -434,9 +434,11 @@ int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride, con
   p.logits_stride = batch > 1 ? logits_row_stride : vocab;
   p.top_value = top_value;
   p.top_index = top_index;
+  p.top_key = top_key;
   attach_workspace(p, workspace);
   p.sample_index = sample_index;
   p.sample_lse = sample_logsumexp;
+  p.sample_key = sample_key;
   p.seeds = seeds;
   p.offset = offset;
   p.inv_temp = 1.0f / temperature;
@@ -619,6 +621,13 @@ int32_t gsp_adaptive_logits(const void* hidden, int64_t hidden_row_stride, const
   if ((err = cudaStreamUpdateCaptureDependencies(s, &node, 1, cudaStreamSetCaptureDependencies)) != cudaSuccess)
     return cuda_status(err, fn);
   return GSP_OK;
+}
+
+int32_t gsp_merge_logsumexp(const float* lse, int32_t parts, int32_t batch, float* out, void* stream) {
+  const char* fn = "gsp_merge_logsumexp";
+  if (parts < 1 || batch < 1) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: parts and batch must be positive", fn);
+  if (!lse || !out) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: lse and out are required", fn);
+  return cuda_status(launch_merge_logsumexp(lse, parts, batch, out, static_cast<cudaStream_t>(stream)), fn);
 }
 
 int32_t gsp_copy_bytes(void* dst, const void* src, size_t bytes, void* stream) {

@@ -73,6 +73,7 @@ struct RowSparseParams {
   // fused sampler (sample_index != nullptr; contract in gsp_sampler.cuh)
   int64_t* sample_index;             // [batch] sampled global token ids
   float* sample_lse;                 // [batch] log-sum-exp of legal logits * inv_temp (optional)
+  int64_t* sample_key;               // [batch] signed-orderable winning key (optional)
   const uint64_t* seeds;             // [batch] per-request generator keys
   uint64_t offset;                   // step counter
   float inv_temp;                    // 1 / temperature
@@ -190,6 +191,7 @@ cudaError_t launch_mask_stats(const uint32_t* mask, int64_t stride, int batch, i
                               int32_t* legal_counts, int32_t* full_words, int32_t* active_tiles,
                               cudaStream_t stream);
 cudaError_t launch_copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+cudaError_t launch_merge_logsumexp(const float* lse, int parts, int batch, float* out, cudaStream_t stream);
 cudaError_t launch_top1_from_keys(const int64_t* keys, int batch, float* top_value,
                                   int64_t* top_index, cudaStream_t stream);
 cudaError_t launch_block_gemm(const BlockGemmParams& p, int dtype, cudaStream_t stream);

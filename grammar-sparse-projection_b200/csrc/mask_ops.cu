@@ -156,6 +156,21 @@ __global__ void __launch_bounds__(kRouteThreads) route_select_kernel(const Route
   if (p.route_word) *p.route_word = route;
 }
 
+// out[b] = log sum_r exp(lse[r][b]), max-shifted; -inf when every part is.
+__global__ void merge_logsumexp_kernel(const float* __restrict__ lse, int parts, int batch, float* __restrict__ out) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  float m = -INFINITY;
+  for (int r = 0; r < parts; ++r) m = fmaxf(m, lse[(size_t)r * batch + b]);
+  if (m == -INFINITY) {
+    out[b] = -INFINITY;
+    return;
+  }
+  float s = 0.f;
+  for (int r = 0; r < parts; ++r) s += expf(lse[(size_t)r * batch + b] - m);
+  out[b] = m + logf(s);
+}
+
 __global__ void top1_from_keys_kernel(const int64_t* __restrict__ keys, int batch,
                                       float* top_value, int64_t* top_index) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -247,6 +262,11 @@ cudaError_t launch_mask_stats(const uint32_t* mask, int64_t stride, int batch, i
 cudaError_t launch_route_select(const RouteSelectParams& p, cudaStream_t stream) {
   const int blocks = (p.ntiles + kRouteTiles - 1) / kRouteTiles;
   route_select_kernel<<<blocks, kRouteThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge_logsumexp(const float* lse, int parts, int batch, float* out, cudaStream_t stream) {
+  merge_logsumexp_kernel<<<(batch + 127) / 128, 128, 0, stream>>>(lse, parts, batch, out);
   return cudaGetLastError();
 }
 

@@ -236,7 +236,11 @@ __device__ __forceinline__ void sample_finish(const RowSparseParams& p) {
   constexpr int kChunkLoads = 8;
   const int G = gridDim.x, B = p.batch, lane = threadIdx.x & 31, warp = threadIdx.x >> 5,
             nwarps = blockDim.x >> 5;
-  for (int b = threadIdx.x; b < B; b += blockDim.x) p.sample_index[b] = key_index(atomicExch(p.sample_keys + b, 0ull));
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const unsigned long long k = atomicExch(p.sample_keys + b, 0ull);
+    p.sample_index[b] = key_index(k);
+    if (p.sample_key) p.sample_key[b] = key_to_signed(k);
+  }
   for (int b = warp; b < B; b += nwarps) {
     float m = -INFINITY, sum = 0.f;
     for (int c0 = 0; c0 < G; c0 += 32 * kChunkLoads) {

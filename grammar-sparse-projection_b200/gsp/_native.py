@@ -67,7 +67,9 @@ SIGNATURES = {
     "gsp_row_sparse_logits_static": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
                                       _vp, _i64, _vp, _vp, _vp, _vp], _i32),
     "gsp_row_sparse_sample": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _vp, _i64,
-                               ctypes.c_float, _vp, ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, _sz, _vp], _i32),
+                               ctypes.c_float, _vp, ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                               _vp], _i32),
+    "gsp_merge_logsumexp": ([_vp, _i32, _i32, _vp, _vp], _i32),
     "gsp_peer_exchange_bytes": ([_i32, _i32], _sz),
     "gsp_peer_exchange_alloc": ([_sz, ctypes.POINTER(_vp), _vp], _i32),
     "gsp_peer_exchange_open": ([_vp, ctypes.POINTER(_vp)], _i32),
@@ -339,7 +341,7 @@ class PreparedVocabParallel:
 
 def row_sparse_sample(hidden, weight, mask, seeds, offset: int, temperature: float, sample_index,
                       sample_logsumexp=None, logits=None, top_value=None, top_index=None,
-                      vocab_offset: int = 0) -> None:
+                      vocab_offset: int = 0, sample_key=None, top_key=None) -> None:
     """Fused sampler (gsp_row_sparse_sample): Gumbel-max draw per request from
     softmax(logits / temperature) over the legal tokens, keyed by
     seeds[b] (uint64 stored as int64) and the step counter `offset`."""
@@ -354,9 +356,17 @@ def row_sparse_sample(hidden, weight, mask, seeds, offset: int, temperature: flo
         batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
         _ptr(logits), 0 if logits is None else logits.stride(0),
         float(temperature), _ptr(seeds), int(offset) & 0xFFFFFFFFFFFFFFFF,
-        _ptr(sample_index), _ptr(sample_logsumexp), _ptr(top_value), _ptr(top_index),
-        _ptr(ws), ws.numel(), _stream(hidden.device))
+        _ptr(sample_index), _ptr(sample_logsumexp), _ptr(sample_key), _ptr(top_value), _ptr(top_index),
+        _ptr(top_key), _ptr(ws), ws.numel(), _stream(hidden.device))
     _check(status, "gsp_row_sparse_sample")
+
+
+def merge_logsumexp(lse_parts, out) -> None:
+    """gsp_merge_logsumexp: lse_parts CUDA float32 [parts, batch] -> out [batch]."""
+    _require_cuda(lse_parts, out)
+    status = load().gsp_merge_logsumexp(_ptr(lse_parts), lse_parts.shape[0], lse_parts.shape[1], _ptr(out),
+                                        _stream(out.device))
+    _check(status, "gsp_merge_logsumexp")
 
 
 def row_sparse_compact(hidden, weight, mask, compact_logits, compact_ids, offsets,

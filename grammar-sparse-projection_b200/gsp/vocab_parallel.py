@@ -204,3 +204,46 @@ class VocabParallelHead:
         _native.top1_from_keys(keys, top_value, top_index)
         logits = gather_logits(local_logits, self.vocab, self.group) if full_logits else None
         return top_value, top_index, logits
+
+    def sample(self, hidden: torch.Tensor, bitmask_gpu: torch.Tensor, *, seeds: torch.Tensor, step: int,
+               temperature: float = 1.0):
+        """Grammar-conditioned sampling over the whole vocabulary from the row
+        shards: every rank runs the fused sampler on its shard (its Gumbel
+        noise is keyed by global token ids), then one integer-MAX all-reduce
+        of the per-request sample keys and greedy keys and an all-gather of
+        the per-shard log-sum-exps (merged by gsp_merge_logsumexp). The token
+        ids equal a single-GPU grammar_sample over the full head bit for bit;
+        the log-sum-exp agrees to fp32 rounding. Returns a SampleResult
+        (logits None)."""
+        from .triton_runtime import SampleResult
+        hidden_2d = hidden.reshape(1, -1) if hidden.ndim == 1 else hidden
+        batch = hidden_2d.shape[0]
+        dev = hidden.device
+        mask = self.local_mask(bitmask_gpu.reshape(batch, -1))
+        skey = torch.empty(batch, device=dev, dtype=torch.int64)
+        tkey = torch.empty(batch, device=dev, dtype=torch.int64)
+        lse = torch.empty(batch, device=dev, dtype=torch.float32)
+        sidx = torch.empty(batch, device=dev, dtype=torch.int64)
+        if self.stop > self.start:
+            _native.row_sparse_sample(hidden_2d, self.weight, mask, seeds.contiguous(), step, temperature, sidx,
+                                      sample_logsumexp=lse, vocab_offset=self.start, sample_key=skey, top_key=tkey)
+        else:
+            skey.fill_(KEY_SIGN)
+            tkey.fill_(KEY_SIGN)
+            lse.fill_(float("-inf"))
+        merge_top1_keys(skey, self.group)
+        merge_top1_keys(tkey, self.group)
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            parts = [torch.empty_like(lse) for _ in range(dist.get_world_size(self.group))]
+            dist.all_gather(parts, lse, group=self.group)
+            stacked = torch.stack(parts)
+        else:
+            stacked = lse.reshape(1, batch)
+        out_lse = torch.empty(batch, device=dev, dtype=torch.float32)
+        _native.merge_logsumexp(stacked.contiguous(), out_lse)
+        token_ids = torch.empty(batch, device=dev, dtype=torch.int64)
+        _native.top1_from_keys(skey, None, token_ids)
+        top_value = torch.empty(batch, device=dev, dtype=torch.float32)
+        top_index = torch.empty(batch, device=dev, dtype=torch.int64)
+        _native.top1_from_keys(tkey, top_value, top_index)
+        return SampleResult(token_ids, out_lse, top_value, top_index, None)

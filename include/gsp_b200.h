@@ -203,7 +203,15 @@ int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
  *                         log-probability is x / T - sample_logsumexp; its
  *                         partial sums merge in arrival order, so repeated calls
  *                         agree to fp32 rounding (the sampled ids bit for bit);
- *   top_value / top_index: the greedy top-1, as in gsp_row_sparse_logits.
+ *   sample_key[b]       = the winning perturbed score and id as a signed-
+ *                         orderable top-1 key (optional): the noise is keyed by
+ *                         the GLOBAL token id (vocab_offset + v), so for row
+ *                         shards of one vocabulary the integer MAX of the
+ *                         shards' keys is the whole vocabulary's draw
+ *                         (gsp_top1_from_keys decodes it), and
+ *                         gsp_merge_logsumexp combines their log-sum-exps;
+ *   top_value / top_index / top_key: the greedy top-1, as in
+ *                         gsp_row_sparse_logits.
  * temperature > 0 and finite; seeds is a device array [batch]; offset is the
  * caller's step counter (use a new one per step). The workspace must hold
  * gsp_workspace_bytes(batch, vocab) bytes. No counterpart in the reference
@@ -217,8 +225,14 @@ int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride,
                               int64_t logits_row_stride, float temperature,
                               const uint64_t* seeds, uint64_t offset,
                               int64_t* sample_index, float* sample_logsumexp,
-                              float* top_value, int64_t* top_index, void* workspace,
-                              size_t workspace_bytes, void* stream);
+                              int64_t* sample_key, float* top_value, int64_t* top_index,
+                              int64_t* top_key, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* out[b] = log sum over r < parts of exp(lse[r * batch + b]) (-inf when every
+ * part is -inf): merges per-shard log-sum-exps of a vocabulary-parallel
+ * sampler step (device arrays). No counterpart in the reference. */
+int32_t gsp_merge_logsumexp(const float* lse, int32_t parts, int32_t batch, float* out, void* stream);
 
 /*
  * Vocabulary-parallel head: top-1 merged across ranks inside the kernel.

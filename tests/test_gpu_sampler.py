@@ -148,3 +148,48 @@ def test_sample_without_legal_tokens_and_workspace_left_zero(cuda_device):
         ws = _native.workspace(dev, batch, vocab)
         torch.cuda.synchronize()
         assert int(ws[:4].count_nonzero()) == 0 and int(ws[8:].count_nonzero()) == 0, (batch, vocab)
+
+
+@pytest.mark.parametrize("shards", [2, 3])
+def test_sharded_sampling_equals_whole_vocabulary(cuda_device, shards):
+    """The sampler on row shards of one vocabulary (vocab_offset = the shard's
+    first id, as each rank of a vocabulary-parallel head runs it): the integer
+    MAX of the shards' sample keys is the unsharded draw bit for bit, their
+    log-sum-exps merged by gsp_merge_logsumexp agree to fp32 rounding, and the
+    greedy keys give the unsharded top-1."""
+    from gsp import vocab_parallel as vp
+    dev = cuda_device
+    rng = np.random.default_rng(60 + shards)
+    vocab, hidden, batch, temperature = 30017, 128, 6, 0.9
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * 0.2).half().to(dev)
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).half().to(dev)
+    ks = [int(k) for k in rng.integers(0, vocab // 20, size=batch)]
+    ks[0] = 0  # a request without a legal token
+    mask = torch.from_numpy(O.make_batch_mask(rng, batch, vocab, ks, clustered=True, max_runs=8)).to(dev)
+    seeds = _seeds(dev, batch, 77)
+    for step in (0, 9):
+        full = tr.grammar_sample(h, w, mask, seeds=seeds, step=step, temperature=temperature)
+        skeys, tkeys, lses = [], [], []
+        for r in range(shards):
+            lo, hi = vp.shard_bounds(vocab, shards, r)
+            sk = torch.empty(batch, dtype=torch.int64, device=dev)
+            tk = torch.empty(batch, dtype=torch.int64, device=dev)
+            ls = torch.empty(batch, device=dev)
+            si = torch.empty(batch, dtype=torch.int64, device=dev)
+            _native.row_sparse_sample(h, w[lo:hi], mask[:, lo // 32:(hi + 31) // 32].contiguous(), seeds, step,
+                                      temperature, si, sample_logsumexp=ls, vocab_offset=lo, sample_key=sk,
+                                      top_key=tk)
+            skeys.append(sk)
+            tkeys.append(tk)
+            lses.append(ls)
+        ids = torch.empty(batch, dtype=torch.int64, device=dev)
+        _native.top1_from_keys(torch.stack(skeys).max(dim=0).values, None, ids)
+        assert torch.equal(ids, full.token_ids), (shards, step)
+        lse = torch.empty(batch, device=dev)
+        _native.merge_logsumexp(torch.stack(lses).contiguous(), lse)
+        assert lse[0].item() == float("-inf") and full.logsumexp[0].item() == float("-inf")
+        assert torch.allclose(lse[1:], full.logsumexp[1:], rtol=1e-5, atol=1e-5), (lse, full.logsumexp)
+        tv = torch.empty(batch, device=dev)
+        ti = torch.empty(batch, dtype=torch.int64, device=dev)
+        _native.top1_from_keys(torch.stack(tkeys).max(dim=0).values, tv, ti)
+        assert torch.equal(ti, full.top_index) and torch.equal(tv, full.top_value)

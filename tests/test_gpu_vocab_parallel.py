@@ -112,6 +112,18 @@ def _worker(rank, world, port, result_path):
                 if not (torch.equal(tv_g, tv_n) and torch.equal(ti_g, ti_n)):
                     failures.append(f"graph replay V={vocab} B={batch}")
             del g
+        # sampling across the shards (NCCL merge) equals the single-GPU sampler
+        from gsp import triton_runtime as tr
+        w, h, mask = _case(30001, 128, 5, 7, torch.float16)
+        head_s = vp.VocabParallelHead.from_full_weight(w.to(dev))
+        seeds = torch.arange(5, device=dev, dtype=torch.int64) * 7919 + 3
+        got = head_s.sample(h.to(dev), torch.from_numpy(mask).to(dev), seeds=seeds, step=4, temperature=0.8)
+        want = tr.grammar_sample(h.to(dev), w.to(dev), torch.from_numpy(mask).to(dev), seeds=seeds, step=4,
+                                 temperature=0.8)
+        if not (torch.equal(got.token_ids, want.token_ids) and torch.equal(got.top_index, want.top_index)):
+            failures.append("vocabulary-parallel sample != single-GPU sample")
+        if not torch.allclose(got.logsumexp, want.logsumexp, rtol=1e-5, atol=1e-5):
+            failures.append("vocabulary-parallel log-sum-exp")
         if _native.workspace_error(dev) != 0:
             failures.append("workspace error word set")
         dist.barrier()

@@ -227,3 +227,9 @@ def test_copy_bytes_validation():
     assert lib.gsp_copy_bytes(None, None, 0, None) == 0  # nothing to copy
     assert lib.gsp_copy_bytes(None, FAKE, 16, None) == -1
     assert lib.gsp_copy_bytes(FAKE, None, 16, None) == -1
+
+
+def test_merge_logsumexp_validation():
+    lib = _native.load()
+    assert lib.gsp_merge_logsumexp(FAKE, 0, 4, FAKE, None) == -1
+    assert lib.gsp_merge_logsumexp(None, 2, 4, FAKE, None) == -1

@@ -43,7 +43,7 @@ FAKE = ctypes.c_void_p(4096)  # never dereferenced: every call below fails valid
 def _sample_call(temperature=1.0, seeds=FAKE, sample=FAKE, ws=FAKE, wsb=1 << 30):
     lib = _native.load()
     return lib.gsp_row_sparse_sample(FAKE, 8, FAKE, 8, None, 0, 1, 64, 8, 0, 0, None, 64, temperature, seeds, 0,
-                                     sample, None, None, None, ws, wsb, None)
+                                     sample, None, None, None, None, None, ws, wsb, None)
 
 
 def test_sample_entry_validation():

@@ -233,3 +233,23 @@ def test_merge_logsumexp_validation():
     lib = _native.load()
     assert lib.gsp_merge_logsumexp(FAKE, 0, 4, FAKE, None) == -1
     assert lib.gsp_merge_logsumexp(None, 2, 4, FAKE, None) == -1
+
+
+def test_newer_python_entries_reject_cpu_tensors_and_bad_arguments():
+    """The device-route, lane-group and graphed-head entry points raise
+    ValueError for CPU tensors like the reference's entry points (no CPU
+    path), and unknown policies or oversized grouped batches are refused
+    before any device work."""
+    h = torch.zeros(2, 8, dtype=torch.float16)
+    w = torch.zeros(64, 8, dtype=torch.float16)
+    m = torch.zeros(2, 2, dtype=torch.int32)
+    for call in (lambda: tr.grammar_head(h, w, m),
+                 lambda: tr.grouped_grammar_logits(h, w, m),
+                 lambda: tr.adaptive_grammar_logits(h, w, m, policy="device"),
+                 lambda: tr.adaptive_grammar_logits(h, w, m, policy="grouped"),
+                 lambda: tr.adaptive_grammar_logits(h, w, m, policy="no-such-policy")):
+        with pytest.raises(ValueError):
+            call()
+    from gsp.graphed import GraphedGrammarHead
+    with pytest.raises(ValueError):
+        GraphedGrammarHead(w, 2)

@@ -101,3 +101,62 @@ def test_tie_across_shards_prefers_lowest_global_index():
     merged = torch.maximum(keys_r0, keys_r1)
     _, idx = vp.decode_keys(merged)
     assert idx.item() == 100
+
+
+def _sample_worker(rank, world, port, case, q):
+    """One CPU rank of a sharded sampling step: the oracle's Gumbel-max keys of
+    this rank's row shard (noise keyed by global token ids, as the sampler
+    kernel keys it), merged across ranks by the integer-MAX all-reduce that
+    VocabParallelHead.sample uses, and the shard log-sum-exps all-gathered and
+    combined; both against the oracle's whole-vocabulary draw."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        vocab, hidden, batch, seed, temperature, step = case
+        rng = np.random.default_rng(seed)
+        w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * 0.3).half()
+        h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).half()
+        ks = [0] + [int(k) for k in rng.integers(1, vocab // 10, size=batch - 1)]
+        mask = O.make_batch_mask(rng, batch, vocab, ks, clustered=True, max_runs=6)
+        seeds = [int(s) for s in rng.integers(1, 2 ** 62, size=batch)]
+        lo, hi = vp.shard_bounds(vocab, world, rank)
+        shard = O.sample_reference(h, w[lo:hi], np.ascontiguousarray(mask[:, lo // 32:(hi + 31) // 32]),
+                                   torch.float16, temperature, seeds, step, vocab_offset=lo)
+        vals = torch.tensor([float(s.max()) if ids.size else 0.0 for _, _, s, ids in shard], dtype=torch.float32)
+        idx = torch.tensor([int(ids[int(np.argmax(s))]) if ids.size else 0 for _, _, s, ids in shard])
+        valid = torch.tensor([ids.size > 0 for _, _, _, ids in shard])
+        keys = vp.encode_keys(vals, idx, valid)
+        vp.merge_top1_keys(keys)
+        _, pick = vp.decode_keys(keys)
+        lse = torch.tensor([lse for _, lse, _, _ in shard], dtype=torch.float64)
+        parts = [torch.empty_like(lse) for _ in range(world)]
+        dist.all_gather(parts, lse)
+        stacked = torch.stack(parts)
+        merged = torch.logsumexp(stacked, dim=0)
+        full = O.sample_reference(h, w, mask, torch.float16, temperature, seeds, step)
+        want_pick = torch.tensor([p for p, _, _, _ in full])
+        want_lse = torch.tensor([l for _, l, _, _ in full], dtype=torch.float64)
+        fin = torch.isfinite(want_lse)
+        q.put((rank, bool(torch.equal(pick, want_pick)),
+               bool(torch.equal(torch.isfinite(merged), fin)
+                    and torch.allclose(merged[fin], want_lse[fin], rtol=1e-12, atol=1e-9))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [(3000, 32, 5, 21, 0.8, 3), (4099, 16, 4, 22, 1.3, 12345)])
+def test_sampling_merge_gloo(case):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sample_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, pick_ok, lse_ok in results:
+        assert pick_ok and lse_ok, (rank, pick_ok, lse_ok)

@@ -253,3 +253,18 @@ def test_newer_python_entries_reject_cpu_tensors_and_bad_arguments():
     from gsp.graphed import GraphedGrammarHead
     with pytest.raises(ValueError):
         GraphedGrammarHead(w, 2)
+
+
+def test_ctypes_signatures_match_header_parameter_counts():
+    """Every entry point declared in include/gsp_b200.h has a ctypes
+    signature with the same number of parameters (an ABI change that misses
+    the binding fails here, on CPU)."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = re.findall(r"^\s*(?:int32_t|size_t|void|const char\s*\*)\s*(gsp_\w+)\s*\(([^;]*?)\)\s*;", text, re.M | re.S)
+    assert len(decls) >= 20
+    for name, params in decls:
+        params = " ".join(params.split())
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert name in _native.SIGNATURES, name
+        assert len(_native.SIGNATURES[name][0]) == n, (name, n, len(_native.SIGNATURES[name][0]))

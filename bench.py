@@ -842,16 +842,7 @@ def mixed_section(dev, peak, steps=10):
     out = []
     for frac in (0.0, 0.25, 0.5, 0.75, 1.0):
         rng = np.random.default_rng(int(frac * 100))
-        n_con = int(round(frac * batch))
-        masks_np = []
-        for _ in range(4):
-            legal = np.zeros((batch, vocab), dtype=bool)
-            order = rng.permutation(batch)
-            for j, b in enumerate(order):
-                ids = (wl.clustered_legal_ids(rng, vocab, int(0.002 * vocab), 16) if j < n_con
-                       else wl.uniform_legal_ids(rng, vocab, int(0.95 * vocab)))
-                legal[b, ids] = True
-            masks_np.append(wl.pack_bitmask(legal))
+        masks_np = [wl.mixed_batch_mask(rng, batch, vocab, frac) for _ in range(4)]
         masks = [torch.from_numpy(m).to(dev) for m in masks_np]
         times = {}
         for name, fn in (("block-sparse", _native.block_gemm), ("dense-mask", _native.dense_masked),

@@ -489,15 +489,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (s_misc[1]) {
     __threadfence();
     if (want_top) {
+      bool ok = true;
       if (p.peers.world > 1) {  // merge across the ranks of a vocabulary-parallel group
         for (int b = tid; b < B; b += kGemmThreads) s_keys[b] = atomicExch(p.keys + b, 0ull);
-        peer_exchange_keys(p.peers, s_keys, B, reinterpret_cast<uint32_t*>(s_misc + 2), p.error);
+        ok = peer_exchange_keys(p.peers, s_keys, B, reinterpret_cast<uint32_t*>(s_misc + 2), p.error);
       }
       for (int b = tid; b < B; b += kGemmThreads) {
         const unsigned long long k = p.peers.world > 1 ? s_keys[b] : atomicExch(p.keys + b, 0ull);
-        if (p.top_value) p.top_value[b] = key_value(k);
-        if (p.top_index) p.top_index[b] = key_index(k);
-        if (p.top_key) p.top_key[b] = key_to_signed(k);
+        store_top1(p.top_value, p.top_index, p.top_key, b, k, ok);
       }
     }
     if (!p.dense)

@@ -128,8 +128,8 @@ int32_t validate_projection(const char* fn, const void* hidden, int64_t hidden_r
   if (!hidden || !weight) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: hidden and weight must be non-null", fn);
   if (batch < 1 || vocab < 1 || hidden_dim < 1)
     return fail(GSP_ERR_INVALID_ARGUMENT, "%s: batch, vocab and hidden_dim must be positive", fn);
-  if (dtype != GSP_DTYPE_F16 && dtype != GSP_DTYPE_BF16)
-    return fail(GSP_ERR_UNSUPPORTED, "%s: dtype must be GSP_DTYPE_F16 or GSP_DTYPE_BF16", fn);
+  if (dtype != GSP_DTYPE_F16 && dtype != GSP_DTYPE_BF16 && dtype != GSP_DTYPE_F32)
+    return fail(GSP_ERR_UNSUPPORTED, "%s: dtype must be GSP_DTYPE_F16, GSP_DTYPE_BF16 or GSP_DTYPE_F32", fn);
   if (batch > 1 && hidden_row_stride < hidden_dim)
     return fail(GSP_ERR_INVALID_ARGUMENT, "%s: hidden_row_stride < hidden_dim", fn);
   if (vocab > 1 && weight_row_stride < hidden_dim)
@@ -207,7 +207,10 @@ int32_t projection_common(const char* fn, bool tensor_core, int dense, const voi
   st = check_workspace(fn, want_top || tensor_core, workspace, workspace_bytes_, batch, vocab);
   if (st != GSP_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (!tensor_core) {
+  // fp32: the tensor-core kernels take half-precision operands, so the block
+  // and dense routes run the row-sparse kernel (same outputs: legal rows dotted
+  // in fp32, -inf elsewhere; the dense route with no mask projects every row)
+  if (!tensor_core || dtype == GSP_DTYPE_F32) {
     RowSparseParams p = make_row_sparse(hidden, hidden_row_stride, weight, weight_row_stride,
                                         bitmask, bitmask_row_stride, batch, vocab, hidden_dim,
                                         vocab_offset);
@@ -423,6 +426,7 @@ int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride, con
   int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
                                    bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
   if (st != GSP_OK) return st;
+  if (dtype == GSP_DTYPE_F32) return fail(GSP_ERR_UNSUPPORTED, "%s: the sampler takes GSP_DTYPE_F16 or GSP_DTYPE_BF16", fn);
   if (!(temperature > 0.f) || !std::isfinite(temperature))
     return fail(GSP_ERR_INVALID_ARGUMENT, "%s: temperature must be positive and finite", fn);
   if (!seeds || !sample_index) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: seeds and sample_index are required", fn);
@@ -522,6 +526,8 @@ int32_t gsp_adaptive_logits(const void* hidden, int64_t hidden_row_stride, const
   int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
                                    bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
   if (st != GSP_OK) return st;
+  if (dtype == GSP_DTYPE_F32)
+    return fail(GSP_ERR_UNSUPPORTED, "%s: fp32 has one route (row-sparse); call gsp_row_sparse_logits", fn);
   if (!bitmask) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask is required", fn);
   st = check_workspace(fn, true, workspace, workspace_bytes_, batch, vocab);
   if (st != GSP_OK) return st;
@@ -720,6 +726,8 @@ int32_t gsp_grouped_logits(const void* hidden, int64_t hidden_row_stride, const 
   int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
                                    bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
   if (st != GSP_OK) return st;
+  if (dtype == GSP_DTYPE_F32)
+    return fail(GSP_ERR_UNSUPPORTED, "%s: fp32 has one route (row-sparse); call gsp_row_sparse_logits", fn);
   if (!bitmask) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: bitmask is required", fn);
   if (batch > kGroupMaxBatch) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: batch %d > %d", fn, batch, kGroupMaxBatch);
   st = check_workspace(fn, true, workspace, workspace_bytes_, batch, vocab);

@@ -14,6 +14,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace gsp {
 
 constexpr unsigned FULL_MASK = 0xffffffffu;
@@ -21,8 +23,11 @@ constexpr unsigned FULL_MASK = 0xffffffffu;
 template <typename T>
 struct DTypeTraits;
 
+// Bits: the storage word of one element; kPerVec: elements per 16-byte vector.
 template <>
 struct DTypeTraits<__half> {
+  using Bits = uint16_t;
+  static constexpr int kPerVec = 8;
   static constexpr uint16_t kNegInfBits = 0xFC00u;
   static __device__ __forceinline__ float2 pair_to_float2(uint32_t v) {
     __half2 h;
@@ -39,6 +44,8 @@ struct DTypeTraits<__half> {
 
 template <>
 struct DTypeTraits<__nv_bfloat16> {
+  using Bits = uint16_t;
+  static constexpr int kPerVec = 8;
   static constexpr uint16_t kNegInfBits = 0xFF80u;
   static __device__ __forceinline__ float2 pair_to_float2(uint32_t v) {
     // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 word.
@@ -50,6 +57,18 @@ struct DTypeTraits<__nv_bfloat16> {
   static __device__ __forceinline__ float bits_to_float(uint16_t u) {
     return __uint_as_float(static_cast<uint32_t>(u) << 16);
   }
+};
+
+// fp32 inputs (the reference's wrappers accept them: the output dtype is the
+// hidden dtype, gsp/triton_runtime.py:111): products accumulate in fp32 and the
+// output is the fp32 sum itself.
+template <>
+struct DTypeTraits<float> {
+  using Bits = uint32_t;
+  static constexpr int kPerVec = 4;
+  static constexpr uint32_t kNegInfBits = 0xFF800000u;
+  static __device__ __forceinline__ uint32_t round_bits(float f) { return __float_as_uint(f); }
+  static __device__ __forceinline__ float bits_to_float(uint32_t u) { return __uint_as_float(u); }
 };
 
 // Order-preserving map float -> uint32 (total order on non-NaN values).
@@ -137,6 +156,21 @@ __device__ __forceinline__ float dot8(uint4 w, uint4 h, float acc) {
   a = DTypeTraits<T>::pair_to_float2(w.w); b = DTypeTraits<T>::pair_to_float2(h.w);
   acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc);
   return acc;
+}
+
+// fp32 dot of one 16-byte vector of weights with one of hidden states
+// (8 half-precision or 4 fp32 elements), accumulated into acc in element order.
+template <typename T>
+__device__ __forceinline__ float dot_vec(uint4 w, uint4 h, float acc) {
+  if constexpr (std::is_same<T, float>::value) {
+    acc = fmaf(__uint_as_float(w.x), __uint_as_float(h.x), acc);
+    acc = fmaf(__uint_as_float(w.y), __uint_as_float(h.y), acc);
+    acc = fmaf(__uint_as_float(w.z), __uint_as_float(h.z), acc);
+    acc = fmaf(__uint_as_float(w.w), __uint_as_float(h.w), acc);
+    return acc;
+  } else {
+    return dot8<T>(w, h, acc);
+  }
 }
 
 }  // namespace gsp

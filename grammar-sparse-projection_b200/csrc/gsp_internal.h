@@ -183,7 +183,8 @@ int32_t record_error(int32_t code, const char* fmt, ...);
 // least `bytes` (thread-safe; a no-op when the current setting suffices).
 cudaError_t raise_smem_limit(const void* func, size_t bytes, int device);
 
-// Each launcher returns a cudaError_t value (cudaSuccess == 0).
+// Each launcher returns a cudaError_t value (cudaSuccess == 0). dtype: 0 fp16,
+// 1 bf16, 2 fp32 (row-sparse kernels only).
 cudaError_t launch_row_sparse(const RowSparseParams& p, int dtype, cudaStream_t stream);
 cudaError_t launch_ids_to_bitmask(const int64_t* ids, int64_t count, int vocab, uint32_t* mask,
                                   unsigned long long* stats, cudaStream_t stream);

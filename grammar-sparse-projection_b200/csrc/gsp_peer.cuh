@@ -23,6 +23,7 @@
 
 #include <stdint.h>
 
+#include "gsp_common.cuh"
 #include "gsp_internal.h"
 
 namespace gsp {
@@ -66,10 +67,13 @@ __device__ __forceinline__ unsigned long long* peer_key_slot(const PeerExchange&
 }
 
 // Called by every thread of ONE CTA with the rank's merged keys in
-// s_keys[0, batch); leaves the group's merged keys there. s_word is one word
-// of shared memory. A wait that runs out sets *error (when given) to 3 and
-// merges what has arrived.
-__device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsigned long long* s_keys, int batch,
+// s_keys[0, batch); leaves the group's merged keys there and returns true.
+// s_word is one word of shared memory. A wait that runs out sets *error (when
+// given) to 3 and returns false on every thread: the keys are then not the
+// group's, and the caller reports no top-1 for the call (its epoch is still
+// recorded, so the host must re-synchronise the group's buffers before the
+// next call).
+__device__ __forceinline__ bool peer_exchange_keys(const PeerExchange& x, unsigned long long* s_keys, int batch,
                                                    uint32_t* s_word, int* error) {
   const int tid = threadIdx.x, nt = blockDim.x;
   unsigned char* self = x.buf[x.rank];
@@ -78,6 +82,7 @@ __device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsign
   __syncthreads();
   const uint32_t e = *s_word;
   const int par = (int)(e & 1u);
+  bool late = false;
   if (x.tagged) {
     for (int i = tid; i < x.world * batch; i += nt) {
       const int q = i / batch, b = i - q * batch;
@@ -94,9 +99,12 @@ __device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsign
         }
         __nanosleep(32);
       }
-      if (!ok && error) atomicExch(error, 3);
+      if (!ok) {
+        late = true;
+        if (error) atomicExch(error, 3);
+      }
     }
-    __syncthreads();
+    const bool failed = __syncthreads_or(late);
     for (int b = tid; b < batch; b += nt) {
       unsigned long long k = 0ull;
       for (int q = 0; q < x.world; ++q) {
@@ -107,7 +115,7 @@ __device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsign
     }
     if (tid == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e;
     __syncthreads();
-    return;
+    return !failed;
   }
   for (int i = tid; i < x.world * batch; i += nt) {
     const int q = i / batch, b = i - q * batch;
@@ -126,9 +134,12 @@ __device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsign
       }
       __nanosleep(64);
     }
-    if (!ok && error) atomicExch(error, 3);
+    if (!ok) {
+      late = true;
+      if (error) atomicExch(error, 3);
+    }
   }
-  __syncthreads();
+  const bool failed = __syncthreads_or(late);
   for (int b = tid; b < batch; b += nt) {
     unsigned long long k = 0ull;
     for (int q = 0; q < x.world; ++q) {
@@ -139,6 +150,17 @@ __device__ __forceinline__ void peer_exchange_keys(const PeerExchange& x, unsign
   }
   if (tid == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e;
   __syncthreads();
+  return !failed;
+}
+
+// Writes request b's decoded top-1 from its merged key k. With ok false (a
+// cross-rank wait ran out) no token is reported: index -1, value NaN, key
+// INT64_MIN, which a caller tells apart from every real result.
+__device__ __forceinline__ void store_top1(float* top_value, int64_t* top_index, int64_t* top_key, int b,
+                                           unsigned long long k, bool ok) {
+  if (top_value) top_value[b] = ok ? key_value(k) : __int_as_float(0x7fc00000);
+  if (top_index) top_index[b] = ok ? key_index(k) : -1;
+  if (top_key) top_key[b] = ok ? key_to_signed(k) : INT64_MIN;
 }
 
 }  // namespace gsp

@@ -180,10 +180,11 @@ template <typename T, bool kSample>
 __device__ __forceinline__ void emit_unit(const RowSparseParams& p, int b, int v, uint64_t rank, float acc,
                                           bool want_top, RunningTop& top, unsigned long long* s_keys,
                                           RunningSample& rs, int ui) {
-  const uint16_t bits = DTypeTraits<T>::round_bits(acc);
-  if (p.logits) static_cast<uint16_t*>(p.logits)[(int64_t)b * p.logits_stride + v] = bits;
+  using Bits = typename DTypeTraits<T>::Bits;
+  const Bits bits = DTypeTraits<T>::round_bits(acc);
+  if (p.logits) static_cast<Bits*>(p.logits)[(int64_t)b * p.logits_stride + v] = bits;
   if (p.compact && rank < (uint64_t)p.capacity) {
-    static_cast<uint16_t*>(p.compact)[rank] = bits;
+    static_cast<Bits*>(p.compact)[rank] = bits;
     p.compact_ids[rank] = p.vocab_offset + v;
   }
   if (want_top)
@@ -271,15 +272,14 @@ __device__ __forceinline__ void sample_finish(const RowSparseParams& p) {
 // writes the decoded top-1. All threads of the CTA call it.
 __device__ __forceinline__ void decode_top1(const RowSparseParams& p, unsigned long long* s_keys, uint32_t* s_word) {
   const int tid = threadIdx.x;
+  bool ok = true;
   if (p.peers.world > 1) {
     for (int b = tid; b < p.batch; b += blockDim.x) s_keys[b] = atomicExch(p.keys + b, 0ull);
-    peer_exchange_keys(p.peers, s_keys, p.batch, s_word, p.error);
+    ok = peer_exchange_keys(p.peers, s_keys, p.batch, s_word, p.error);
   }
   for (int b = tid; b < p.batch; b += blockDim.x) {
     const unsigned long long k = p.peers.world > 1 ? s_keys[b] : atomicExch(p.keys + b, 0ull);
-    if (p.top_value) p.top_value[b] = key_value(k);
-    if (p.top_index) p.top_index[b] = key_index(k);
-    if (p.top_key) p.top_key[b] = key_to_signed(k);
+    store_top1(p.top_value, p.top_index, p.top_key, b, k, ok);
   }
 }
 
@@ -326,7 +326,8 @@ __device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w
                                              int t0 = 0, int nt = 0) {
   const int V = p.vocab, nw = p.nw;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 15) == 0) && (p.logits_stride % 8 == 0);
-  const uint16_t ninf = DTypeTraits<T>::kNegInfBits;
+  using Bits = typename DTypeTraits<T>::Bits;
+  const Bits ninf = DTypeTraits<T>::kNegInfBits;
   if (nt == 0) nt = blockDim.x;
   const int me = (int)threadIdx.x - t0;
   if (me < 0 || me >= nt) return;
@@ -337,10 +338,15 @@ __device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w
     const uint32_t byte = (word_of(f, b, w) >> (q * 8)) & 0xffu;
     const int row0 = w * 32 + q * 8;
     if (row0 >= V || byte == 0xffu) continue;
-    uint16_t* dst = static_cast<uint16_t*>(p.logits) + (int64_t)b * p.logits_stride + row0;
+    Bits* dst = static_cast<Bits*>(p.logits) + (int64_t)b * p.logits_stride + row0;
     if (byte == 0u && vec_ok && row0 + 8 <= V) {
-      const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(x, x, x, x);
+      if constexpr (sizeof(Bits) == 2) {
+        const uint32_t x = (uint32_t)ninf | ((uint32_t)ninf << 16);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(x, x, x, x);
+      } else {
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(ninf, ninf, ninf, ninf);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(ninf, ninf, ninf, ninf);
+      }
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e)
@@ -353,10 +359,11 @@ __device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w
 // With kHSmem, s_h holds the hidden rows of requests b0, b0 + 1, ... .
 template <typename T, bool kHSmem, bool kSample>
 __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint32_t* s_list, int n, uint64_t rbase,
-                                            uint32_t code_stride, const uint16_t* s_h, int b0, bool want_top,
+                                            uint32_t code_stride, const void* s_h, int b0, bool want_top,
                                             unsigned long long* s_keys) {
+  using Bits = typename DTypeTraits<T>::Bits;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int H = p.hidden_dim, nvec = H / 8;
+  const int H = p.hidden_dim, nvec = H / DTypeTraits<T>::kPerVec;
   RunningTop top;
   RunningSample rs;
   for (int i = warp; i < n; i += 2 * kWarps) {
@@ -365,13 +372,13 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
     const uint32_t ca = s_list[i], cb = has2 ? s_list[j] : ca;
     const int ba = (int)(ca / code_stride), va = (int)(ca - (uint32_t)ba * code_stride);
     const int bb = (int)(cb / code_stride), vb = (int)(cb - (uint32_t)bb * code_stride);
-    const uint16_t* wa = static_cast<const uint16_t*>(p.weight) + (int64_t)va * p.weight_stride;
-    const uint16_t* wb = static_cast<const uint16_t*>(p.weight) + (int64_t)vb * p.weight_stride;
-    const uint4* ha = kHSmem ? reinterpret_cast<const uint4*>(s_h + (size_t)(ba - b0) * H)
-                             : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) +
+    const uint4* wa = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)va * p.weight_stride);
+    const uint4* wb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)vb * p.weight_stride);
+    const uint4* ha = kHSmem ? reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)(ba - b0) * H)
+                             : reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) +
                                                               (int64_t)ba * p.hidden_stride);
-    const uint4* hb = kHSmem ? reinterpret_cast<const uint4*>(s_h + (size_t)(bb - b0) * H)
-                             : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) +
+    const uint4* hb = kHSmem ? reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)(bb - b0) * H)
+                             : reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) +
                                                               (int64_t)bb * p.hidden_stride);
     float acc_a = 0.f, acc_b = 0.f;
     for (int base = 0; base < nvec; base += 32 * kUnroll) {
@@ -379,15 +386,15 @@ __device__ __forceinline__ void stream_rows(const RowSparseParams& p, const uint
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const int e = base + u * 32 + lane;
-        ra[u] = e < nvec ? ld_stream_v4(wa + e * 8) : make_uint4(0, 0, 0, 0);
-        rb[u] = (has2 && e < nvec) ? ld_stream_v4(wb + e * 8) : make_uint4(0, 0, 0, 0);
+        ra[u] = e < nvec ? ld_stream_v4(wa + e) : make_uint4(0, 0, 0, 0);
+        rb[u] = (has2 && e < nvec) ? ld_stream_v4(wb + e) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const int e = base + u * 32 + lane;
         if (e < nvec) {
-          acc_a = dot8<T>(ra[u], kHSmem ? ha[e] : __ldg(ha + e), acc_a);
-          if (has2) acc_b = dot8<T>(rb[u], kHSmem ? hb[e] : __ldg(hb + e), acc_b);
+          acc_a = dot_vec<T>(ra[u], kHSmem ? ha[e] : __ldg(ha + e), acc_a);
+          if (has2) acc_b = dot_vec<T>(rb[u], kHSmem ? hb[e] : __ldg(hb + e), acc_b);
         }
       }
     }
@@ -417,8 +424,9 @@ __device__ __forceinline__ void stream_rows_scalar(const RowSparseParams& p, con
   for (int i = warp; i < n; i += kWarps) {
     const uint32_t c = s_list[i];
     const int b = (int)(c / code_stride), v = (int)(c - (uint32_t)b * code_stride);
-    const uint16_t* w = static_cast<const uint16_t*>(p.weight) + (int64_t)v * p.weight_stride;
-    const uint16_t* h = static_cast<const uint16_t*>(p.hidden) + (int64_t)b * p.hidden_stride;
+    using Bits = typename DTypeTraits<T>::Bits;
+    const Bits* w = static_cast<const Bits*>(p.weight) + (int64_t)v * p.weight_stride;
+    const Bits* h = static_cast<const Bits*>(p.hidden) + (int64_t)b * p.hidden_stride;
     float acc = 0.f;
     for (int k = lane; k < H; k += 32)
       acc = fmaf(DTypeTraits<T>::bits_to_float(__ldg(w + k)), DTypeTraits<T>::bits_to_float(__ldg(h + k)), acc);
@@ -466,7 +474,7 @@ struct StagedLayout {
 };
 
 // `words` = number of mask words staged (kThreads * words per thread).
-__host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim, int words) {
+__host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim, int words, int elem_bytes) {
   StagedLayout l;
   size_t off = 0;
   l.list = off;
@@ -482,7 +490,7 @@ __host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim,
   l.pre = align_up(off, 16);
   off = l.pre + 4 * (size_t)words;
   l.hidden = align_up(off, 16);
-  off = l.hidden + 2 * (size_t)batch * hidden_dim;
+  off = l.hidden + (size_t)elem_bytes * batch * hidden_dim;
   l.total = align_up(off, 128);
   return l;
 }
@@ -505,19 +513,20 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   // runs; nothing is read or written before that kernel has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(1024) unsigned char smem[];
-  const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * kWpt);
+  using Bits = typename DTypeTraits<T>::Bits;
+  const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * kWpt, (int)sizeof(Bits));
   uint32_t* s_list = reinterpret_cast<uint32_t*>(smem + L.list);
   unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
   uint32_t* s_warp = reinterpret_cast<uint32_t*>(smem + L.warp);
   int* s_misc = reinterpret_cast<int*>(smem + L.misc);
   uint32_t* s_words = reinterpret_cast<uint32_t*>(smem + L.words);
   uint32_t* s_pre = reinterpret_cast<uint32_t*>(smem + L.pre);
-  uint16_t* s_h = reinterpret_cast<uint16_t*>(smem + L.hidden);
+  Bits* s_h = reinterpret_cast<Bits*>(smem + L.hidden);
 
   const int tid = threadIdx.x;
   const int G = gridDim.x, cta = blockIdx.x;
   const int B = p.batch, V = p.vocab, H = p.hidden_dim, nw = p.nw;
-  const int nvec = H / 8;
+  const int nvec = H / DTypeTraits<T>::kPerVec;
   const bool has_mask = p.mask != nullptr;
   const bool want_top = (p.top_value != nullptr) | (p.top_index != nullptr) | (p.top_key != nullptr);
   const int F = has_mask ? B * nw : 0;  // <= kThreads * kWpt (checked on the host)
@@ -565,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   for (int i = tid; i < B * nvec; i += kThreads) {
     const int b = i / nvec, j = i - b * nvec;
     reinterpret_cast<uint4*>(s_h)[i] = __ldg(
-        reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
+        reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
   }
   for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
   if constexpr (kSample) sample_smem_init(p, s_keys);
@@ -922,7 +931,7 @@ __device__ __forceinline__ uint32_t scan_chunk(const RowSparseParams& p, int c0,
 // the error word and is skipped, so no address is ever formed from it.
 template <typename T, bool kSample>
 __device__ __forceinline__ void coop_stream_round(const RowSparseParams& p, const uint32_t* s_list, int n,
-                                                  uint32_t rbase, uint32_t code_stride, uint16_t* s_h, int& h_lo,
+                                                  uint32_t rbase, uint32_t code_stride, void* s_h, int& h_lo,
                                                   int& h_hi, bool want_top, unsigned long long* s_keys) {
   const int tid = threadIdx.x, H = p.hidden_dim;
   bool bad = false;
@@ -937,13 +946,14 @@ __device__ __forceinline__ void coop_stream_round(const RowSparseParams& p, cons
   }
   round_noise<kSample>(p, sample_smem(s_keys, p.batch), s_list, n, code_stride);
   const int rb0 = (int)(s_list[0] / code_stride), rb1 = (int)(s_list[n - 1] / code_stride);
-  if ((size_t)(rb1 - rb0 + 1) * H * 2 <= (size_t)kHStageBytes) {
+  using Bits = typename DTypeTraits<T>::Bits;
+  if ((size_t)(rb1 - rb0 + 1) * H * sizeof(Bits) <= (size_t)kHStageBytes) {
     if (rb0 < h_lo || rb1 >= h_hi) {
-      const int nvec = H / 8;
+      const int nvec = H / DTypeTraits<T>::kPerVec;
       for (int i = tid; i < (rb1 - rb0 + 1) * nvec; i += kThreads) {
         const int b = rb0 + i / nvec, j = i - (i / nvec) * nvec;
         reinterpret_cast<uint4*>(s_h)[i] = __ldg(
-            reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
+            reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
       }
       h_lo = rb0;
       h_hi = rb1 + 1;
@@ -1028,7 +1038,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowS
   uint32_t* s_base = reinterpret_cast<uint32_t*>(smem + L.base);
   uint32_t* s_words = reinterpret_cast<uint32_t*>(smem + L.words);
   uint32_t* s_pre = reinterpret_cast<uint32_t*>(smem + L.pre);
-  uint16_t* s_h = reinterpret_cast<uint16_t*>(smem + L.hidden);
+  void* s_h = smem + L.hidden;
 
   const int tid = threadIdx.x, G = gridDim.x, cta = blockIdx.x;
   const int B = p.batch, nw = p.nw, F = B * nw;
@@ -1222,9 +1232,10 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
   const int grid = num_sms(dev);
-  const bool vec = (p.hidden_dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.weight) & 15) == 0) &&
-                   (p.weight_stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.hidden) & 15) == 0) &&
-                   (p.batch == 1 || p.hidden_stride % 8 == 0);
+  constexpr int kPV = DTypeTraits<T>::kPerVec;
+  const bool vec = (p.hidden_dim % kPV == 0) && ((reinterpret_cast<uintptr_t>(p.weight) & 15) == 0) &&
+                   (p.weight_stride % kPV == 0) && ((reinterpret_cast<uintptr_t>(p.hidden) & 15) == 0) &&
+                   (p.batch == 1 || p.hidden_stride % kPV == 0);
   const int64_t F64 = p.mask ? (int64_t)p.batch * p.nw : 0;
   if (vec && F64 > kCoopMinWords && p.slice_counts != nullptr && p.published != nullptr && p.slice_ready != nullptr &&
       F64 * 32 < (int64_t)1 << 32) {
@@ -1248,7 +1259,7 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
   if (vec) {
     const int F = p.mask ? p.batch * p.nw : 0;
     const int wpt = F <= kThreads * 16 ? 16 : 32;
-    const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * wpt);
+    const StagedLayout L = staged_layout(p.batch, p.hidden_dim, kThreads * wpt, (int)sizeof(typename DTypeTraits<T>::Bits));
     if (L.total <= kStagedSmemMax && F <= kThreads * 32) {
       auto k = wpt == 16 ? row_sparse_staged_kernel<T, 4, kSample> : row_sparse_staged_kernel<T, 8, kSample>;
       if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
@@ -1282,6 +1293,10 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
 
 cudaError_t launch_row_sparse(const RowSparseParams& p, int dtype, cudaStream_t stream) {
   const bool sample = p.sample_index != nullptr;
+  if (dtype == 2) {
+    if (sample) return cudaErrorNotSupported;  // the sampler takes half-precision inputs only
+    return launch_typed<float, false>(p, stream);
+  }
   if (dtype == 1) return sample ? launch_typed<__nv_bfloat16, true>(p, stream) : launch_typed<__nv_bfloat16, false>(p, stream);
   return sample ? launch_typed<__half, true>(p, stream) : launch_typed<__half, false>(p, stream);
 }

@@ -22,7 +22,7 @@ GSP_ERR_WORKSPACE = -3
 GSP_ERR_CUDA = -4
 TILE_ROWS = 128
 
-DTYPE_CODES = {torch.float16: 0, torch.bfloat16: 1}
+DTYPE_CODES = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 
 
 class GSPNativeError(RuntimeError):
@@ -66,6 +66,7 @@ SIGNATURES = {
     "gsp_top1_from_keys": ([_vp, _i32, _vp, _vp, _vp], _i32),
     "gsp_row_sparse_logits_static": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64,
                                       _vp, _i64, _vp, _vp, _vp, _vp], _i32),
+    "gsp_row_sparse_static_error": ([ctypes.POINTER(_i32), _vp], _i32),
     "gsp_row_sparse_sample": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _vp, _i64,
                                ctypes.c_float, _vp, ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                _vp], _i32),
@@ -135,7 +136,7 @@ def dtype_code(dtype: torch.dtype) -> int:
     try:
         return DTYPE_CODES[dtype]
     except KeyError:
-        raise ValueError(f"unsupported dtype {dtype}: the B200 kernels take float16 or bfloat16") from None
+        raise ValueError(f"unsupported dtype {dtype}: the B200 kernels take float16, bfloat16 or float32") from None
 
 
 # ---------------------------------------------------------------------------

@@ -46,6 +46,8 @@ class GraphedGrammarHead:
         if weight.device.type != "cuda" or weight.ndim != 2:
             raise ValueError("weight must be a CUDA [V, H] tensor")
         _native.dtype_code(weight.dtype)
+        if weight.dtype == torch.float32:
+            raise ValueError("GraphedGrammarHead takes float16 or bfloat16 weights")
         if batch < 1:
             raise ValueError("batch must be positive")
         dev = weight.device

@@ -97,6 +97,14 @@ def _sparse_inputs(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torc
     return hidden_2d, mask_2d, squeeze, batch, vocab
 
 
+def _half_only(dtype: torch.dtype, what: str) -> None:
+    """The device route selector, lane grouping and the sampler take
+    half-precision inputs; float32 heads have one route (row-sparse), which
+    the reference API functions run for every route name."""
+    if dtype == torch.float32:
+        raise ValueError(f"{what} takes float16 or bfloat16; float32 runs the row-sparse kernel on every route")
+
+
 def _block_inputs(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torch.Tensor):
     """gsp/triton_runtime.py:222-239."""
     if hidden.ndim != 2 or hidden.shape[0] < 2:
@@ -327,6 +335,8 @@ def adaptive_grammar_logits(
     a split reports its routes joined by "+", e.g. "row-sparse+block-sparse".
     """
     batch = 1 if hidden.ndim == 1 else hidden.shape[0]
+    if policy in ("grouped", "device"):
+        _half_only(hidden.dtype, f"policy={policy!r}")
     if policy == "grouped":
         if full_word_fraction is not None and len(full_word_fraction) != batch:
             raise ValueError("full_word_fraction length must equal batch")
@@ -424,6 +434,7 @@ def grammar_head(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torch.
     capturing). Warm up once outside capture on the capturing stream.
     """
     hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
+    _half_only(hidden.dtype, "grammar_head")
     dev = hidden.device
     if out is None:
         out = HeadResult(
@@ -462,6 +473,7 @@ def grouped_grammar_logits(hidden: torch.Tensor, weight: torch.Tensor, bitmask_g
     capturable in a CUDA graph (grammar_head is).
     """
     hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
+    _half_only(hidden.dtype, "grouped_grammar_logits")
     if batch > _native.GROUP_MAX_BATCH:
         raise ValueError(f"grouped_grammar_logits takes at most {_native.GROUP_MAX_BATCH} requests")
     dev = hidden.device
@@ -502,6 +514,7 @@ def grammar_sample(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torc
     greedy top-1 comes with it. Shapes are [B, ...] always.
     """
     hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
+    _half_only(hidden.dtype, "grammar_sample")
     if seeds.device.type != "cuda" or seeds.dtype != torch.int64 or seeds.numel() != batch:
         raise ValueError("seeds must be a CUDA int64 tensor with one seed per request")
     if not (temperature > 0.0) or temperature == float("inf"):

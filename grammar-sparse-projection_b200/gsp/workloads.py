@@ -80,6 +80,22 @@ def make_batch_mask(rng: np.random.Generator, batch: int, vocab: int, k_per_requ
     return pack_bitmask(legal)
 
 
+def mixed_batch_mask(rng: np.random.Generator, batch: int, vocab: int, constrained_fraction: float, *,
+                     dense_density: float = 0.95, sparse_density: float = 0.002, max_runs: int = 16) -> np.ndarray:
+    """Mixed-density batch of the dispatcher sweep: round(fraction * batch)
+    requests at random positions are constrained (sparse_density of the tokens
+    legal, in <= max_runs clustered runs), the others near-unconstrained
+    (dense_density legal, drawn uniformly)."""
+    n_con = int(round(constrained_fraction * batch))
+    legal = np.zeros((batch, vocab), dtype=bool)
+    order = rng.permutation(batch)
+    for j, b in enumerate(order):
+        ids = (clustered_legal_ids(rng, vocab, int(sparse_density * vocab), max_runs) if j < n_con
+               else uniform_legal_ids(rng, vocab, int(dense_density * vocab)))
+        legal[b, ids] = True
+    return pack_bitmask(legal)
+
+
 def legal_counts(mask, vocab: int) -> np.ndarray:
     """Legal tokens per request."""
     return unpack_bitmask(mask, vocab).sum(axis=1)

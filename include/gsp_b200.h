@@ -14,8 +14,14 @@
  *     (outer) dimension; the inner dimension is contiguous.
  *   - `stream` is a cudaStream_t handle passed as void* (NULL = legacy default
  *     stream). Every call is asynchronous on that stream: no host sync.
- *   - `dtype`: GSP_DTYPE_F16 or GSP_DTYPE_BF16; hidden, weight and the logits
- *     share it. Accumulation is fp32, rounded once to `dtype`.
+ *   - `dtype`: GSP_DTYPE_F16, GSP_DTYPE_BF16 or GSP_DTYPE_F32; hidden, weight
+ *     and the logits share it. Accumulation is fp32, rounded once to `dtype`.
+ *     The reference's wrappers take any floating dtype (the output dtype is
+ *     the hidden dtype, gsp/triton_runtime.py:111; gsp/runtime.py:46-51 is a
+ *     plain F.linear). fp32 runs on the row-sparse kernels only: the block and
+ *     dense entry points given GSP_DTYPE_F32 run the row-sparse kernel (same
+ *     outputs), and the sampler, adaptive and grouped entry points return
+ *     GSP_ERR_UNSUPPORTED for it.
  *   - `vocab_offset` shifts the token ids reported in top_index / compact ids,
  *     for a weight that is one contiguous row shard of a larger vocabulary.
  *   - Optional outputs may be NULL.
@@ -51,6 +57,7 @@ extern "C" {
 
 #define GSP_DTYPE_F16 0
 #define GSP_DTYPE_BF16 1
+#define GSP_DTYPE_F32 2
 
 /* Rows of one vocabulary tile for the block and dense GEMM paths and for the
  * active-tile statistics. */
@@ -158,12 +165,15 @@ int32_t gsp_dense_masked_logits(const void* hidden, int64_t hidden_row_stride,
  * the library, kept on every GPU that loads it until exit, so batch must be
  * <= GSP_STATIC_MAX_BATCH and vocab <= GSP_STATIC_MAX_VOCAB (larger sizes fail
  * with GSP_ERR_INVALID_ARGUMENT and a message in gsp_last_error()).
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture. Each call clears the scratch it needs on `stream` and
- * allocates nothing. All calls share the one array: calls that may run at the
- * same time on the GPU (other streams, other host threads) race on it and
- * must be serialised by the caller.
+ * The first call on each device (and CUDA context) looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture. Each call first launches a small
+ * clearing kernel on `stream` that zeroes the scratch it needs (no memory is
+ * allocated), then the projection. All calls share the one array: calls that
+ * may run at the same time on the GPU (other streams, other host threads)
+ * race on it and must be serialised by the caller. A kernel that gave up a
+ * bounded wait leaves an error word in the array; it is kept across calls
+ * until gsp_row_sparse_static_error reads it.
  * No counterpart in the reference.
  */
 #define GSP_STATIC_MAX_BATCH 1024
@@ -175,6 +185,17 @@ int32_t gsp_row_sparse_logits_static(const void* hidden, int64_t hidden_row_stri
                                      int32_t dtype, int64_t vocab_offset, void* logits,
                                      int64_t logits_row_stride, float* top_value,
                                      int64_t* top_index, int64_t* top_key, void* stream);
+
+/*
+ * Reads and clears the error word of gsp_row_sparse_logits_static's scratch on
+ * the current device: *error = 0 when every call since the last read ran to
+ * completion, else the code of the first wait that gave up (4: a row copy did
+ * not land). Synchronises `stream` (call it after the calls to be checked have
+ * been issued on that stream); when the word was set, re-zeroes the whole
+ * scratch array on `stream`. Allocates nothing. No counterpart in the
+ * reference.
+ */
+int32_t gsp_row_sparse_static_error(int32_t* error, void* stream);
 
 /*
  * Decode top-1 keys (e.g. after an integer MAX all-reduce across vocabulary

@@ -199,7 +199,7 @@ def test_constrained_projection_golden(cuda_device):
     meta = json.loads(str(data["meta"]))
     for c in meta:
         if c["name"].startswith("config0"):
-            continue  # fp32: checked below in fp16
+            continue  # the fp32 configuration: test_gpu_fp32.py
         w, h = O.projection_case_inputs(c["dtype"], c["seed"])
         if c["hidden_1d"]:
             h = h[0]
@@ -225,9 +225,10 @@ def test_constrained_projection_errors_and_config0(cuda_device):
         rt.constrained_projection(h, w, torch.tensor([5, 100]))
     with pytest.raises(ValueError, match="one-dimensional"):
         rt.constrained_projection(h, w, torch.tensor([[1, 2]]))
-    with pytest.raises(ValueError, match="float16 or bfloat16"):
-        rt.constrained_projection(h.float(), w.float(), torch.tensor([1]))
-    # 32,768 x 1,024, batch 1, 1% uniform (seed 0), in fp16
+    with pytest.raises(ValueError, match="unsupported dtype"):
+        rt.constrained_projection(h.double(), w.double(), torch.tensor([1]))
+    # 32,768 x 1,024, batch 1, 1% uniform (seed 0), also in fp16 (the fp32
+    # configuration itself is checked in test_gpu_fp32.py)
     w32, h32, ids = O.config0_inputs(seed=0)
     w16, h16 = w32.half(), h32.half()
     res = rt.constrained_projection(h16.to(cuda_device), w16.to(cuda_device), torch.from_numpy(ids).to(cuda_device))

@@ -69,7 +69,7 @@ def test_reference_block_gemm_test_shapes(cuda_device):
         _check(O.masked_logits_exact(hd.cpu(), w, mask), got, torch.float16, f"batch={batch}")
 
 
-@pytest.mark.parametrize("batch", [2, 8, 32])
+@pytest.mark.parametrize("batch", [2, 4, 8, 16, 32])
 def test_batched_clustered_workload(cuda_device, batch):
     """V=248,320, H=2,048 fp16, each request 0.5% legal in <= 16 clustered runs."""
     vocab, hidden = 248320, 2048

@@ -65,6 +65,54 @@ def test_static_entry_matches_workspace_entry_twice(cuda_device, dtype):
         assert got[2][1].item() == 0 and got[1][1].item() == float("-inf")  # empty legal set
 
 
+def _static_error(lib):
+    err = ctypes.c_int32(-1)
+    status = lib.gsp_row_sparse_static_error(ctypes.byref(err),
+                                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert status == _native.GSP_OK, lib.gsp_last_error()
+    return err.value
+
+
+# (batch, vocab, hidden): a batch whose flat mask (62,080 words) is above the
+# multi-request threshold, the largest batch on a small vocabulary, and the
+# largest vocabulary at batch 1; run in this order, so each call finds the
+# scratch as a call of another size left it.
+_LIMIT_CASES = [(8, 248_320, 256), (STATIC_MAX_BATCH, 2_000, 64), (1, STATIC_MAX_VOCAB, 64), (8, 248_320, 256)]
+
+
+def test_static_entry_large_batches_and_limits(cuda_device):
+    lib = _native.load()
+    assert _static_error(lib) == 0
+    rng = np.random.default_rng(77)
+    dtype = torch.float16
+    for batch, vocab, hidden in _LIMIT_CASES:
+        w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * np.float32(0.02)).to(dtype)
+        h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).to(dtype)
+        legal = [int(x) for x in rng.integers(0, max(2, vocab // 100), size=batch)]
+        legal[0] = 0
+        mask = O.make_batch_mask(rng, batch, vocab, legal, clustered=batch % 2 == 0, max_runs=16)
+        wd, hd, md = w.to(cuda_device), h.to(cuda_device), torch.from_numpy(mask).to(cuda_device)
+        ref = _outputs(batch, vocab, cuda_device, dtype)
+        _native.row_sparse(hd, wd, md, logits=ref[0], top_value=ref[1], top_index=ref[2], top_key=ref[3])
+        got = _outputs(batch, vocab, cuda_device, dtype)
+        for _ in range(2):  # two calls in a row on the same inputs
+            got[0].fill_(0)
+            status = _static_call(hd, wd, md, *got)
+            assert status == _native.GSP_OK, lib.gsp_last_error()
+            torch.cuda.synchronize()
+            rep = O.compare_logits(ref[0].cpu().double(), got[0].cpu(), dtype=dtype)
+            assert rep["support"] and rep["values"], (batch, vocab, rep)
+            assert torch.equal(got[2], ref[2]) and torch.equal(got[3], ref[3]), (batch, vocab)
+        sel = slice(0, min(batch, 64))  # the oracle on a slice of the batch
+        exact = O.masked_logits_exact(h[sel], w, mask[sel])
+        rep = O.compare_logits(exact, got[0][sel].cpu(), dtype=dtype)
+        assert rep["support"] and rep["values"], (batch, vocab, rep)
+        assert got[2][0].item() == 0 and got[1][0].item() == float("-inf")  # request 0 has no legal token
+        assert _static_error(lib) == 0
+        del w, wd, ref, got
+        torch.cuda.empty_cache()
+
+
 def test_static_entry_rejects_sizes_beyond_its_scratch(cuda_device):
     lib = _native.load()
     h = torch.zeros(1, 8, device=cuda_device, dtype=torch.float16)

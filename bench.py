@@ -69,10 +69,13 @@ def parse_args():
     ap.add_argument("--sweep-steps", type=int, default=100)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-vp", action="store_true", help="skip the vocabulary-parallel head section")
-    ap.add_argument("--only", choices=("batched", "mixed", "vp", "sampler", "graphed", "groups"), default=None,
+    ap.add_argument("--only", choices=("batched", "mixed", "vp", "sampler", "graphed", "groups", "reference-triton",
+                                       "kernel"),
+                    default=None,
                     help="run one extra section alone (small; for profiling)")
     ap.add_argument("--batch", type=int, default=32, help="batch of --only batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-out", default=None, help="(reference-triton child) file for its step-0 logits")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -103,16 +106,67 @@ def read_peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def read_profile_traffic(kernel: str):
-    """Per-launch DRAM traffic recorded from an ncu capture in profiles/."""
-    path = os.path.join(REPO, "profiles", f"{kernel}.md")
+TRAFFIC_CSV = os.path.join("profiles", "row_sparse_staged_b1_1pct_dram.csv")
+
+
+def read_traffic_csv(kernel_substr: str = "row_sparse_staged_kernel", path: str = TRAFFIC_CSV):
+    """Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum,
+    mean over the captured launches of `kernel_substr`) from an ncu CSV
+    (`ncu --csv --print-units base --metrics ...`) committed under profiles/.
+    Returns (bytes or None, source description). Not measured by this run:
+    the capture's command is in the CSV's companion summary."""
+    import csv
+    full = os.path.join(REPO, path)
     try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].strip().split()[0])
+        rows = list(csv.DictReader(open(full)))
     except OSError:
-        pass
-    return None
+        return None, f"no ncu capture at {path}"
+    per_launch = {}
+    for r in rows:
+        if kernel_substr not in r.get("Kernel Name", ""):
+            continue
+        if r.get("Metric Name") in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            unit = (r.get("Metric Unit") or "byte").strip()
+            scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(unit, 1)
+            per_launch[r["ID"]] = per_launch.get(r["ID"], 0.0) + float(r["Metric Value"].replace(",", "")) * scale
+    if not per_launch:
+        return None, f"no {kernel_substr} launch in {path}"
+    return (statistics.mean(per_launch.values()),
+            f"ncu capture committed at {path} ({len(per_launch)} launches), not this run")
+
+
+def exact_check(hidden, weight, mask, logits, top_index, *, rtol=2e-3, atol=2e-3, chunk_rows=32768):
+    """Checks one timed step's outputs on the device against exact float64
+    products (plain torch): legal support bit-exact (-inf on every illegal
+    token), each legal logit within atol + max(rtol |x|, half an output ulp),
+    the fused top-1 equal to argmax of the logits and within the near-tie
+    window of the exact maximum. Returns a small dict for the JSON line."""
+    batch, vocab = logits.shape
+    v = torch.arange(vocab, device=logits.device)
+    legal = ((mask.reshape(batch, -1)[:, v >> 5] >> (v & 31)) & 1).bool()
+    lg = logits.double()
+    support = bool(torch.equal(torch.isfinite(lg), legal)) and bool(torch.isneginf(lg[~legal]).all())
+    h64 = hidden.double()
+    exact = torch.empty(batch, vocab, dtype=torch.float64, device=logits.device)
+    for r0 in range(0, vocab, chunk_rows):
+        r1 = min(vocab, r0 + chunk_rows)
+        exact[:, r0:r1] = h64 @ weight[r0:r1].double().T
+    exact.masked_fill_(~legal, float("-inf"))
+    mant = {torch.float16: 10, torch.bfloat16: 7}.get(logits.dtype, 23)
+    fin = legal
+    ax = exact[fin].abs().clamp_min(2.0 ** -14)
+    half_ulp = 0.5 * torch.exp2(torch.floor(torch.log2(ax)) - mant)
+    diff = (lg[fin] - exact[fin]).abs()
+    values = bool((diff <= atol + torch.maximum(rtol * exact[fin].abs(), half_ulp)).all()) if fin.any() else True
+    top_ok = bool(torch.equal(top_index.reshape(-1), logits.argmax(-1)))
+    best = exact.max(dim=-1).values
+    picked = exact.gather(1, top_index.reshape(-1, 1))[:, 0]
+    window = atol + torch.maximum(rtol * best.abs(), torch.exp2(torch.floor(torch.log2(best.abs().clamp_min(2.0 ** -14))) - mant))
+    has = torch.isfinite(best)
+    top_ok &= bool(((best - picked <= window) | ~has).all())
+    return {"support": support, "values": values, "top1": top_ok,
+            "max_abs_err": float(diff.max()) if fin.any() else 0.0,
+            "method": "float64 torch products on the device, the tolerance of the parity tests"}
 
 
 # ---------------------------------------------------------------------------
@@ -206,6 +260,110 @@ def time_cpu_steps(weight_cpu: np.ndarray, hidden_cpu: np.ndarray, masks: np.nda
     return legal_bytes / el / 1e9, el / done * 1e6, done
 
 
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def reference_runtime():
+    """The reference's own gsp/runtime.py from the unmodified copy under
+    baseline/_ref (baseline/install_reference.py), loaded under its own module
+    name; None when the copy is absent."""
+    import importlib.util
+    path = os.path.join(REF_DIR, "gsp", "runtime.py")
+    if not os.path.exists(path):
+        return None
+    spec = importlib.util.spec_from_file_location("gsp_reference_runtime", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def time_cpu_reference_sparse(weight_cpu: np.ndarray, hidden_cpu: np.ndarray, masks: np.ndarray,
+                              steps: int | None, seconds: float | None):
+    """The reference's own CPU path for the step (gsp/runtime.py:16-51,
+    constrained_projection on CPU tensors; sparse-gather below 30% legal):
+    the mask row's legal ids, the projection of those rows, the -inf-filled
+    vocabulary row and its argmax. Returns (GB/s, us/step, steps) or None."""
+    from gsp import workloads as wl
+    ref = reference_runtime()
+    if ref is None:
+        return None
+    w = torch.from_numpy(weight_cpu)
+    h = torch.from_numpy(hidden_cpu)
+    counts = legal_counts(masks)
+    done, legal_bytes, t0 = 0, 0, time.perf_counter()
+    while True:
+        m = masks[done % len(masks)][None]
+        ids = torch.from_numpy(np.flatnonzero(wl.unpack_bitmask(m, VOCAB)[0]))
+        res = ref.constrained_projection(h, w, ids)
+        full = torch.full((VOCAB,), float("-inf"), dtype=w.dtype)
+        full[res.token_ids] = res.logits[0]
+        int(full.argmax())
+        legal_bytes += int(counts[done % len(masks)]) * HIDDEN * 2
+        done += 1
+        el = time.perf_counter() - t0
+        if steps is not None and done >= steps:
+            break
+        if seconds is not None and el >= seconds and done >= 3:
+            break
+    el = time.perf_counter() - t0
+    return legal_bytes / el / 1e9, el / done * 1e6, done
+
+
+def time_cpu_reference_dense(weight_cpu: np.ndarray, hidden_cpu: np.ndarray, masks: np.ndarray, seconds: float):
+    """The reference's dense route on the host (gsp/triton_runtime.py:302-307
+    with xgrammar's CPU mask kernel): F.linear over every row, the mask applied
+    in place, argmax. Returns (GB/s of legal rows, us/step, steps) or None."""
+    try:
+        import torch.nn.functional as F
+        import xgrammar as xgr
+    except ImportError:
+        return None
+    w = torch.from_numpy(weight_cpu)
+    h = torch.from_numpy(hidden_cpu)
+    counts = legal_counts(masks)
+    done, legal_bytes, t0 = 0, 0, time.perf_counter()
+    while True:
+        m = torch.from_numpy(masks[done % len(masks)][None])
+        lg = F.linear(h, w)
+        xgr.apply_token_bitmask_inplace(lg, m, vocab_size=VOCAB, backend="cpu")
+        int(lg.argmax())
+        legal_bytes += int(counts[done % len(masks)]) * HIDDEN * 2
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and done >= 2:
+            break
+    return legal_bytes / el / 1e9, el / done * 1e6, done
+
+
+def cpu_baselines(weight_cpu, hidden_cpu, masks, seconds: float, density: float, pattern: str):
+    """Every CPU figure for the headline step, on this host's cores: the
+    reference's own sparse path (the baseline when its copy is present), its
+    dense route with xgrammar's CPU mask, and the oracle's restatement."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    what = f"batch 1, V={VOCAB}, H={HIDDEN} fp16, {density:.2%} {pattern}"
+    out = {}
+    r = time_cpu_reference_sparse(weight_cpu, hidden_cpu, masks, steps=None, seconds=seconds)
+    if r is not None:
+        out["reference_sparse"] = {"value": r[0], "unit": UNIT, "us_per_step": r[1], "cores": cpu_threads(),
+                                   "kind": "reference",
+                                   "sample": (f"{r[2]} steps ({r[1]:.0f} us/step) of the reference's own "
+                                              f"constrained_projection on CPU tensors (unmodified copy under "
+                                              f"baseline/_ref) + -inf row + argmax, {what}, bounded to "
+                                              f"{seconds:.0f} s")}
+    d = time_cpu_reference_dense(weight_cpu, hidden_cpu, masks, seconds=min(seconds, 5.0))
+    if d is not None:
+        out["reference_dense"] = {"value": d[0], "unit": UNIT, "us_per_step": d[1], "cores": cpu_threads(),
+                                  "kind": "reference",
+                                  "sample": (f"{d[2]} steps of F.linear + xgrammar apply_token_bitmask_inplace("
+                                             f"backend='cpu') + argmax, {what}")}
+    gbs, us, n = time_cpu_steps(weight_cpu, hidden_cpu, masks, steps=None, seconds=seconds)
+    out["port"] = {"value": gbs, "unit": UNIT, "us_per_step": us, "cores": cpu_threads(), "kind": "port",
+                   "sample": f"{n} steps ({us:.0f} us/step) of the oracle's restatement, {what}"}
+    head = dict(out.get("reference_sparse") or out["port"])
+    head["others"] = {k: v for k, v in out.items() if v is not None and v.get("sample") != head.get("sample")}
+    return head
+
+
 def host_weight(seed: int) -> tuple[np.ndarray, np.ndarray]:
     g = torch.Generator().manual_seed(seed)
     w = (torch.randn(VOCAB, HIDDEN, generator=g) * 0.02).half().numpy()
@@ -220,21 +378,162 @@ def run_reference_arm(args):
     torch.set_num_threads(os.cpu_count() or 1)
     masks = make_masks(args.masks, args.density, args.pattern, seed=100)
     w, h = host_weight(1234)
-    time_cpu_steps(w, h, masks, steps=max(args.warmup, 1), seconds=None)
-    gbs, us, n = time_cpu_steps(w, h, masks, steps=args.steps, seconds=None)
-    sample = (f"{n} steps of the batch-1 row-sparse step (mask decode, legal-row gather, fp32 dots, "
-              f"-inf fill, argmax) at V={VOCAB}, H={HIDDEN}, {args.density:.2%} {args.pattern}")
+    what = f"at V={VOCAB}, H={HIDDEN} fp16, {args.density:.2%} {args.pattern}"
+    kind = "reference"
+    if time_cpu_reference_sparse(w, h, masks, steps=max(args.warmup, 1), seconds=None) is not None:
+        gbs, us, n = time_cpu_reference_sparse(w, h, masks, steps=args.steps, seconds=None)
+        sample = (f"{n} steps of the reference's own CPU path (gsp.runtime.constrained_projection on CPU "
+                  f"tensors from the unmodified copy under baseline/_ref, then the -inf-filled row and its "
+                  f"argmax) {what}")
+    else:
+        kind = "port"
+        time_cpu_steps(w, h, masks, steps=max(args.warmup, 1), seconds=None)
+        gbs, us, n = time_cpu_steps(w, h, masks, steps=args.steps, seconds=None)
+        sample = (f"{n} steps of the oracle's restatement of the batch-1 row-sparse step (mask decode, "
+                  f"legal-row gather, fp32 dots, -inf fill, argmax) {what}; the reference copy under "
+                  f"baseline/_ref is absent")
     line = {
         "metric": METRIC, "value": gbs, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3, "us_per_step": us,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic",
         "config": workload_config(args),
-        "cpu_baseline": {"value": gbs, "unit": UNIT, "cores": cpu_threads(), "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": gbs, "unit": UNIT, "cores": cpu_threads(), "kind": kind, "sample": sample},
         "e2e": {"value": gbs, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def run_kernel_only(args):
+    """The headline step alone, eagerly, --warmup + --steps times over
+    --copies weight copies and --masks masks: the command the committed ncu
+    captures of the row-sparse kernel run (a few GB on the device)."""
+    from gsp import _native
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(args.copies)]
+    hidden = torch.randn(1, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(99)).half()
+    masks_np = make_masks(args.masks, args.density, args.pattern, seed=100)
+    masks = torch.from_numpy(masks_np).to(dev)
+    logits = torch.empty(1, VOCAB, device=dev, dtype=torch.float16)
+    tv = torch.empty(1, device=dev)
+    ti = torch.empty(1, device=dev, dtype=torch.int64)
+    for i in range(args.warmup + args.steps):
+        _native.row_sparse(hidden, weights[i % len(weights)], masks[i % len(masks)][None], logits=logits,
+                           top_value=tv, top_index=ti)
+    torch.cuda.synchronize()
+    counts = legal_counts(masks_np)
+    print(json.dumps({"only": "kernel", "launches": args.warmup + args.steps,
+                      "legal_bytes_per_launch_mean": float(np.mean(counts)) * HIDDEN * 2}), flush=True)
+    return 0
+
+
+def run_reference_triton(args):
+    """Child process of reference_triton_section: the reference's own Triton
+    kernels (gsp/triton_runtime.py:15-125, 147-258 of the unmodified copy
+    under baseline/_ref) through its public wrappers, on the headline workload
+    (batch 1, the same seeded weights, hidden state and masks) and the batched
+    block-GEMM workload; CUDA-graph timed like this library's routes. Prints
+    one JSON object; saves its step-0 logits (int16 view) to --ref-out."""
+    import importlib.util
+    try:
+        sys.path.insert(0, REF_DIR)
+        import gsp.triton_runtime as ref  # the reference's package, first on the path
+        if not os.path.abspath(ref.__file__).startswith(os.path.abspath(REF_DIR)):
+            raise ImportError(f"gsp resolved to {ref.__file__}, not the copy under baseline/_ref")
+    except Exception as exc:
+        print(json.dumps({"unavailable": f"{type(exc).__name__}: {exc}"}), flush=True)
+        return 0
+    spec = importlib.util.spec_from_file_location(
+        "gsp_b200_workloads", os.path.join(REPO, "grammar-sparse-projection_b200", "gsp", "workloads.py"))
+    wl = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(wl)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    weights = [(torch.randn(VOCAB, HIDDEN, device=dev, generator=g) * 0.02).half() for _ in range(8)]
+    hidden = torch.randn(1, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(99)).half()
+    rng = np.random.default_rng(100)
+    k = int(round(args.density * VOCAB))
+    masks_np = np.concatenate([wl.make_batch_mask(rng, 1, VOCAB, [k], clustered=(args.pattern == "clustered"),
+                                                  max_runs=64) for _ in range(args.masks)])
+    masks = torch.from_numpy(masks_np).to(dev)
+    counts = wl.unpack_bitmask(masks_np, VOCAB).sum(axis=1)
+    out = {"source": "unmodified reference copy under baseline/_ref, Triton " + __import__("triton").__version__}
+    steps = 20
+    try:
+        t = graph_time_us(dev, steps, lambda i: ref.bitmask_sparse_logits(hidden, weights[i % 8], masks[i % len(masks)]))
+        lb = float(sum(int(counts[i % len(masks)]) for i in range(steps))) * HIDDEN * 2
+        out["batch1"] = {"us_per_step": t / steps, "legal_gbs": lb / (t * 1e-6) / 1e9,
+                         "kernel": "_bitmask_sparse_lm_head_kernel via bitmask_sparse_logits"}
+        lg = ref.bitmask_sparse_logits(hidden, weights[0], masks[0])
+        torch.cuda.synchronize()
+        if args.ref_out:
+            np.save(args.ref_out, lg.view(torch.int16).cpu().numpy())
+    except Exception as exc:
+        out["batch1"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    batched = []
+    for batch in (2, 4, 8, 16, 32):
+        try:
+            rng = np.random.default_rng(300 + batch)
+            bm = [torch.from_numpy(wl.make_batch_mask(rng, batch, VOCAB, [1242] * batch, clustered=True,
+                                                      max_runs=16)).to(dev) for _ in range(8)]
+            hb = torch.randn(batch, HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(batch)).half()
+            t = graph_time_us(dev, steps, lambda i: ref.bitmask_block_gemm_logits(hb, weights[i % 8], bm[i % 8]))
+            batched.append({"batch": batch, "us_per_step": t / steps,
+                            "kernel": "_bitmask_block_gemm_kernel via bitmask_block_gemm_logits"})
+        except Exception as exc:
+            batched.append({"batch": batch, "unavailable": f"{type(exc).__name__}: {exc}"})
+    out["batched"] = batched
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def reference_triton_section(dev, args, weights, hidden, masks, ours_us_per_step, batched):
+    """The reference's Triton kernels on this GPU (child process: its package
+    is also named gsp) beside this library's: timings, speed-ups, and the
+    reference's step-0 logits against this library's on the same inputs."""
+    import subprocess
+    import tempfile
+    from gsp import _native
+    if not os.path.exists(os.path.join(REF_DIR, "gsp", "triton_runtime.py")):
+        return {"unavailable": "no reference copy under baseline/_ref (baseline/install_reference.py)"}
+    with tempfile.TemporaryDirectory() as tmp:
+        ref_out = os.path.join(tmp, "ref_logits.npy")
+        proc = subprocess.run([sys.executable, os.path.abspath(__file__), "--only", "reference-triton",
+                               "--density", str(args.density), "--pattern", args.pattern, "--masks", str(args.masks),
+                               "--ref-out", ref_out], capture_output=True, text=True, timeout=900)
+        lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
+        if proc.returncode != 0 or not lines:
+            return {"unavailable": f"child exited {proc.returncode}: {proc.stderr.strip()[-300:]}"}
+        res = json.loads(lines[-1])
+        if os.path.exists(ref_out):
+            ref_bits = torch.from_numpy(np.load(ref_out)).to(dev)
+            lg = torch.empty(1, VOCAB, device=dev, dtype=torch.float16)
+            ti = torch.empty(1, device=dev, dtype=torch.int64)
+            _native.row_sparse(hidden, weights[0], masks[0][None], logits=lg, top_index=ti)
+            ref_lg = ref_bits.view(torch.float16).reshape(1, -1).float()
+            ours = lg.float()
+            fin = torch.isfinite(ref_lg)
+            res["parity_vs_ours"] = {
+                "support_equal": bool(torch.equal(fin, torch.isfinite(ours))),
+                "max_abs_diff": float((ref_lg[fin] - ours[fin]).abs().max()) if fin.any() else 0.0,
+                "argmax_equal": int(ref_lg.argmax()) == int(ti.item()),
+                "what": "the reference kernel's step-0 logits vs this library's on the same W, h and mask"}
+    b1 = res.get("batch1", {})
+    if "us_per_step" in b1:
+        b1["ours_us_per_step"] = ours_us_per_step
+        b1["speedup_ours"] = b1["us_per_step"] / ours_us_per_step
+    ours_block = {r["batch"]: r["us_per_step"] for r in (batched or [])}
+    for r in res.get("batched", []):
+        o = ours_block.get(r["batch"])
+        if o and "us_per_step" in r:
+            r["ours_block_us_per_step"] = o["block-sparse"]
+            r["ours_best_us_per_step"] = min(v for k2, v in o.items() if k2 != "cublas+xgrammar" and v)
+            r["speedup_ours_best"] = r["us_per_step"] / r["ours_best_us_per_step"]
+    return res
 
 
 def workload_config(args):
@@ -254,6 +553,10 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.only == "reference-triton":
+        return run_reference_triton(args)
+    if args.only == "kernel":
+        return run_kernel_only(args)
     if args.only:
         dev = torch.device("cuda", 0)
         torch.cuda.set_device(dev)
@@ -342,6 +645,35 @@ def main():
         torch.cuda.synchronize()
         return [a.elapsed_time(b) * 1e3 for a, b in zip(ev0, ev1)]
 
+    def graph_replays_us(n, fn, min_replays=50, min_seconds=1.0, max_replays=20000):
+        """n steps captured in one CUDA graph, replayed at least min_replays
+        times and for at least min_seconds of device time; CUDA events around
+        every replay (µs per replay, one entry per replay)."""
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for i in range(3):
+                fn(i)  # creates this stream's workspace before capture
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(n):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        out = []
+        while len(out) < max_replays and (len(out) < min_replays or sum(out) < min_seconds * 1e6):
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
+            for a, b in ev:
+                a.record()
+                graph.replay()
+                b.record()
+            ev[-1][1].synchronize()
+            out += [a.elapsed_time(b) * 1e3 for a, b in ev]
+        del graph
+        return out
+
     def graph_total_us(n, fn):
         """n steps captured in one CUDA graph; events around one replay (µs)."""
         s = torch.cuda.Stream(device=dev)
@@ -372,10 +704,21 @@ def main():
     clocks = ClockSampler(local_rank)
     with clocks:
         t_wall = time.perf_counter()
-        total_us = graph_total_us(args.steps, step)
+        replay_us = graph_replays_us(args.steps, step)
         barrier()
         t_wall = time.perf_counter() - t_wall
-    total_us = max_over_ranks(total_us, world)
+    total_us = max_over_ranks(statistics.median(replay_us), world)
+    replays = {"count": len(replay_us), "median_us": statistics.median(replay_us), "min_us": min(replay_us),
+               "p90_us": sorted(replay_us)[int(0.9 * (len(replay_us) - 1))],
+               "what": (f"the {args.steps} timed steps captured in one CUDA graph and replayed {len(replay_us)} "
+                        f"times (>= 50 replays and >= 1 s), CUDA events around each replay; value uses the median "
+                        f"replay (max over ranks)")}
+    # the last timed step again, eagerly on the same inputs, checked against
+    # exact float64 products
+    last = args.steps - 1
+    step(last)
+    parity = exact_check(hidden, weights[last % len(weights)], local_masks[last % local_masks.shape[0]][None], logits,
+                         top_index) if world == 1 else None
     steps_idx = [i % args.masks for i in range(args.steps)]
     legal_bytes = float(sum(int(counts[j]) for j in steps_idx)) * HIDDEN * 2
     value = legal_bytes / (total_us * 1e-6) / 1e9
@@ -428,8 +771,20 @@ def main():
     for i in range(3):
         e2e_step(i)
     barrier()
-    e2e_steps = timed(args.steps, e2e_step, 0, flush_l2=False)
+    # one step at a time, as a decode loop runs it: events around the step and
+    # a host wait for its result record before the next step is issued
+    e2e_steps = []
+    for i in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        e2e_step(i)
+        b.record()
+        b.synchronize()
+        int(host_top[0])  # the step's result, read on the host
+        e2e_steps.append(a.elapsed_time(b) * 1e3)
     barrier()
+    e2e_parts = e2e_breakdown(dev, e2e_step, lambda i: _native.copy_bytes(dev_in, host_in[i % args.masks]),
+                              lambda i: calls[i % len(calls)](), args.steps) if world == 1 else None
     # the last step's record on the host equals a call on its inputs with device outputs
     last = (args.steps - 1) % len(weights)
     if world == 1:
@@ -453,9 +808,10 @@ def main():
     algo_per_launch = local_bytes / args.steps
     if world == 1:
         achieved = algo_per_launch / (kernel_us * 1e-6) / 1e9
+        traffic, traffic_src = read_traffic_csv()
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                    "frac": achieved / peak, "traffic": read_profile_traffic("row_sparse_gemv"),
-                    "kernel": "row_sparse_kernel", "algorithmic_bytes_per_launch": algo_per_launch,
+                    "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
+                    "kernel": "row_sparse_staged_kernel", "algorithmic_bytes_per_launch": algo_per_launch,
                     "peak_source": peak_src, "avg_launch_us": kernel_us,
                     "all_bytes_per_launch": algo_per_launch + (VOCAB // 32) * 4 + HIDDEN * 2 + VOCAB * 2}
     else:
@@ -468,6 +824,7 @@ def main():
     graphed = None
     groups = None
     same_gpu_dense = None
+    ref_triton = None
     cpu_base = None
     if world == 1 and not args.no_sweep:
         sweep = []
@@ -490,14 +847,12 @@ def main():
         sampler_res = sampler_section(dev, weights[:8])
         graphed = graphed_head_section(dev)
         groups = lane_groups_section(dev, weights[:8])
+        ref_triton = reference_triton_section(dev, args, weights, hidden, masks, us_per_step, batched)
     vp_head = None if args.no_vp else vocab_parallel_section(dev, world, rank, peak)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         w_cpu = weight.cpu().numpy()
         h_cpu = hidden.cpu().numpy()
-        gbs, us, n = time_cpu_steps(w_cpu, h_cpu, masks_np, steps=None, seconds=args.cpu_seconds)
-        cpu_base = {"value": gbs, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                    "sample": f"{n} CPU steps ({us:.0f} us/step) of the same batch-1 1% workload, "
-                              f"bounded to {args.cpu_seconds:.0f} s"}
+        cpu_base = cpu_baselines(w_cpu, h_cpu, masks_np, args.cpu_seconds, args.density, args.pattern)
 
     if rank == 0:
         line = {
@@ -509,13 +864,17 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": e2e_total / args.steps,
                     "graph_replay_us_per_step": e2e_graph_us,
-                    "what": ("eager steps, events around each: the step's mask and hidden state copied from one "
-                             "pinned staging row to the device by gsp_copy_bytes (SM-driven copy), the prepared "
-                             "C-ABI call on weight copy i % copies (at N > 1 with the in-kernel cross-rank "
-                             "exchange) storing the 16-byte top-1 record into pinned host memory; "
+                    "breakdown": e2e_parts,
+                    "what": ("eager steps one at a time, events around each and a host wait for the step's result "
+                             "before the next: the step's mask and hidden state copied from one pinned staging row "
+                             "to the device by gsp_copy_bytes (SM-driven copy), the prepared C-ABI call on weight "
+                             "copy i % copies (at N > 1 with the in-kernel cross-rank exchange) storing the "
+                             "16-byte top-1 record into pinned host memory, read by the host; "
                              "graph_replay_us_per_step: the same step recorded once per weight copy as a CUDA "
                              "graph and replayed (one GPU)")},
             "gpu_launches": args.steps,
+            "timing": replays,
+            "parity": parity,
             "roofline": roofline,
             "cpu_baseline": cpu_base,
             "clocks": clocks.summary(),
@@ -525,6 +884,7 @@ def main():
             "batched": batched,
             "mixed": mixed,
             "same_gpu_dense_mask": same_gpu_dense,
+            "reference_triton_same_gpu": ref_triton,
             "vocab_parallel_head": vp_head,
             "sampler": sampler_res,
             "graphed_head": graphed,
@@ -582,6 +942,50 @@ def e2e_graph_replay(dev, weights, host_in, dev_in, dev_hidden, dev_mask, logits
     return us
 
 
+def e2e_breakdown(dev, full_step, copy_step, call_step, n: int):
+    """Splits the end-to-end step (one GPU): device time of the input copy
+    kernel alone, of the prepared projection call alone and of the whole step,
+    each with CUDA events and a host wait after every step (medians); the
+    host-side issue cost of a step (Python + ctypes + launches, the calls
+    queued without waiting); and the wall-clock time of a step including the
+    host's wake-up after the result is ready."""
+    def events_us(fn):
+        ts = []
+        for i in range(n):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn(i)
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return statistics.median(ts)
+
+    def issue_us(fn):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(n):
+            fn(i)
+        el = time.perf_counter() - t0
+        torch.cuda.synchronize()
+        return el / n * 1e6
+
+    def wall_us(fn):
+        ts = []
+        for i in range(n):
+            t0 = time.perf_counter()
+            fn(i)
+            torch.cuda.current_stream().synchronize()
+            ts.append((time.perf_counter() - t0) * 1e6)
+        return statistics.median(ts)
+
+    return {"copy_kernel_us": events_us(copy_step), "projection_call_us": events_us(call_step),
+            "step_us": events_us(full_step), "host_issue_us_per_step": issue_us(full_step),
+            "wall_us_per_step": wall_us(full_step),
+            "what": ("medians over the timed steps; *_us: CUDA events around each piece with a host wait after "
+                     "each; host_issue: host time to queue one step without waiting; wall: perf_counter around "
+                     "a step and the wait for its result")}
+
+
 def legal_counts_local(masks_np: np.ndarray, lo: int, hi: int) -> np.ndarray:
     from gsp import workloads as wl
     return wl.unpack_bitmask(masks_np, VOCAB)[:, lo:hi].sum(axis=1)
@@ -595,8 +999,9 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def graph_time_us(dev, n, fn):
-    """n calls of fn(i) captured in one CUDA graph; events around one replay (us)."""
+def graph_time_us(dev, n, fn, replays: int = 10):
+    """n calls of fn(i) captured in one CUDA graph; events around each of
+    `replays` replays; the median replay (us)."""
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -610,13 +1015,14 @@ def graph_time_us(dev, n, fn):
             fn(i)
     graph.replay()
     torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    graph.replay()
-    b.record()
-    b.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(replays)]
+    for a, b in ev:
+        a.record()
+        graph.replay()
+        b.record()
+    ev[-1][1].synchronize()
     del graph
-    return a.elapsed_time(b) * 1e3
+    return statistics.median(a.elapsed_time(b) * 1e3 for a, b in ev)
 
 
 def eager_time_us(n, fn):
@@ -667,6 +1073,10 @@ def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
             times["cublas+xgrammar"] = eager_time_us(10, ref_dense)
         except Exception as exc:  # pragma: no cover - optional comparison
             times["cublas+xgrammar"] = None
+        parity = {}
+        for name, fn in routes.items():  # one timed step per route, checked
+            fn(hidden, weights[0], masks[0], logits=logits, top_value=tv, top_index=ti)
+            parity[name] = exact_check(hidden, weights[0], masks[0], logits, ti)
         mean_active = float(np.mean(active))
         block_bytes = mean_active * 128 * HIDDEN * 2
         row_bytes = float(np.mean([l.sum() for l in legal])) * HIDDEN * 2  # legal rows, every request
@@ -685,7 +1095,7 @@ def batched_section(dev, weights, peak, steps=20, batches=(2, 4, 8, 16, 32)):
             "speedup_block_vs_cublas_xgrammar": (times["cublas+xgrammar"] / times["block-sparse"]
                                                  if times["cublas+xgrammar"] else None),
             "tokens_per_s": batch / (times[best] * 1e-6),
-            "best_route": best, "b200_policy_route": choice,
+            "best_route": best, "b200_policy_route": choice, "parity": parity,
         })
     return out
 
@@ -785,9 +1195,17 @@ def vocab_parallel_section(dev, world, rank, peak, steps=10, batches=(1, 32, 128
             t = max_over_ranks(synced_graph_time_us(dev, steps, fn, world), world) / steps
             times[route] = t
             fracs[route] = route_bytes[route] / (t * 1e-6) / 1e9 / peak
+        parity = None
+        if xch is None:  # one GPU: every route once with logits, checked
+            parity = {}
+            lg = torch.empty(batch, vloc, device=dev, dtype=torch.bfloat16)
+            for route, fn in plain.items():
+                fn(h, w, masks[0], logits=lg, top_value=tv, top_index=ti)
+                parity[route] = exact_check(h, w, masks[0], lg, ti)
+            del lg
         best = min(times, key=times.get)
         choice = tr.choose_route(batch, vloc, VP_HIDDEN, 2, legal[0].tolist(), active[0])
-        out.append({"batch": batch, "us_per_step": times, "hbm_roofline_frac_per_rank": fracs,
+        out.append({"batch": batch, "us_per_step": times, "hbm_roofline_frac_per_rank": fracs, "parity": parity,
                     "active_tile_fraction_per_rank": float(np.mean(active)) / ((vloc + 127) // 128),
                     "best_route": best, "b200_policy_route": choice,
                     "tokens_per_s": batch / (times[best] * 1e-6)})
@@ -849,6 +1267,11 @@ def mixed_section(dev, peak, steps=10):
                          ("row-sparse", _native.row_sparse)):
             times[name] = graph_time_us(dev, steps, lambda i, fn=fn: fn(h, weights[i % 4], masks[i % 4], logits=logits,
                                                                        top_value=tv, top_index=ti)) / steps
+        parity = {}
+        for name, fn in (("block-sparse", _native.block_gemm), ("dense-mask", _native.dense_masked),
+                         ("row-sparse", _native.row_sparse)):
+            fn(h, weights[0], masks[0], logits=logits, top_value=tv, top_index=ti)
+            parity[name] = exact_check(h, weights[0], masks[0], logits, ti)
         best = min(times, key=times.get)
         fwf = tr.full_word_fraction_cpu(torch.from_numpy(masks_np[0]))
         ref_route = tr._reference_route(batch, fwf, 0.80)
@@ -857,7 +1280,7 @@ def mixed_section(dev, peak, steps=10):
         out.append({"constrained_fraction": frac, "us_per_step": times, "best_route": best,
                     "reference_policy_route": ref_route, "reference_policy_us": times[ref_route],
                     "b200_policy_route": b200_route, "b200_policy_us": times[b200_route],
-                    "tokens_per_s_best": batch / (times[best] * 1e-6)})
+                    "tokens_per_s_best": batch / (times[best] * 1e-6), "parity": parity})
     del weights
     return out
 

@@ -1,8 +1,8 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Runs ONLY where the reference checkout is available (it reads
-/root/reference, or the path in $GSP_REFERENCE_ROOT); the fixtures it writes
-are committed next to it and are all the tests need afterwards.
+Runs ONLY where a reference checkout is available; its path is the one
+required argument. The fixtures it writes are committed next to this script
+and are all the tests need afterwards.
 
 What is recorded, all produced by the reference's own code on this machine:
   * row_sparse_ref.npz   -- gsp/triton_runtime.py:15-58 (_bitmask_sparse_lm_head_kernel)
@@ -19,7 +19,7 @@ What is recorded, all produced by the reference's own code on this machine:
                             three route functions replaced by recorders, and
                             gsp/triton_runtime.py:310-321 full_word_fraction_cpu
 
-Usage:  python tests/golden/make_golden.py
+Usage:  python tests/golden/make_golden.py /path/to/reference/checkout
 """
 from __future__ import annotations
 
@@ -34,7 +34,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("GSP_REFERENCE_ROOT", "/root/reference")
+if len(sys.argv) != 2 or not os.path.isdir(os.path.join(sys.argv[1], "gsp")):
+    raise SystemExit("usage: python tests/golden/make_golden.py /path/to/reference/checkout")
+REF = os.path.abspath(sys.argv[1])
 sys.path.insert(0, REPO)
 sys.path.insert(0, REF)
 

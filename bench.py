@@ -792,8 +792,9 @@ def main():
     else:
         _native.vocab_parallel("row-sparse", dev_hidden, weights[last], dev_mask, xch.peers, rank, xch.max_batch,
                                VOCAB, top_value=out_value, top_index=out_index, vocab_offset=lo)
-    if int(out_index.item()) != int(host_top[0]):
-        raise RuntimeError("end-to-end step's host record disagrees with the device-output call")
+    if int(out_index.item()) != int(host_top[0]) or int(host_top[0]) < 0:
+        raise RuntimeError("end-to-end step's host record disagrees with the device-output call "
+                           "(or the cross-rank exchange timed out)")
     e2e_total = max_over_ranks(sum(e2e_steps), world)
     e2e_value = legal_bytes / (e2e_total * 1e-6) / 1e9
     e2e_graph_us = e2e_graph_replay(dev, weights, host_in, dev_in, dev_hidden, dev_mask, logits, host_value,

@@ -456,7 +456,7 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
                                   int64_t logits_row_stride, float* top_value, int64_t* top_index,
                                   int64_t* top_key, void* workspace, size_t workspace_bytes_,
                                   void* const* peer_buffers, int32_t rank, int32_t world_size,
-                                  int32_t max_batch, int64_t total_vocab, void* stream) {
+                                  int32_t max_batch, int64_t total_vocab, int64_t wait_us, void* stream) {
   const char* fn = "gsp_vocab_parallel_logits";
   if (route != GSP_ROUTE_ROW_SPARSE && route != GSP_ROUTE_BLOCK_SPARSE && route != GSP_ROUTE_DENSE_MASK)
     return fail(GSP_ERR_INVALID_ARGUMENT, "%s: unknown route %d", fn, route);
@@ -470,6 +470,7 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
   x.rank = rank;
   x.world = world_size;
   x.max_batch = max_batch;
+  x.wait_ns = (wait_us > 0 ? wait_us : kDefaultPeerWaitUs) * 1000;
   if (vocab_offset < 0 || vocab_offset + (int64_t)vocab > total_vocab)
     return fail(GSP_ERR_INVALID_ARGUMENT, "%s: shard [%lld, %lld) outside the head's %lld tokens", fn,
                 (long long)vocab_offset, (long long)(vocab_offset + vocab), (long long)total_vocab);

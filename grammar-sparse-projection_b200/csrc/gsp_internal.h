@@ -28,7 +28,10 @@ struct PeerExchange {
   int max_batch;   // key slots per rank
   int batch_base;  // slot of this launch's request 0 (batch chunks of the block path)
   int tagged;      // global token ids < 2^24 - 1: one self-tagged store per key, no flag
+  int64_t wait_ns; // how long the last CTA waits for the other ranks' keys before it gives up
 };
+
+constexpr int64_t kDefaultPeerWaitUs = 250000;
 
 // Parameters of the row-sparse kernel (one launch covers every request).
 struct RowSparseParams {

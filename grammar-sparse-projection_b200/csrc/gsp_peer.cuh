@@ -28,7 +28,16 @@
 
 namespace gsp {
 
-constexpr uint32_t kPeerSpinLimit = 1u << 22;  // x ~64 ns back-off: about a quarter of a second
+// Waits end after x.wait_ns of %globaltimer time; the poll count is capped as
+// well (2^26 polls with a >= 32 ns back-off, over two seconds), so a wait ends
+// even if the timer were not to advance.
+constexpr uint32_t kPeerSpinLimit = 1u << 26;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -92,11 +101,13 @@ __device__ __forceinline__ bool peer_exchange_keys(const PeerExchange& x, unsign
       const int q = i / batch, b = i - q * batch;
       const unsigned long long* slot = peer_key_slot(x, x.rank, par, q) + b;
       bool ok = false;
+      const uint64_t t0 = globaltimer_ns();
       for (uint32_t it = 0; it < kPeerSpinLimit; ++it) {
         if (tag_is(ld_relaxed_sys_u64(slot), e)) {
           ok = true;
           break;
         }
+        if ((int64_t)(globaltimer_ns() - t0) > x.wait_ns) break;
         __nanosleep(32);
       }
       if (!ok) {
@@ -127,11 +138,13 @@ __device__ __forceinline__ bool peer_exchange_keys(const PeerExchange& x, unsign
   if (tid < x.world) {
     const uint32_t* f = reinterpret_cast<const uint32_t*>(self + 128 + 128 * tid);
     bool ok = false;
+    const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
       if ((int32_t)(ld_acquire_sys(f) - e) >= 0) {
         ok = true;
         break;
       }
+      if ((int64_t)(globaltimer_ns() - t0) > x.wait_ns) break;
       __nanosleep(64);
     }
     if (!ok) {

@@ -59,6 +59,15 @@ int32_t gsp_peer_exchange_close(void* peer_buffer) {
   return GSP_OK;
 }
 
+int32_t gsp_peer_exchange_reset(void* buffer, int32_t world_size, int32_t max_batch) {
+  const char* fn = "gsp_peer_exchange_reset";
+  if (!buffer || world_size < 1 || world_size > kMaxPeers || max_batch < 1)
+    return record_error(GSP_ERR_INVALID_ARGUMENT, "%s: bad buffer, world size or max_batch", fn);
+  const cudaError_t err = cudaMemset(buffer, 0, peer_exchange_bytes_for((size_t)world_size, (size_t)max_batch));
+  if (err != cudaSuccess) return record_error(GSP_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(err));
+  return GSP_OK;
+}
+
 int32_t gsp_peer_exchange_free(void* buffer) {
   if (!buffer) return GSP_OK;
   const cudaError_t err = cudaFree(buffer);

@@ -76,8 +76,9 @@ SIGNATURES = {
     "gsp_peer_exchange_open": ([_vp, ctypes.POINTER(_vp)], _i32),
     "gsp_peer_exchange_close": ([_vp], _i32),
     "gsp_peer_exchange_free": ([_vp], _i32),
+    "gsp_peer_exchange_reset": ([_vp, _i32, _i32], _i32),
     "gsp_vocab_parallel_logits": ([_i32] + _PROJECTION_ARGS[:-1] + [ctypes.POINTER(_vp), _i32, _i32, _i32, _i64,
-                                                               _vp], _i32),
+                                                               _i64, _vp], _i32),
     "gsp_default_route_cost": ([ctypes.POINTER(RouteCost)], None),
     "gsp_choose_route": ([_i32, _i32, _i32, _i32, _i64, _i64, ctypes.POINTER(RouteCost)], _i32),
     "gsp_adaptive_logits": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _vp,
@@ -288,12 +289,19 @@ def peer_exchange_free(ptr: int) -> None:
     _check(load().gsp_peer_exchange_free(_vp(ptr)), "gsp_peer_exchange_free")
 
 
+def peer_exchange_reset(ptr: int, world_size: int, max_batch: int) -> None:
+    """Zeroes this rank's own exchange buffer (synchronous)."""
+    _check(load().gsp_peer_exchange_reset(_vp(ptr), world_size, max_batch), "gsp_peer_exchange_reset")
+
+
 def vocab_parallel(route: str, hidden, weight, mask, peers: list[int], rank: int, max_batch: int,
                    total_vocab: int, logits=None, top_value=None, top_index=None, top_key=None,
-                   vocab_offset: int = 0) -> None:
+                   vocab_offset: int = 0, wait_us: int = 0) -> None:
     """One rank's projection with the cross-rank top-1 merge in the kernel
     (gsp_vocab_parallel_logits); peers[q] is rank q's exchange buffer as
-    mapped in this process, total_vocab the whole head's vocabulary."""
+    mapped in this process, total_vocab the whole head's vocabulary, wait_us
+    the longest wait for the other ranks' keys (0: 250 ms). A wait that runs
+    out leaves top_index -1 for every request."""
     _require_cuda(hidden, weight, mask, logits)
     lib = load()
     batch, hdim = hidden.shape
@@ -306,7 +314,7 @@ def vocab_parallel(route: str, hidden, weight, mask, peers: list[int], rank: int
         batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
         _ptr(logits), 0 if logits is None else logits.stride(0),
         _ptr(top_value), _ptr(top_index), _ptr(top_key),
-        _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, total_vocab, _stream(hidden.device))
+        _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, total_vocab, wait_us, _stream(hidden.device))
     _check(status, "gsp_vocab_parallel_logits")
 
 
@@ -317,7 +325,7 @@ class PreparedVocabParallel:
 
     def __init__(self, route: str, hidden, weight, mask, peers: list[int], rank: int, max_batch: int,
                  total_vocab: int, logits=None, top_value=None, top_index=None, top_key=None,
-                 vocab_offset: int = 0):
+                 vocab_offset: int = 0, wait_us: int = 0):
         _require_cuda(hidden, weight, mask, logits)
         lib = load()
         batch, hdim = hidden.shape
@@ -332,7 +340,7 @@ class PreparedVocabParallel:
             batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
             _ptr(logits), 0 if logits is None else logits.stride(0),
             _ptr(top_value), _ptr(top_index), _ptr(top_key),
-            _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, total_vocab, _stream(hidden.device))
+            _ptr(ws), ws.numel(), arr, rank, len(peers), max_batch, total_vocab, wait_us, _stream(hidden.device))
 
     def __call__(self) -> None:
         status = self._fn(*self._args)

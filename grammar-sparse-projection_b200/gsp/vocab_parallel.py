@@ -30,6 +30,20 @@ from . import _native
 KEY_SIGN = -(1 << 63)  # XOR with this flips the top bit of an int64
 
 
+class ExchangeTimeout(RuntimeError):
+    """A rank's in-kernel wait for the other ranks' top-1 keys ran out (a peer
+    stalled or left): the call reported no token (top_index -1). The group
+    must call PeerExchange.reset() on every rank before its next call."""
+
+
+def check_exchange(top_index: torch.Tensor) -> None:
+    """Raises ExchangeTimeout when a vocabulary-parallel call reported no
+    token (top_index -1, the in-kernel exchange's time-out marker). Reads the
+    tensor on the host: call it where the step's result is read anyway."""
+    if bool((top_index < 0).any()):
+        raise ExchangeTimeout("the cross-rank top-1 exchange timed out; call PeerExchange.reset() on every rank")
+
+
 def shard_bounds(vocab: int, world_size: int, rank: int, align: int = 32) -> tuple[int, int]:
     """Contiguous row range of `rank`: boundaries are multiples of `align`
     (whole mask words), sizes differ by at most one `align` block, the last
@@ -108,7 +122,7 @@ class PeerExchange:
     process through CUDA IPC (one node). Creating and closing are collective:
     every rank of `group` must take part, in the same order."""
 
-    def __init__(self, max_batch: int, group=None):
+    def __init__(self, max_batch: int, group=None, wait_us: int = 250_000):
         if not dist.is_initialized():
             raise RuntimeError("PeerExchange needs an initialised process group")
         self.world = dist.get_world_size(group)
@@ -116,12 +130,25 @@ class PeerExchange:
         if self.world > _native.MAX_PEERS:
             raise ValueError(f"at most {_native.MAX_PEERS} ranks share an exchange")
         self.max_batch = int(max_batch)
+        self.wait_us = int(wait_us)  # longest in-kernel wait for the other ranks' keys
         self.group = group
         self.own, handle = _native.peer_exchange_alloc(self.world, self.max_batch)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group)
         self.peers = [self.own if q == self.rank else _native.peer_exchange_open(h) for q, h in enumerate(handles)]
         dist.barrier(group)  # every rank has mapped every buffer before any kernel writes
+
+    def reset(self) -> None:
+        """Collective re-synchronisation after a wait ran out (ExchangeTimeout):
+        every rank waits for its own calls, the group meets at a barrier, each
+        rank zeroes its own buffer (epoch, flags, keys) and its workspace, and
+        the group meets again before anyone calls the exchange."""
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        _native.peer_exchange_reset(self.own, self.world, self.max_batch)
+        _native.reset_workspace(torch.device("cuda", torch.cuda.current_device()))
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
 
     def close(self) -> None:
         """Collective: after every rank's last exchange call has completed."""
@@ -176,7 +203,11 @@ class VocabParallelHead:
         return bitmask_gpu[:, w0:w1]
 
     def forward(self, hidden: torch.Tensor, bitmask_gpu: torch.Tensor | None, *,
-                route: str = "row-sparse", full_logits: bool = False):
+                route: str = "row-sparse", full_logits: bool = False, check: bool = True):
+        """With the peer exchange, check=True reads top_index back and raises
+        ExchangeTimeout when the in-kernel wait ran out (no partial merge is
+        ever returned as a token); check=False leaves that to the caller
+        (check_exchange), e.g. under CUDA-graph capture."""
         hidden_2d = hidden.reshape(1, -1) if hidden.ndim == 1 else hidden
         batch = hidden_2d.shape[0]
         dev = hidden.device
@@ -188,7 +219,10 @@ class VocabParallelHead:
             top_index = torch.empty(batch, device=dev, dtype=torch.int64)
             _native.vocab_parallel(route, hidden_2d, self.weight, mask, self.exchange.peers, self.exchange.rank,
                                    self.exchange.max_batch, self.vocab, logits=local_logits,
-                                   top_value=top_value, top_index=top_index, vocab_offset=self.start)
+                                   top_value=top_value, top_index=top_index, vocab_offset=self.start,
+                                   wait_us=self.exchange.wait_us)
+            if check:
+                check_exchange(top_index)
             logits = gather_logits(local_logits, self.vocab, self.group) if full_logits else None
             return top_value, top_index, logits
         keys = torch.empty(batch, device=dev, dtype=torch.int64)

@@ -271,13 +271,18 @@ int32_t gsp_merge_logsumexp(const float* lse, int32_t parts, int32_t batch, floa
  * buffer as mapped here (peer_buffers[rank] = buf) ends, inside the projection
  * kernel, with an exchange over peer memory: the last CTA stores the rank's
  * per-request top-1 keys into every rank's buffer, raises its flag there,
- * waits (bounded, about a quarter of a second) for the other ranks' flags and
- * writes the GLOBAL top-1 (global token ids) to top_value / top_index /
- * top_key. Logits, when given, are this rank's shard only. No collective
- * library call and no extra launch is involved, so the call can be captured
- * in a CUDA graph. Every rank must make the same sequence of calls with the
- * same route and batch; a wait that runs out sets the workspace error word
- * to 3, after which the exchange buffers must be re-created. route is one of
+ * waits for the other ranks' flags for at most wait_us microseconds (<= 0:
+ * 250,000) and writes the GLOBAL top-1 (global token ids) to top_value /
+ * top_index / top_key. Logits, when given, are this rank's shard only. No
+ * collective library call and no extra launch is involved, so the call can be
+ * captured in a CUDA graph. Every rank must make the same sequence of calls
+ * with the same route and batch. A wait that runs out reports no token for
+ * the call: every top_index is -1 (top_value NaN, top_key INT64_MIN), never a
+ * merge of the keys that happened to arrive, and the workspace error word is
+ * set to 3. The group must then re-synchronise before its next call: every
+ * rank, once its calls have completed, calls gsp_peer_exchange_reset on its
+ * own buffer and re-zeroes its workspace, with a host barrier between the
+ * ranks before and after. route is one of
  * GSP_ROUTE_*; world_size 1 runs the plain projection. total_vocab is the
  * whole head's vocabulary, the same on every rank (below 2^24 - 1 each key
  * travels as one self-tagged store; larger heads add a fence and a flag).
@@ -295,6 +300,9 @@ int32_t gsp_peer_exchange_alloc(size_t bytes, void** buffer, void* ipc_handle);
 int32_t gsp_peer_exchange_open(const void* ipc_handle, void** peer_buffer);
 int32_t gsp_peer_exchange_close(void* peer_buffer);
 int32_t gsp_peer_exchange_free(void* buffer);
+/* Zeroes this rank's own exchange buffer (epoch, flags, keys) on the legacy
+ * stream and waits for it: the re-synchronisation after a wait ran out. */
+int32_t gsp_peer_exchange_reset(void* buffer, int32_t world_size, int32_t max_batch);
 int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hidden_row_stride,
                                   const void* weight, int64_t weight_row_stride,
                                   const int32_t* bitmask, int64_t bitmask_row_stride,
@@ -304,7 +312,7 @@ int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hid
                                   int64_t* top_index, int64_t* top_key, void* workspace,
                                   size_t workspace_bytes, void* const* peer_buffers,
                                   int32_t rank, int32_t world_size, int32_t max_batch,
-                                  int64_t total_vocab, void* stream);
+                                  int64_t total_vocab, int64_t wait_us, void* stream);
 
 /* ---- Device-side route choice (adaptive_grammar_logits without a host
  * round trip) ----------------------------------------------------------------

@@ -4,8 +4,10 @@ NCCL all-reduce path both give the global greedy top-1 of the full head, equal
 to the oracle's exact argmax outside the near-tie window and bit-identical to
 each other, for every route, over repeated calls and CUDA-graph replays.
 Skipped on machines with fewer than 2 GPUs."""
+import math
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -157,12 +159,15 @@ def test_vocab_parallel_peer_exchange_two_gpus(tmp_path):
         assert text == "", f"rank {r}: {text}"
 
 
-def test_exchange_wait_runs_out_on_one_gpu(cuda_device):
+@pytest.mark.parametrize("route", ["row-sparse", "block-sparse"])
+def test_exchange_wait_runs_out_on_one_gpu(cuda_device, route):
     """Failure detection without a fault: a two-rank exchange whose second
     rank never runs (its buffer is a second local one that nothing writes).
-    The last CTA's bounded wait gives up, the call returns, the workspace
-    error word reads 3, and after re-zeroing the workspace the device keeps
-    working (a plain call on the same stream succeeds)."""
+    The last CTA's wait gives up after the caller's limit (5 ms), the call
+    returns no token (top_index -1, top_value NaN: not a merge of what
+    arrived), check_exchange raises, the workspace error word reads 3; after
+    the buffers and the workspace are re-zeroed the device keeps working (a
+    plain call on the same stream succeeds)."""
     import sys
     sys.path.insert(0, os.path.join(os.path.dirname(__file__), "..", "grammar-sparse-projection_b200"))
     from gsp import _native
@@ -175,13 +180,21 @@ def test_exchange_wait_runs_out_on_one_gpu(cuda_device):
     own, _ = _native.peer_exchange_alloc(2, 1)
     silent, _ = _native.peer_exchange_alloc(2, 1)
     try:
+        from gsp import vocab_parallel as vp
         _native.reset_workspace(dev)
         tv = torch.empty(1, device=dev)
         ti = torch.empty(1, device=dev, dtype=torch.int64)
-        _native.vocab_parallel("row-sparse", h, w[: vocab // 2], mask[:, : vocab // 64], [own, silent], 0, 1,
-                               vocab, top_value=tv, top_index=ti)
+        t0 = time.perf_counter()
+        _native.vocab_parallel(route, h, w[: vocab // 2], mask[:, : vocab // 64], [own, silent], 0, 1,
+                               vocab, top_value=tv, top_index=ti, wait_us=5000)
         torch.cuda.synchronize()
+        assert time.perf_counter() - t0 < 2.0  # the caller's limit, not the default
+        assert ti.item() == -1 and math.isnan(tv.item())
+        with pytest.raises(vp.ExchangeTimeout):
+            vp.check_exchange(ti)
         assert _native.workspace_error(dev) == 3
+        _native.peer_exchange_reset(own, 2, 1)
+        _native.peer_exchange_reset(silent, 2, 1)
         _native.reset_workspace(dev)
         logits = torch.empty(1, vocab, device=dev, dtype=torch.float16)
         _native.row_sparse(h, w, mask, logits=logits, top_value=tv, top_index=ti)

@@ -78,7 +78,7 @@ def _vp_call(route=0, batch=1, tv=FAKE, peers=None, rank=0, world=2, max_batch=4
     lib = _native.load()
     arr = None if peers is None else (ctypes.c_void_p * len(peers))(*peers)
     return lib.gsp_vocab_parallel_logits(route, FAKE, 8, FAKE, 8, None, 0, batch, 64, 8, 0, offset, None, 64,
-                                         tv, None, None, FAKE, 1 << 30, arr, rank, world, max_batch, total, None)
+                                         tv, None, None, FAKE, 1 << 30, arr, rank, world, max_batch, total, 0, None)
 
 
 def test_vocab_parallel_entry_validation():

@@ -160,3 +160,13 @@ def test_sampling_merge_gloo(case):
         assert p.exitcode == 0
     for rank, pick_ok, lse_ok in results:
         assert pick_ok and lse_ok, (rank, pick_ok, lse_ok)
+
+
+def test_check_exchange_raises_on_the_time_out_marker():
+    """An in-kernel exchange whose wait ran out reports top_index -1 for every
+    request; check_exchange turns that into ExchangeTimeout and passes real
+    token ids (0 included: the id of an all -inf row) through."""
+    from gsp import vocab_parallel as vp
+    vp.check_exchange(torch.tensor([0, 5, 123456], dtype=torch.int64))
+    with pytest.raises(vp.ExchangeTimeout):
+        vp.check_exchange(torch.tensor([-1, -1], dtype=torch.int64))

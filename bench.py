@@ -764,9 +764,18 @@ def main():
                                                VOCAB, logits=logits, top_value=host_value, top_index=host_index,
                                                vocab_offset=lo) for w in weights]
 
-    def e2e_step(i):
-        _native.copy_bytes(dev_in, host_in[i % args.masks])
-        calls[i % len(calls)]()
+    host_rows = [host_in[j] for j in range(args.masks)]
+    if world == 1:
+        # one C-ABI call per step: the pinned row's copy and the projection
+        fused = [_native.PreparedStep(host_rows[0], dev_in, dev_hidden, w, dev_mask, logits=logits,
+                                      top_value=host_value, top_index=host_index) for w in weights]
+
+        def e2e_step(i):
+            fused[i % len(fused)](host_rows[i % args.masks])
+    else:
+        def e2e_step(i):
+            _native.copy_bytes(dev_in, host_rows[i % args.masks])
+            calls[i % len(calls)]()
 
     for i in range(3):
         e2e_step(i)
@@ -783,8 +792,14 @@ def main():
         int(host_top[0])  # the step's result, read on the host
         e2e_steps.append(a.elapsed_time(b) * 1e3)
     barrier()
-    e2e_parts = e2e_breakdown(dev, e2e_step, lambda i: _native.copy_bytes(dev_in, host_in[i % args.masks]),
+    e2e_parts = e2e_breakdown(dev, e2e_step, lambda i: _native.copy_bytes(dev_in, host_rows[i % args.masks]),
                               lambda i: calls[i % len(calls)](), args.steps) if world == 1 else None
+    if e2e_parts is not None:  # the same step as two C-ABI calls (copy, then projection)
+        def two_calls(i):
+            _native.copy_bytes(dev_in, host_rows[i % args.masks])
+            calls[i % len(calls)]()
+        e2e_parts["two_calls_step_us"] = e2e_breakdown(dev, two_calls, lambda i: None, lambda i: None,
+                                                       args.steps)["step_us"]
     # the last step's record on the host equals a call on its inputs with device outputs
     last = (args.steps - 1) % len(weights)
     if world == 1:
@@ -867,10 +882,11 @@ def main():
                     "graph_replay_us_per_step": e2e_graph_us,
                     "breakdown": e2e_parts,
                     "what": ("eager steps one at a time, events around each and a host wait for the step's result "
-                             "before the next: the step's mask and hidden state copied from one pinned staging row "
-                             "to the device by gsp_copy_bytes (SM-driven copy), the prepared C-ABI call on weight "
-                             "copy i % copies (at N > 1 with the in-kernel cross-rank exchange) storing the "
-                             "16-byte top-1 record into pinned host memory, read by the host; "
+                             "before the next: one prepared C-ABI call (gsp_row_sparse_step) copies the step's mask "
+                             "and hidden state from a pinned staging row to the device (SM-driven copy) and runs the "
+                             "projection on weight copy i % copies, storing the 16-byte top-1 record into pinned "
+                             "host memory, read by the host (at N > 1: gsp_copy_bytes, then the vocabulary-parallel "
+                             "call with the in-kernel cross-rank exchange); "
                              "graph_replay_us_per_step: the same step recorded once per weight copy as a CUDA "
                              "graph and replayed (one GPU)")},
             "gpu_launches": args.steps,

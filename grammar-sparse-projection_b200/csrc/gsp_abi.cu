@@ -643,6 +643,31 @@ int32_t gsp_copy_bytes(void* dst, const void* src, size_t bytes, void* stream) {
   return cuda_status(launch_copy_bytes(dst, src, bytes, static_cast<cudaStream_t>(stream)), "gsp_copy_bytes");
 }
 
+int32_t gsp_row_sparse_step(const void* host_inputs, size_t input_bytes, void* device_inputs, const void* hidden,
+                            int64_t hidden_row_stride, const void* weight, int64_t weight_row_stride,
+                            const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch, int32_t vocab,
+                            int32_t hidden_dim, int32_t dtype, int64_t vocab_offset, void* logits,
+                            int64_t logits_row_stride, float* top_value, int64_t* top_index, int64_t* top_key,
+                            void* workspace, size_t workspace_bytes_, void* stream) {
+  const char* fn = "gsp_row_sparse_step";
+  if (input_bytes > 0 && (!host_inputs || !device_inputs))
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: host_inputs and device_inputs are required", fn);
+  // validated before the copy is queued, so a failed call queues nothing
+  int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                   bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
+  if (st != GSP_OK) return st;
+  st = check_workspace(fn, top_value || top_index || top_key, workspace, workspace_bytes_, batch, vocab);
+  if (st != GSP_OK) return st;
+  if (input_bytes > 0) {
+    st = cuda_status(launch_copy_bytes(device_inputs, host_inputs, input_bytes, static_cast<cudaStream_t>(stream)),
+                     fn);
+    if (st != GSP_OK) return st;
+  }
+  return projection_common(fn, false, 0, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                           bitmask_row_stride, batch, vocab, hidden_dim, dtype, vocab_offset, logits, logits_row_stride,
+                           top_value, top_index, top_key, workspace, workspace_bytes_, stream);
+}
+
 size_t gsp_group_plan_words(int32_t batch) {
   if (batch < 1) return 0;
   return (size_t)kPlanHeader + 6 * (size_t)batch;

@@ -87,6 +87,7 @@ SIGNATURES = {
     "gsp_group_plan": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(RouteCost), _vp, _vp], _i32),
     "gsp_gather_rows": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp], _i32),
     "gsp_copy_bytes": ([_vp, _vp, _sz, _vp], _i32),
+    "gsp_row_sparse_step": ([_vp, _sz, _vp] + _PROJECTION_ARGS, _i32),
     "gsp_grouped_scratch_bytes": ([_i32, _i32, _i32, _i32], _sz),
     "gsp_grouped_logits": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _vp,
                             ctypes.POINTER(RouteCost), ctypes.POINTER(_i32), _vp, _sz, _vp, _sz, _vp], _i32),
@@ -238,6 +239,40 @@ class PreparedProjection:
         status = self._fn(*self._args)
         if status:
             _check(status, self._entry)
+
+
+class PreparedStep:
+    """One decode step from pinned host inputs in one C-ABI call
+    (gsp_row_sparse_step): the staging row host_row (pinned, the step's
+    packed mask and hidden state) is copied into dev_row by the SM copy and
+    the row-sparse projection runs on the views hidden / mask of dev_row;
+    top_value / top_index may be pinned host tensors. Arguments are converted
+    once; call(host_row) may name another pinned row of the same size."""
+
+    def __init__(self, host_row, dev_row, hidden, weight, mask, logits=None, top_value=None, top_index=None,
+                 top_key=None, vocab_offset: int = 0):
+        _require_cuda(hidden, weight, mask, logits, dev_row)
+        lib = load()
+        batch, hdim = hidden.shape
+        vocab = weight.shape[0]
+        ws = workspace(hidden.device, batch, vocab)
+        self._nbytes = host_row.numel() * host_row.element_size()
+        self._keep = (dev_row, hidden, weight, mask, logits, top_value, top_index, top_key, ws)
+        self._fn = lib.gsp_row_sparse_step
+        self._tail = (
+            _ptr(dev_row), _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+            _ptr(mask), 0 if mask is None else mask.stride(0),
+            batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+            _ptr(logits), 0 if logits is None else logits.stride(0),
+            _ptr(top_value), _ptr(top_index), _ptr(top_key),
+            _ptr(ws), ws.numel(), _stream(hidden.device))
+        self._default = host_row
+
+    def __call__(self, host_row=None) -> None:
+        row = self._default if host_row is None else host_row
+        status = self._fn(_vp(row.data_ptr()), self._nbytes, *self._tail)
+        if status:
+            _check(status, "gsp_row_sparse_step")
 
 
 def row_sparse(hidden, weight, mask, logits=None, top_value=None, top_index=None, top_key=None,

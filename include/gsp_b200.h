@@ -400,6 +400,24 @@ int32_t gsp_adaptive_logits(const void* hidden, int64_t hidden_row_stride, const
  * No counterpart in the reference (its decode loop copies with torch). */
 int32_t gsp_copy_bytes(void* dst, const void* src, size_t bytes, void* stream);
 
+/* One decode step from host inputs in one call: gsp_copy_bytes of
+ * input_bytes from host_inputs (pinned host memory: the step's packed mask
+ * and hidden state) to device_inputs, then gsp_row_sparse_logits with the
+ * remaining arguments, whose hidden and bitmask point into device_inputs and
+ * whose top_value / top_index may point into pinned host memory. Every
+ * argument is checked before anything is queued. The decode loop's mask copy
+ * (gsp/triton_runtime.py:133-144) and head call
+ * (benchmarks/qwen35_adaptive_paired.py:63-94) in one crossing of the ABI. */
+int32_t gsp_row_sparse_step(const void* host_inputs, size_t input_bytes, void* device_inputs,
+                            const void* hidden, int64_t hidden_row_stride,
+                            const void* weight, int64_t weight_row_stride,
+                            const int32_t* bitmask, int64_t bitmask_row_stride,
+                            int32_t batch, int32_t vocab, int32_t hidden_dim,
+                            int32_t dtype, int64_t vocab_offset, void* logits,
+                            int64_t logits_row_stride, float* top_value,
+                            int64_t* top_index, int64_t* top_key, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 #define GSP_GROUP_MAX_BATCH 256
 size_t gsp_group_plan_words(int32_t batch);
 int32_t gsp_group_plan(const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch, int32_t vocab,

@@ -292,3 +292,56 @@ def test_copy_bytes_and_top1_into_pinned_memory(cuda_device):
         _native.row_sparse(h, w, mask, top_value=tv_d, top_index=ti_d)
         torch.cuda.synchronize()
         assert ti_h.item() == ti_d.item() and tv_h.item() == tv_d.item()
+
+
+def test_fused_host_input_step(cuda_device):
+    """gsp_row_sparse_step (PreparedStep): one C-ABI call copies the pinned
+    staging row (mask + hidden state) to the device and projects, the top-1
+    record landing in pinned host memory; equal to gsp_copy_bytes followed by
+    gsp_row_sparse_logits, over staging rows that change every call. A bad
+    argument fails before anything is queued (the device row is untouched)."""
+    import ctypes
+    dev = cuda_device
+    rng = np.random.default_rng(31)
+    vocab, hidden = 30_000, 512
+    words = (vocab + 31) // 32
+    mask_pad = (words * 4 + 15) // 16 * 16
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * 0.05).half().to(dev)
+    rows = []
+    for j in range(3):
+        row = torch.zeros(mask_pad + hidden * 2, dtype=torch.uint8).pin_memory()
+        m = O.make_batch_mask(rng, 1, vocab, [50 * (j + 1)], clustered=j == 1, max_runs=4)
+        row[:words * 4] = torch.from_numpy(np.ascontiguousarray(m)).view(torch.uint8).reshape(-1)
+        row[mask_pad:] = torch.from_numpy(rng.standard_normal(hidden, dtype=np.float32)).half().view(torch.uint8)
+        rows.append(row)
+    dev_row = torch.zeros(rows[0].numel(), dtype=torch.uint8, device=dev)
+    dev_mask = dev_row[:words * 4].view(torch.int32).view(1, words)
+    dev_hidden = dev_row[mask_pad:].view(torch.float16).view(1, hidden)
+    host_top = torch.zeros(2, dtype=torch.int64).pin_memory()
+    logits = torch.empty(1, vocab, device=dev, dtype=torch.float16)
+    step = _native.PreparedStep(rows[0], dev_row, dev_hidden, w, dev_mask, logits=logits,
+                                top_value=host_top[1:2].view(torch.float32)[:1], top_index=host_top[0:1])
+    ref_logits = torch.empty_like(logits)
+    ti = torch.empty(1, device=dev, dtype=torch.int64)
+    for j in (0, 1, 2, 0):
+        host_top.fill_(-7)
+        step(rows[j])
+        torch.cuda.synchronize()
+        ref_row = torch.empty_like(dev_row)
+        _native.copy_bytes(ref_row, rows[j])
+        _native.row_sparse(ref_row[mask_pad:].view(torch.float16).view(1, hidden), w,
+                           ref_row[:words * 4].view(torch.int32).view(1, words), logits=ref_logits, top_index=ti)
+        torch.cuda.synchronize()
+        assert torch.equal(dev_row, ref_row) and torch.equal(logits.view(torch.int16), ref_logits.view(torch.int16))
+        assert int(host_top[0]) == ti.item() == logits.argmax(-1).item()
+    # hidden_dim 0 is rejected before the copy: the device row keeps its bytes
+    before = dev_row.clone()
+    lib = _native.load()
+    st = lib.gsp_row_sparse_step(ctypes.c_void_p(rows[1].data_ptr()), rows[1].numel(),
+                                 ctypes.c_void_p(dev_row.data_ptr()), ctypes.c_void_p(dev_hidden.data_ptr()), hidden,
+                                 ctypes.c_void_p(w.data_ptr()), hidden, ctypes.c_void_p(dev_mask.data_ptr()), words,
+                                 1, vocab, 0, 0, 0, None, vocab, None, None, None, None, 0,
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == _native.GSP_ERR_INVALID_ARGUMENT
+    torch.cuda.synchronize()
+    assert torch.equal(dev_row, before)

@@ -466,11 +466,121 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
   return incl - v + (warp > 0 ? s_warp[warp - 1] : 0u);
 }
 
+// Unit code (request * code_stride + row) of rank r, found from the per-thread
+// exclusive rank prefixes s_excl[kThreads] (non-decreasing, s_excl[0] == 0)
+// and the staged mask words (kWpt words per thread, transposed layout): the
+// thread holding rank r is the largest t with s_excl[t] <= r (nine dependent
+// shared-memory reads), then the word inside its kWpt words, then the bit.
+// r must be below the block total.
+template <int kWpt>
+__device__ __forceinline__ uint32_t code_of_rank(uint32_t r, const uint32_t* s_excl, const uint32_t* s_words, int nw,
+                                                 uint32_t code_stride) {
+  int t = 0;
+#pragma unroll
+  for (int step = kThreads / 2; step > 0; step >>= 1)
+    if (s_excl[t + step] <= r) t += step;
+  uint32_t local = r - s_excl[t];
+  uint32_t word = 0u;
+  int f = t * kWpt;
+  bool found = false;
+#pragma unroll
+  for (int v = 0; v < kWpt / 4; ++v) {
+    const uint4 x = reinterpret_cast<const uint4*>(s_words)[v * kThreads + t];
+    const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t pc = (uint32_t)__popc(w4[q]);
+      if (!found) {
+        if (local < pc) {
+          found = true;
+          word = w4[q];
+          f = t * kWpt + 4 * v + q;
+        } else {
+          local -= pc;
+        }
+      }
+    }
+  }
+  const int bit = (int)__fns(word, 0u, (int)local + 1);
+  const int b = f / nw, w = f - b * nw;
+  return (uint32_t)b * code_stride + (uint32_t)(w * 32 + bit);
+}
+
+// Greedy streaming of the CTA's units of rank [rbase, rbase + n) with no unit
+// list: warp w takes units w, w + 16, w + 32, ... two rows at a time, and
+// before every 16 such pairs its 32 lanes resolve those 32 units' codes at
+// once (code_of_rank; without a mask the code follows from the rank). No
+// block barrier between the scan and the first row load.
+template <typename T, int kWpt>
+__device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uint64_t rbase, int n, bool has_mask,
+                                                   const uint32_t* s_excl, const uint32_t* s_words,
+                                                   uint32_t code_stride, const void* s_h, bool want_top,
+                                                   unsigned long long* s_keys) {
+  using Bits = typename DTypeTraits<T>::Bits;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int H = p.hidden_dim, nvec = H / DTypeTraits<T>::kPerVec;
+  RunningTop top;
+  RunningSample rs;
+  for (int g0 = warp; g0 < n; g0 += 32 * kWarps) {
+    const int my_i = g0 + lane * kWarps;
+    uint32_t my_code = 0u;
+    if (my_i < n) {
+      const uint64_t r = rbase + (uint64_t)my_i;
+      if (has_mask) {
+        my_code = code_of_rank<kWpt>((uint32_t)r, s_excl, s_words, p.nw, code_stride);
+      } else {
+        const uint32_t b = (uint32_t)(r / (uint64_t)p.vocab);
+        my_code = b * code_stride + (uint32_t)(r - (uint64_t)b * p.vocab);
+      }
+    }
+    for (int k = 0; k < 32; k += 2) {
+      const int i = g0 + k * kWarps;
+      if (i >= n) break;
+      const int j = i + kWarps;
+      const bool has2 = j < n;
+      const uint32_t ca = __shfl_sync(FULL_MASK, my_code, k);
+      const uint32_t cb = has2 ? __shfl_sync(FULL_MASK, my_code, k + 1) : ca;
+      const int ba = (int)(ca / code_stride), va = (int)(ca - (uint32_t)ba * code_stride);
+      const int bb = (int)(cb / code_stride), vb = (int)(cb - (uint32_t)bb * code_stride);
+      const uint4* wa = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)va * p.weight_stride);
+      const uint4* wb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)vb * p.weight_stride);
+      const uint4* ha = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)ba * H);
+      const uint4* hb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)bb * H);
+      float acc_a = 0.f, acc_b = 0.f;
+      for (int base = 0; base < nvec; base += 32 * kUnroll) {
+        uint4 ra[kUnroll], rb[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int e = base + u * 32 + lane;
+          ra[u] = e < nvec ? ld_stream_v4(wa + e) : make_uint4(0, 0, 0, 0);
+          rb[u] = (has2 && e < nvec) ? ld_stream_v4(wb + e) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int e = base + u * 32 + lane;
+          if (e < nvec) {
+            acc_a = dot_vec<T>(ra[u], ha[e], acc_a);
+            if (has2) acc_b = dot_vec<T>(rb[u], hb[e], acc_b);
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        acc_a += __shfl_xor_sync(FULL_MASK, acc_a, o);
+        acc_b += __shfl_xor_sync(FULL_MASK, acc_b, o);
+      }
+      if (lane == 0) emit_unit<T, false>(p, ba, va, rbase + (uint64_t)i, acc_a, want_top, top, s_keys, rs, 0);
+      if (lane == 1 && has2) emit_unit<T, false>(p, bb, vb, rbase + (uint64_t)j, acc_b, want_top, top, s_keys, rs, 0);
+    }
+  }
+  if (lane < 2) top.flush(s_keys);
+}
+
 // ===========================================================================
 // staged kernel
 // ===========================================================================
 struct StagedLayout {
-  size_t list, keys, warp, misc, words, pre, hidden, total;
+  size_t list, keys, warp, misc, excl, words, pre, hidden, total;
 };
 
 // `words` = number of mask words staged (kThreads * words per thread).
@@ -485,6 +595,8 @@ __host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim,
   off = l.warp + 4 * 32;
   l.misc = align_up(off, 16);
   off = l.misc + 16;
+  l.excl = align_up(off, 16);
+  off = l.excl + 4 * (size_t)kThreads;
   l.words = align_up(off, 16);
   off = l.words + 4 * (size_t)words;
   l.pre = align_up(off, 16);
@@ -521,6 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   int* s_misc = reinterpret_cast<int*>(smem + L.misc);
   uint32_t* s_words = reinterpret_cast<uint32_t*>(smem + L.words);
   uint32_t* s_pre = reinterpret_cast<uint32_t*>(smem + L.pre);
+  uint32_t* s_excl = reinterpret_cast<uint32_t*>(smem + L.excl);
   Bits* s_h = reinterpret_cast<Bits*>(smem + L.hidden);
 
   const int tid = threadIdx.x;
@@ -591,6 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   // extraction and the -inf fill run one word per thread. Layout: the 16-byte
   // vector v of thread t sits at vector index v * kThreads + t (conflict-free
   // stores); staged_index() maps a flat word index to its slot.
+  if constexpr (!kSample) s_excl[tid] = excl;
   if (has_mask) {
     uint32_t run = excl;
 #pragma unroll
@@ -605,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
       pr.w = run;
       run += __popc(wd[4 * v + 3]);
       reinterpret_cast<uint4*>(s_words)[v * kThreads + tid] = make_uint4(wd[4 * v], wd[4 * v + 1], wd[4 * v + 2], wd[4 * v + 3]);
-      reinterpret_cast<uint4*>(s_pre)[v * kThreads + tid] = pr;
+      if constexpr (kSample) reinterpret_cast<uint4*>(s_pre)[v * kThreads + tid] = pr;
     }
   }
   if (p.offsets != nullptr && cta == 0) {
@@ -625,13 +739,18 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
 
   // -inf over the illegal entries of this CTA's output slice, issued before
   // the rows so that the stores drain while the row loads are in flight
-  if (p.logits && has_mask) {
-    __syncthreads();  // staged words complete
+  if (!kSample || (p.logits && has_mask)) __syncthreads();  // staged words (and prefixes) complete
+  if (p.logits && has_mask)
     fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_words[staged_index<kWpt>((int)f)]; });
-  }
   const uint64_t lo = total * (uint64_t)cta / (uint64_t)G;
   const uint64_t hi = total * (uint64_t)(cta + 1) / (uint64_t)G;
   const uint32_t code_stride = (uint32_t)nw * 32u;
+  if constexpr (!kSample) {
+    // greedy: each warp resolves its own units from the prefixes, no unit list
+    stream_rows_ranked<T, kWpt>(p, lo, (int)(hi - lo), has_mask, s_excl, s_words, code_stride, s_h, want_top, s_keys);
+    if (want_top) finalize_top1<false>(p, s_keys, s_misc, want_top);
+    return;
+  }
 
   for (uint64_t rbase = lo; rbase < hi; rbase += kListCap) {
     const uint64_t rend = min(hi, rbase + (uint64_t)kListCap);

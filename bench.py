@@ -766,11 +766,18 @@ def main():
 
     host_rows = [host_in[j] for j in range(args.masks)]
     if world == 1:
-        # one C-ABI call per step: the pinned row's copy and the projection
+        # one C-ABI call per step: the step recorded once per weight copy as a
+        # CUDA graph inside the library (the pinned row's copy, then the
+        # projection), replayed with its copy pointed at the step's row
         fused = [_native.PreparedStep(host_rows[0], dev_in, dev_hidden, w, dev_mask, logits=logits,
                                       top_value=host_value, top_index=host_index) for w in weights]
+        graphs = [_native.GraphStep(host_rows[0], dev_in, dev_hidden, w, dev_mask, logits=logits,
+                                    top_value=host_value, top_index=host_index) for w in weights]
 
         def e2e_step(i):
+            graphs[i % len(graphs)](host_rows[i % args.masks])
+
+        def fused_step(i):
             fused[i % len(fused)](host_rows[i % args.masks])
     else:
         def e2e_step(i):
@@ -800,6 +807,8 @@ def main():
             calls[i % len(calls)]()
         e2e_parts["two_calls_step_us"] = e2e_breakdown(dev, two_calls, lambda i: None, lambda i: None,
                                                        args.steps)["step_us"]
+        e2e_parts["one_call_no_graph_step_us"] = e2e_breakdown(dev, fused_step, lambda i: None, lambda i: None,
+                                                               args.steps)["step_us"]
     # the last step's record on the host equals a call on its inputs with device outputs
     last = (args.steps - 1) % len(weights)
     if world == 1:
@@ -882,8 +891,9 @@ def main():
                     "graph_replay_us_per_step": e2e_graph_us,
                     "breakdown": e2e_parts,
                     "what": ("eager steps one at a time, events around each and a host wait for the step's result "
-                             "before the next: one prepared C-ABI call (gsp_row_sparse_step) copies the step's mask "
-                             "and hidden state from a pinned staging row to the device (SM-driven copy) and runs the "
+                             "before the next: one C-ABI call (gsp_step_graph_launch: the step recorded once per "
+                             "weight copy as a CUDA graph inside the library) copies the step's mask and hidden "
+                             "state from its pinned staging row to the device (SM-driven copy) and runs the "
                              "projection on weight copy i % copies, storing the 16-byte top-1 record into pinned "
                              "host memory, read by the host (at N > 1: gsp_copy_bytes, then the vocabulary-parallel "
                              "call with the in-kernel cross-rank exchange); "

@@ -195,6 +195,9 @@ cudaError_t launch_mask_stats(const uint32_t* mask, int64_t stride, int batch, i
                               int32_t* legal_counts, int32_t* full_words, int32_t* active_tiles,
                               cudaStream_t stream);
 cudaError_t launch_copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+// The copy kernel launch_copy_bytes uses (arguments: dst, src, bytes, vec16),
+// for finding its node in a captured graph.
+const void* copy_bytes_kernel_fn();
 cudaError_t launch_merge_logsumexp(const float* lse, int parts, int batch, float* out, cudaStream_t stream);
 cudaError_t launch_top1_from_keys(const int64_t* keys, int batch, float* top_value,
                                   int64_t* top_index, cudaStream_t stream);

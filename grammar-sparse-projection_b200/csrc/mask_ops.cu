@@ -202,6 +202,8 @@ __global__ void copy_bytes_kernel(unsigned char* __restrict__ dst, const unsigne
 
 }  // namespace
 
+const void* copy_bytes_kernel_fn() { return reinterpret_cast<const void*>(copy_bytes_kernel); }
+
 cudaError_t launch_copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
   if (bytes == 0) return cudaSuccess;
   const int vec16 = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0;

@@ -88,6 +88,9 @@ SIGNATURES = {
     "gsp_gather_rows": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp], _i32),
     "gsp_copy_bytes": ([_vp, _vp, _sz, _vp], _i32),
     "gsp_row_sparse_step": ([_vp, _sz, _vp] + _PROJECTION_ARGS, _i32),
+    "gsp_step_graph_create": ([ctypes.POINTER(_vp), _vp, _sz, _vp] + _PROJECTION_ARGS[:-1], _i32),
+    "gsp_step_graph_launch": ([_vp, _vp, _vp], _i32),
+    "gsp_step_graph_destroy": ([_vp], _i32),
     "gsp_grouped_scratch_bytes": ([_i32, _i32, _i32, _i32], _sz),
     "gsp_grouped_logits": ([_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _vp,
                             ctypes.POINTER(RouteCost), ctypes.POINTER(_i32), _vp, _sz, _vp, _sz, _vp], _i32),
@@ -273,6 +276,50 @@ class PreparedStep:
         status = self._fn(_vp(row.data_ptr()), self._nbytes, *self._tail)
         if status:
             _check(status, "gsp_row_sparse_step")
+
+
+class GraphStep:
+    """The decode step of PreparedStep recorded once as a CUDA graph inside
+    the library (gsp_step_graph_create): each call(host_row) is one
+    gsp_step_graph_launch on the current stream at construction, the copy
+    retargeted to host_row (a pinned row of the same size and alignment)."""
+
+    def __init__(self, host_row, dev_row, hidden, weight, mask, logits=None, top_value=None, top_index=None,
+                 top_key=None, vocab_offset: int = 0):
+        _require_cuda(hidden, weight, mask, logits, dev_row)
+        lib = load()
+        batch, hdim = hidden.shape
+        vocab = weight.shape[0]
+        ws = workspace(hidden.device, batch, vocab)
+        self._keep = (host_row, dev_row, hidden, weight, mask, logits, top_value, top_index, top_key, ws)
+        self._lib = lib
+        self._handle = _vp()
+        status = lib.gsp_step_graph_create(
+            ctypes.byref(self._handle), _ptr(host_row), host_row.numel() * host_row.element_size(), _ptr(dev_row),
+            _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+            _ptr(mask), 0 if mask is None else mask.stride(0),
+            batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
+            _ptr(logits), 0 if logits is None else logits.stride(0),
+            _ptr(top_value), _ptr(top_index), _ptr(top_key), _ptr(ws), ws.numel())
+        _check(status, "gsp_step_graph_create")
+        self._launch = lib.gsp_step_graph_launch
+        self._stream = _stream(hidden.device)
+
+    def __call__(self, host_row=None) -> None:
+        status = self._launch(self._handle, None if host_row is None else _vp(host_row.data_ptr()), self._stream)
+        if status:
+            _check(status, "gsp_step_graph_launch")
+
+    def close(self) -> None:
+        if self._handle:
+            self._lib.gsp_step_graph_destroy(self._handle)
+            self._handle = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def row_sparse(hidden, weight, mask, logits=None, top_value=None, top_index=None, top_key=None,

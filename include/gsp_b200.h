@@ -418,6 +418,28 @@ int32_t gsp_row_sparse_step(const void* host_inputs, size_t input_bytes, void* d
                             int64_t* top_index, int64_t* top_key, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* The same step recorded once as a CUDA graph (copy node + projection; the
+ * projection's launch overlaps the copy through a programmatic edge), for a
+ * decode loop that repeats it on the same device buffers: create takes
+ * gsp_row_sparse_step's arguments without the stream (host_inputs names the
+ * pinned row recorded; nothing runs at create), launch replays the graph on
+ * `stream` with one driver call, first pointing the copy at host_inputs when
+ * given (a pinned row of the recorded size and 16-byte alignment). Launches
+ * of one handle must not overlap (they share the workspace and buffers).
+ * Extends the decode loop's copy + head call
+ * (benchmarks/qwen35_adaptive_paired.py:63-94); no Triton counterpart. */
+int32_t gsp_step_graph_create(void** handle, const void* host_inputs, size_t input_bytes,
+                              void* device_inputs, const void* hidden, int64_t hidden_row_stride,
+                              const void* weight, int64_t weight_row_stride,
+                              const int32_t* bitmask, int64_t bitmask_row_stride,
+                              int32_t batch, int32_t vocab, int32_t hidden_dim,
+                              int32_t dtype, int64_t vocab_offset, void* logits,
+                              int64_t logits_row_stride, float* top_value,
+                              int64_t* top_index, int64_t* top_key, void* workspace,
+                              size_t workspace_bytes);
+int32_t gsp_step_graph_launch(void* handle, const void* host_inputs, void* stream);
+int32_t gsp_step_graph_destroy(void* handle);
+
 #define GSP_GROUP_MAX_BATCH 256
 size_t gsp_group_plan_words(int32_t batch);
 int32_t gsp_group_plan(const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch, int32_t vocab,

@@ -334,6 +334,23 @@ def test_fused_host_input_step(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(dev_row, ref_row) and torch.equal(logits.view(torch.int16), ref_logits.view(torch.int16))
         assert int(host_top[0]) == ti.item() == logits.argmax(-1).item()
+    # the same step recorded as a CUDA graph inside the library, its copy
+    # pointed at another pinned row on each launch
+    gstep = _native.GraphStep(rows[0], dev_row, dev_hidden, w, dev_mask, logits=logits,
+                              top_value=host_top[1:2].view(torch.float32)[:1], top_index=host_top[0:1])
+    for j in (2, 1, 1, 0, 2):
+        host_top.fill_(-7)
+        gstep(rows[j])
+        torch.cuda.synchronize()
+        ref_row = torch.empty_like(dev_row)
+        _native.copy_bytes(ref_row, rows[j])
+        _native.row_sparse(ref_row[mask_pad:].view(torch.float16).view(1, hidden), w,
+                           ref_row[:words * 4].view(torch.int32).view(1, words), logits=ref_logits, top_index=ti)
+        torch.cuda.synchronize()
+        assert torch.equal(dev_row, ref_row) and torch.equal(logits.view(torch.int16), ref_logits.view(torch.int16))
+        assert int(host_top[0]) == ti.item()
+    gstep.close()
+    assert _native.workspace_error(dev) == 0
     # hidden_dim 0 is rejected before the copy: the device row keeps its bytes
     before = dev_row.clone()
     lib = _native.load()

@@ -1167,8 +1167,14 @@ def sampler_section(dev, weights, steps=50, batches=(1, 32)):
             u = torch.rand(batch, VOCAB, device=dev)
             tok.copy_((logits.float() / temperature - torch.log(-torch.log(u))).argmax(-1))
 
-        times = {name: graph_time_us(dev, steps, fn) / steps
-                 for name, fn in (("fused", fused), ("greedy", greedy), ("unfused", unfused))}
+        def fused_block(i):  # the sampler in the tensor-core epilogue, active tiles only
+            _native.row_sparse_sample(hidden, weights[i % len(weights)], masks[i % 8], seeds, i, temperature, tok,
+                                      sample_logsumexp=lse, top_value=tv, top_index=ti, route="block-sparse")
+
+        fns = [("fused", fused), ("greedy", greedy), ("unfused", unfused)]
+        if batch > 1:
+            fns.append(("fused_block_sparse", fused_block))
+        times = {name: graph_time_us(dev, steps, fn) / steps for name, fn in fns}
         out.append({"batch": batch, "us_per_step": times,
                     "speedup_fused_vs_unfused": times["unfused"] / times["fused"]})
     return out

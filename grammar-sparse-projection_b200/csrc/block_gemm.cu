@@ -49,6 +49,7 @@
 #include "gsp_common.cuh"
 #include "gsp_internal.h"
 #include "gsp_peer.cuh"
+#include "gsp_sampler.cuh"
 #include "gsp_tcgen05.cuh"
 
 namespace gsp {
@@ -76,7 +77,7 @@ struct GemmConfig {
 };
 
 struct GemmLayout {
-  size_t a, b, bars, tmem, keys, pref, misc, total;
+  size_t a, b, bars, tmem, keys, skeys, stats, pref, misc, total;
 };
 
 __host__ __device__ inline size_t align_to(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -94,6 +95,10 @@ __host__ __device__ inline GemmLayout gemm_layout(int npad, int stages, int nbui
   off = l.tmem + 16;
   l.keys = align_to(off, 16);
   off = l.keys + 8 * (size_t)kMaxNpad;
+  l.skeys = align_to(off, 16);  // sampler: the CTA's winning perturbed key per request
+  off = l.skeys + 8 * (size_t)kMaxNpad;
+  l.stats = align_to(off, 16);  // sampler: the CTA's (max, sum) pair per request
+  off = l.stats + 8 * (size_t)kMaxNpad;
   l.pref = align_to(off, 16);
   off = l.pref + 4 * ((size_t)nbuild + 1);
   l.misc = align_to(off, 16);
@@ -180,15 +185,60 @@ __device__ __forceinline__ unsigned long long merge_unit_key(unsigned long long 
   return key > running ? key : running;
 }
 
+// Sampler state of one epilogue unit (kSample kernels): its requests' seeds and
+// the CTA's per-request accumulators in shared memory, all offset to the
+// unit's first column, and the global token id of this lane's row.
+struct UnitSampler {
+  const uint64_t* seeds;
+  unsigned long long* skeys;
+  unsigned long long* stats;
+  uint64_t offset;
+  float inv_temp;
+  int64_t global_row;
+};
+
+// Fused sampler, one accumulator column jj of the warp's 32 rows (the contract
+// of gsp_sampler.cuh): the legal rows' perturbed scores x * inv_temp + Gumbel
+// noise keyed by (seed, step, global id), their warp maximum as a top-1 key
+// (ties to the lower id), and the warp's (max, sum of exp) pair of the scaled
+// logits, folded into the CTA's shared accumulators by lane 0 (one shared
+// atomicMax and one compare-and-swap merge per warp and column). Columns with
+// no legal row in the warp cost one ballot. Called by all 32 lanes.
+template <typename T>
+__device__ __forceinline__ void sample_column(const UnitSampler& su, int jj, bool legal, uint16_t bits) {
+  if (__ballot_sync(FULL_MASK, legal) == 0u) return;
+  const float y = legal ? DTypeTraits<T>::bits_to_float(bits) * su.inv_temp : -INFINITY;
+  unsigned long long sk = 0ull;
+  if (legal)
+    sk = top1_key(y + gumbel_noise_outlined(su.seeds[jj], su.offset, (uint64_t)su.global_row),
+                  (uint64_t)su.global_row);
+  sk = warp_max_u64(sk);
+  const float m = from_ordered_bits(__reduce_max_sync(FULL_MASK, legal ? ordered_bits(y) : 0u));
+  float e = legal ? __expf(y - m) : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(FULL_MASK, e, o);
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&su.skeys[jj], sk);
+    unsigned long long old = su.stats[jj], assumed;
+    do {
+      assumed = old;
+      float mm = stats_m(assumed), ss = stats_s(assumed);
+      merge_stats(mm, ss, m, e);
+      old = atomicCAS(&su.stats[jj], assumed, pack_stats(mm, ss));
+    } while (old != assumed);
+  }
+}
+
 // One epilogue unit: kCols accumulator columns (requests b0 .. b0 + kCols - 1)
 // of this warp's 32 TMEM lanes (one vocabulary row per thread). Rounds to the
 // logits dtype, applies the mask bit (word_l: this lane's mask word for
 // request b0 + lane % kCols), stores the row's logits (-inf where illegal) and
 // returns in lane l < kCols the warp_key16 maximum over the 32 rows for
-// request b0 + l.
-template <typename T, int kCols>
+// request b0 + l. With kSample, also feeds every column to sample_column.
+template <typename T, int kCols, bool kSample>
 __device__ __forceinline__ uint32_t epilogue_unit(uint32_t taddr, uint32_t word_l, int b0, int B, bool row_ok,
-                                                  bool store, uint16_t* out, int64_t stride, int lane) {
+                                                  bool store, uint16_t* out, int64_t stride, int lane,
+                                                  const UnitSampler& su) {
   uint32_t v[kCols];
   if constexpr (kCols == 32) tmem_ld32(taddr, v);
   else tmem_ld16(taddr, v);
@@ -204,6 +254,7 @@ __device__ __forceinline__ uint32_t epilogue_unit(uint32_t taddr, uint32_t word_
       const uint16_t bits = legal ? DTypeTraits<T>::round_bits(__uint_as_float(v[jj])) : ninf;
       if (store) out[jj * stride] = bits;
       key[jj] = legal ? warp_key16(bits, low) : 0u;
+      if constexpr (kSample) sample_column<T>(su, jj, legal, bits);
     }
   } else {
 #pragma unroll
@@ -212,6 +263,7 @@ __device__ __forceinline__ uint32_t epilogue_unit(uint32_t taddr, uint32_t word_
       const uint16_t bits = legal ? DTypeTraits<T>::round_bits(__uint_as_float(v[jj])) : ninf;
       if (store && b0 + jj < B) out[jj * stride] = bits;
       key[jj] = legal ? warp_key16(bits, low) : 0u;
+      if constexpr (kSample) sample_column<T>(su, jj, legal, bits);
     }
   }
   // transpose-reduce: lane l ends with the maximum over the 32 rows of
@@ -235,7 +287,8 @@ __device__ __forceinline__ uint32_t epilogue_unit(uint32_t taddr, uint32_t word_
 }
 
 // kNarrow: the batch pads to 32 columns (one 16-column unit per epilogue warp).
-template <typename T, bool kNarrow>
+// kSample: the fused sampler (p.sample_index != nullptr) runs in the epilogue.
+template <typename T, bool kNarrow, bool kSample>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_projection_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_h,
                          const BlockGemmParams p, const GemmConfig c) {
@@ -252,6 +305,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + kMaxAcc;  // [kMaxAcc]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.tmem);
   unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
+  unsigned long long* s_skeys = reinterpret_cast<unsigned long long*>(smem + L.skeys);
+  unsigned long long* s_stats = reinterpret_cast<unsigned long long*>(smem + L.stats);
   int* s_pref = reinterpret_cast<int*>(smem + L.pref);
   int* s_misc = reinterpret_cast<int*>(smem + L.misc);  // [0] abort, [1] last-CTA flag
   volatile int* abort_flag = s_misc;
@@ -282,6 +337,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_relinquish();
   }
   for (int i = tid; i < kMaxNpad; i += kGemmThreads) s_keys[i] = 0ull;
+  if constexpr (kSample) {
+    for (int i = tid; i < kMaxNpad; i += kGemmThreads) {
+      s_skeys[i] = 0ull;
+      s_stats[i] = empty_stats();
+    }
+  }
   // Everything above overlaps the tile builder; from here on its outputs (and
   // the inactive-tile -inf fill) are complete and visible.
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -423,16 +484,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint16_t* out = static_cast<uint16_t*>(p.logits) + row;
       if constexpr (narrow) {
         const int b0 = 16 * half;
-        const uint32_t k = epilogue_unit<T, 16>(tcol + (uint32_t)b0, words[0], b0, B, row_ok, store,
-                                                 out + (int64_t)b0 * p.logits_stride, p.logits_stride, lane);
+        UnitSampler su{};
+        if constexpr (kSample)
+          su = UnitSampler{p.seeds + b0, s_skeys + b0, s_stats + b0, p.offset, p.inv_temp, p.vocab_offset + row};
+        const uint32_t k = epilogue_unit<T, 16, kSample>(tcol + (uint32_t)b0, words[0], b0, B, row_ok, store,
+                                                 out + (int64_t)b0 * p.logits_stride, p.logits_stride, lane, su);
         running[0] = merge_unit_key<T>(running[0], k, p.vocab_offset + row0);
       } else {
 #pragma unroll
         for (int u = 0; u < kMaxUnits; ++u) {
           if (u < nunits) {
             const int b0 = unit_col(false, half, u);
-            const uint32_t k = epilogue_unit<T, 32>(tcol + (uint32_t)b0, words[u], b0, B, row_ok, store,
-                                                     out + (int64_t)b0 * p.logits_stride, p.logits_stride, lane);
+            UnitSampler su{};
+            if constexpr (kSample)
+              su = UnitSampler{p.seeds + b0, s_skeys + b0, s_stats + b0, p.offset, p.inv_temp, p.vocab_offset + row};
+            const uint32_t k = epilogue_unit<T, 32, kSample>(tcol + (uint32_t)b0, words[u], b0, B, row_ok, store,
+                                                     out + (int64_t)b0 * p.logits_stride, p.logits_stride, lane, su);
             running[u] = merge_unit_key<T>(running[u], k, p.vocab_offset + row0);
           }
         }
@@ -468,7 +535,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // clears the per-builder-block counts, which every CTA read at set-up.
   if (!p.dense)
     for (int pos = cta + tid * G; pos < total; pos += G * kGemmThreads) p.tile_list[list_slot(c, s_pref, pos)] = 0;
-  if (!want_top && p.dense) return;
+  if (!want_top && p.dense && !kSample) return;
   bool did = false;
   if (want_top) {
     for (int b = tid; b < B; b += kGemmThreads) {
@@ -477,6 +544,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         atomicMax(p.keys + b, k);
         did = true;
       }
+    }
+  }
+  if constexpr (kSample) {  // the CTA's sample keys and (max, sum) partials (request-major rows)
+    for (int b = tid; b < B; b += kGemmThreads) {
+      if (s_skeys[b] != 0ull) atomicMax(p.sample_keys + b, s_skeys[b]);
+      p.stat_partials[(size_t)b * kMaxSlices + cta] = s_stats[b];
+      did = true;
     }
   }
   if (did) __threadfence();
@@ -499,6 +573,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         store_top1(p.top_value, p.top_index, p.top_key, b, k, ok);
       }
     }
+    if constexpr (kSample)
+      sampler_finish(p.sample_keys, p.stat_partials, B, G, p.sample_index, p.sample_key, p.sample_lse);
     if (!p.dense)
       for (int j = tid; j < c.nbuild; j += kGemmThreads) p.tile_counts[j] = 0;
     if (tid == 0) atomicExch(p.ticket, 0u);
@@ -629,7 +705,9 @@ cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream)
     tile_builder_kernel<T><<<c.nbuild, kBuilderThreads, 0, stream>>>(p, c.ntiles);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
   }
-  auto k = c.npad == 32 ? tc_projection_kernel<T, true> : tc_projection_kernel<T, false>;
+  const bool sample = p.sample_index != nullptr;
+  auto k = c.npad == 32 ? (sample ? tc_projection_kernel<T, true, true> : tc_projection_kernel<T, true, false>)
+                        : (sample ? tc_projection_kernel<T, false, true> : tc_projection_kernel<T, false, false>);
   const size_t smem_bytes = L.total + 1024;
   if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), smem_bytes, dev)) != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
@@ -677,6 +755,14 @@ cudaError_t launch_typed(const BlockGemmParams& p0, cudaStream_t stream) {
     r.ticket = p0.ticket;
     r.error = p0.error;
     r.peers = p0.peers;
+    r.sample_index = p0.sample_index;
+    r.sample_lse = p0.sample_lse;
+    r.sample_key = p0.sample_key;
+    r.seeds = p0.seeds;
+    r.offset = p0.offset;
+    r.inv_temp = p0.inv_temp;
+    r.sample_keys = p0.sample_keys;
+    r.stat_partials = p0.stat_partials;
     return launch_row_sparse(r, std::is_same<T, __nv_bfloat16>::value ? 1 : 0, stream);
   }
   // Batches above kMaxNpad run as consecutive chunks of requests.
@@ -692,6 +778,14 @@ cudaError_t launch_typed(const BlockGemmParams& p0, cudaStream_t stream) {
     if (p0.top_key) p.top_key = p0.top_key + b0;
     p.keys = p0.keys + b0;
     p.peers.batch_base = p0.peers.batch_base + b0;
+    if (p0.sample_index) {
+      p.sample_index = p0.sample_index + b0;
+      if (p0.sample_lse) p.sample_lse = p0.sample_lse + b0;
+      if (p0.sample_key) p.sample_key = p0.sample_key + b0;
+      p.seeds = p0.seeds + b0;
+      p.sample_keys = p0.sample_keys + b0;
+      p.stat_partials = p0.stat_partials + (size_t)b0 * kMaxSlices;
+    }
     if ((err = launch_chunk<T>(p, dev, stream)) != cudaSuccess) return err;
   }
   return cudaSuccess;

@@ -415,14 +415,18 @@ int32_t gsp_top1_from_keys(const int64_t* keys, int32_t batch, float* top_value,
       fn);
 }
 
-int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride, const void* weight,
-                              int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride,
-                              int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype,
-                              int64_t vocab_offset, void* logits, int64_t logits_row_stride, float temperature,
-                              const uint64_t* seeds, uint64_t offset, int64_t* sample_index,
-                              float* sample_logsumexp, int64_t* sample_key, float* top_value, int64_t* top_index,
-                              int64_t* top_key, void* workspace, size_t workspace_bytes_, void* stream) {
-  const char* fn = "gsp_row_sparse_sample";
+// The fused sampler on any route: validation shared by the entry points, then
+// the row-sparse kernels (route 0) or the tensor-core kernels (1 block-sparse,
+// 2 dense) with the sampler in their epilogue.
+static int32_t sample_common(const char* fn, int32_t route, const void* hidden, int64_t hidden_row_stride,
+                      const void* weight, int64_t weight_row_stride, const int32_t* bitmask,
+                      int64_t bitmask_row_stride, int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype,
+                      int64_t vocab_offset, void* logits, int64_t logits_row_stride, float temperature,
+                      const uint64_t* seeds, uint64_t offset, int64_t* sample_index, float* sample_logsumexp,
+                      int64_t* sample_key, float* top_value, int64_t* top_index, int64_t* top_key, void* workspace,
+                      size_t workspace_bytes_, void* stream) {
+  if (route != GSP_ROUTE_ROW_SPARSE && route != GSP_ROUTE_BLOCK_SPARSE && route != GSP_ROUTE_DENSE_MASK)
+    return fail(GSP_ERR_INVALID_ARGUMENT, "%s: unknown route %d", fn, route);
   int32_t st = validate_projection(fn, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
                                    bitmask_row_stride, batch, vocab, hidden_dim, dtype, logits, logits_row_stride);
   if (st != GSP_OK) return st;
@@ -432,21 +436,84 @@ int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride, con
   if (!seeds || !sample_index) return fail(GSP_ERR_INVALID_ARGUMENT, "%s: seeds and sample_index are required", fn);
   st = check_workspace(fn, true, workspace, workspace_bytes_, batch, vocab, true);
   if (st != GSP_OK) return st;
-  RowSparseParams p = make_row_sparse(hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
-                                      bitmask_row_stride, batch, vocab, hidden_dim, vocab_offset);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (route == GSP_ROUTE_ROW_SPARSE) {
+    RowSparseParams p = make_row_sparse(hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                                        bitmask_row_stride, batch, vocab, hidden_dim, vocab_offset);
+    p.logits = logits;
+    p.logits_stride = batch > 1 ? logits_row_stride : vocab;
+    p.top_value = top_value;
+    p.top_index = top_index;
+    p.top_key = top_key;
+    attach_workspace(p, workspace);
+    p.sample_index = sample_index;
+    p.sample_lse = sample_logsumexp;
+    p.sample_key = sample_key;
+    p.seeds = seeds;
+    p.offset = offset;
+    p.inv_temp = 1.0f / temperature;
+    return cuda_status(launch_row_sparse(p, dtype, s), fn);
+  }
+  BlockGemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.hidden = hidden;
+  p.hidden_stride = batch > 1 ? hidden_row_stride : hidden_dim;
+  p.weight = weight;
+  p.weight_stride = vocab > 1 ? weight_row_stride : hidden_dim;
+  p.mask = reinterpret_cast<const uint32_t*>(bitmask);
+  p.mask_stride = batch > 1 ? bitmask_row_stride : 0;
+  p.batch = batch;
+  p.vocab = vocab;
+  p.hidden_dim = hidden_dim;
+  p.nw = (vocab + 31) / 32;
+  p.vocab_offset = vocab_offset;
   p.logits = logits;
   p.logits_stride = batch > 1 ? logits_row_stride : vocab;
   p.top_value = top_value;
   p.top_index = top_index;
   p.top_key = top_key;
-  attach_workspace(p, workspace);
+  Workspace w = carve_workspace(workspace, batch, vocab);
+  p.keys = w.keys;
+  p.ticket = w.ticket;
+  p.error = w.error;
+  p.tile_list = w.tile_list;
+  p.tile_counts = w.tile_counts;
+  p.dense = route == GSP_ROUTE_DENSE_MASK || bitmask == nullptr;
+  p.no_pdl = tl_no_pdl ? 1 : 0;
   p.sample_index = sample_index;
   p.sample_lse = sample_logsumexp;
   p.sample_key = sample_key;
   p.seeds = seeds;
   p.offset = offset;
   p.inv_temp = 1.0f / temperature;
-  return cuda_status(launch_row_sparse(p, dtype, static_cast<cudaStream_t>(stream)), fn);
+  p.sample_keys = w.sample_keys;
+  p.stat_partials = w.stat_partials;
+  return cuda_status(launch_block_gemm(p, dtype, s), fn);
+}
+
+int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                              int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride,
+                              int32_t batch, int32_t vocab, int32_t hidden_dim, int32_t dtype,
+                              int64_t vocab_offset, void* logits, int64_t logits_row_stride, float temperature,
+                              const uint64_t* seeds, uint64_t offset, int64_t* sample_index,
+                              float* sample_logsumexp, int64_t* sample_key, float* top_value, int64_t* top_index,
+                              int64_t* top_key, void* workspace, size_t workspace_bytes_, void* stream) {
+  return sample_common("gsp_row_sparse_sample", GSP_ROUTE_ROW_SPARSE, hidden, hidden_row_stride, weight,
+                       weight_row_stride, bitmask, bitmask_row_stride, batch, vocab, hidden_dim, dtype, vocab_offset,
+                       logits, logits_row_stride, temperature, seeds, offset, sample_index, sample_logsumexp,
+                       sample_key, top_value, top_index, top_key, workspace, workspace_bytes_, stream);
+}
+
+int32_t gsp_sample(int32_t route, const void* hidden, int64_t hidden_row_stride, const void* weight,
+                   int64_t weight_row_stride, const int32_t* bitmask, int64_t bitmask_row_stride, int32_t batch,
+                   int32_t vocab, int32_t hidden_dim, int32_t dtype, int64_t vocab_offset, void* logits,
+                   int64_t logits_row_stride, float temperature, const uint64_t* seeds, uint64_t offset,
+                   int64_t* sample_index, float* sample_logsumexp, int64_t* sample_key, float* top_value,
+                   int64_t* top_index, int64_t* top_key, void* workspace, size_t workspace_bytes_, void* stream) {
+  return sample_common("gsp_sample", route, hidden, hidden_row_stride, weight, weight_row_stride, bitmask,
+                       bitmask_row_stride, batch, vocab, hidden_dim, dtype, vocab_offset, logits, logits_row_stride,
+                       temperature, seeds, offset, sample_index, sample_logsumexp, sample_key, top_value, top_index,
+                       top_key, workspace, workspace_bytes_, stream);
 }
 
 int32_t gsp_vocab_parallel_logits(int32_t route, const void* hidden, int64_t hidden_row_stride,

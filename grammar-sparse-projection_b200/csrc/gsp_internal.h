@@ -110,6 +110,15 @@ struct BlockGemmParams {
   int dense;              // 1: every tile is projected (dense_masked_logits)
   int no_pdl;             // 1: launch the projection without programmatic dependent launch
   PeerExchange peers;     // cross-rank top-1 merge (world < 2: none)
+  // fused sampler (sample_index != nullptr; contract in gsp_sampler.cuh)
+  int64_t* sample_index;
+  float* sample_lse;
+  int64_t* sample_key;
+  const uint64_t* seeds;
+  uint64_t offset;
+  float inv_temp;
+  unsigned long long* sample_keys;    // workspace [batch]
+  unsigned long long* stat_partials;  // workspace [batch][kMaxSlices]
 };
 
 // Workspace layout (fixed offsets first, so calls with different batch sizes

@@ -25,6 +25,7 @@
 #include <stdint.h>
 
 #include "gsp_common.cuh"
+#include "gsp_internal.h"
 
 namespace gsp {
 
@@ -73,6 +74,54 @@ __device__ __forceinline__ void merge_stats(float& m, float& s, float m2, float 
   const float mm = fmaxf(m, m2);
   s = s * __expf(m - mm) + s2 * __expf(m2 - mm);
   m = mm;
+}
+
+// The same noise through one out-of-line copy, for kernels that call it at many
+// unrolled sites (the tensor-core epilogue's columns).
+static __device__ __noinline__ float gumbel_noise_outlined(uint64_t seed, uint64_t offset, uint64_t v) {
+  return gumbel_noise(seed, offset, v);
+}
+
+// Last CTA of a sampling launch of G CTAs: takes the per-request winning
+// sample keys out of the workspace (re-zeroing them) into sample_index /
+// sample_key, and merges the CTAs' (max, sum) partials (request-major rows of
+// kMaxSlices) into sample_lse (re-zeroing them). The ids take one thread per
+// request; the log-sum-exp a warp per request, its lanes loading the G partials
+// (each load instruction coalesced) eight at a time, then merging across the
+// warp with shuffles. All threads of the CTA call it.
+__device__ __forceinline__ void sampler_finish(unsigned long long* sample_keys, unsigned long long* stat_partials,
+                                               int B, int G, int64_t* sample_index, int64_t* sample_key,
+                                               float* sample_lse) {
+  constexpr int kChunkLoads = 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const unsigned long long k = atomicExch(sample_keys + b, 0ull);
+    sample_index[b] = key_index(k);
+    if (sample_key) sample_key[b] = key_to_signed(k);
+  }
+  for (int b = warp; b < B; b += nwarps) {
+    float m = -INFINITY, sum = 0.f;
+    for (int c0 = 0; c0 < G; c0 += 32 * kChunkLoads) {
+      unsigned long long x[kChunkLoads];
+#pragma unroll
+      for (int k = 0; k < kChunkLoads; ++k) {
+        const int c = c0 + lane + 32 * k;
+        x[k] = c < G ? __ldcg(stat_partials + (size_t)b * kMaxSlices + c) : empty_stats();
+      }
+#pragma unroll
+      for (int k = 0; k < kChunkLoads; ++k) {
+        const int c = c0 + lane + 32 * k;
+        if (c < G) stat_partials[(size_t)b * kMaxSlices + c] = 0ull;
+        merge_stats(m, sum, stats_m(x[k]), stats_s(x[k]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(FULL_MASK, m, o), s2 = __shfl_xor_sync(FULL_MASK, sum, o);
+      merge_stats(m, sum, m2, s2);
+    }
+    if (lane == 0 && sample_lse) sample_lse[b] = sum > 0.f ? m + logf(sum) : -INFINITY;
+  }
 }
 
 }  // namespace gsp

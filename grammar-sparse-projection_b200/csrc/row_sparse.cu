@@ -228,43 +228,9 @@ __device__ __forceinline__ bool sample_publish(const RowSparseParams& p, const S
 }
 
 // Last CTA: sampled ids and log-sum-exp per request; re-zeroes the sampler's
-// workspace (keys and every CTA's partials). The ids take one thread per
-// request; the log-sum-exp a warp per request, its lanes loading the G
-// partials (request-major, so each load instruction is coalesced) eight at a
-// time (one L2 round trip per 256 CTAs), then merging across the warp with
-// shuffles.
+// workspace (sampler_finish in gsp_sampler.cuh).
 __device__ __forceinline__ void sample_finish(const RowSparseParams& p) {
-  constexpr int kChunkLoads = 8;
-  const int G = gridDim.x, B = p.batch, lane = threadIdx.x & 31, warp = threadIdx.x >> 5,
-            nwarps = blockDim.x >> 5;
-  for (int b = threadIdx.x; b < B; b += blockDim.x) {
-    const unsigned long long k = atomicExch(p.sample_keys + b, 0ull);
-    p.sample_index[b] = key_index(k);
-    if (p.sample_key) p.sample_key[b] = key_to_signed(k);
-  }
-  for (int b = warp; b < B; b += nwarps) {
-    float m = -INFINITY, sum = 0.f;
-    for (int c0 = 0; c0 < G; c0 += 32 * kChunkLoads) {
-      unsigned long long x[kChunkLoads];
-#pragma unroll
-      for (int k = 0; k < kChunkLoads; ++k) {
-        const int c = c0 + lane + 32 * k;
-        x[k] = c < G ? __ldcg(p.stat_partials + (size_t)b * kMaxSlices + c) : empty_stats();
-      }
-#pragma unroll
-      for (int k = 0; k < kChunkLoads; ++k) {
-        const int c = c0 + lane + 32 * k;
-        if (c < G) p.stat_partials[(size_t)b * kMaxSlices + c] = 0ull;
-        merge_stats(m, sum, stats_m(x[k]), stats_s(x[k]));
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(FULL_MASK, m, o), s2 = __shfl_xor_sync(FULL_MASK, sum, o);
-      merge_stats(m, sum, m2, s2);
-    }
-    if (lane == 0 && p.sample_lse) p.sample_lse[b] = sum > 0.f ? m + logf(sum) : -INFINITY;
-  }
+  sampler_finish(p.sample_keys, p.stat_partials, p.batch, (int)gridDim.x, p.sample_index, p.sample_key, p.sample_lse);
 }
 
 // Last CTA: takes the merged keys out of the workspace (re-zeroing it), merges
@@ -749,9 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
     // greedy: each warp resolves its own units from the prefixes, no unit list
     stream_rows_ranked<T, kWpt>(p, lo, (int)(hi - lo), has_mask, s_excl, s_words, code_stride, s_h, want_top, s_keys);
     if (want_top) finalize_top1<false>(p, s_keys, s_misc, want_top);
-    return;
-  }
-
+  } else {
   for (uint64_t rbase = lo; rbase < hi; rbase += kListCap) {
     const uint64_t rend = min(hi, rbase + (uint64_t)kListCap);
     const int n = (int)(rend - rbase);
@@ -807,7 +771,8 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   }
 
   // ---- 7. top-1 ------------------------------------------------------------
-  if (want_top || kSample) finalize_top1<kSample>(p, s_keys, s_misc, want_top);
+  finalize_top1<kSample>(p, s_keys, s_misc, want_top);
+  }
 }
 
 // ===========================================================================

@@ -71,6 +71,8 @@ SIGNATURES = {
                                ctypes.c_float, _vp, ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                _vp], _i32),
     "gsp_merge_logsumexp": ([_vp, _i32, _i32, _vp, _vp], _i32),
+    "gsp_sample": ([_i32, _vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _vp, _i64,
+                    ctypes.c_float, _vp, ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp], _i32),
     "gsp_peer_exchange_bytes": ([_i32, _i32], _sz),
     "gsp_peer_exchange_alloc": ([_sz, ctypes.POINTER(_vp), _vp], _i32),
     "gsp_peer_exchange_open": ([_vp, ctypes.POINTER(_vp)], _i32),
@@ -432,24 +434,26 @@ class PreparedVocabParallel:
 
 def row_sparse_sample(hidden, weight, mask, seeds, offset: int, temperature: float, sample_index,
                       sample_logsumexp=None, logits=None, top_value=None, top_index=None,
-                      vocab_offset: int = 0, sample_key=None, top_key=None) -> None:
-    """Fused sampler (gsp_row_sparse_sample): Gumbel-max draw per request from
-    softmax(logits / temperature) over the legal tokens, keyed by
-    seeds[b] (uint64 stored as int64) and the step counter `offset`."""
+                      vocab_offset: int = 0, sample_key=None, top_key=None, route: str = "row-sparse") -> None:
+    """Fused sampler: Gumbel-max draw per request from softmax(logits /
+    temperature) over the legal tokens, keyed by seeds[b] (uint64 stored as
+    int64) and the step counter `offset`; route "row-sparse"
+    (gsp_row_sparse_sample) or "block-sparse" / "dense-mask" (gsp_sample: the
+    tensor-core projection with the sampler in its epilogue)."""
     _require_cuda(hidden, weight, mask, seeds, sample_index, sample_logsumexp, logits)
     lib = load()
     batch, hdim = hidden.shape
     vocab = weight.shape[0]
     ws = workspace(hidden.device, batch, vocab)
-    status = lib.gsp_row_sparse_sample(
-        _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
+    status = lib.gsp_sample(
+        ROUTE_CODES[route], _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0),
         _ptr(mask), 0 if mask is None else mask.stride(0),
         batch, vocab, hdim, dtype_code(hidden.dtype), vocab_offset,
         _ptr(logits), 0 if logits is None else logits.stride(0),
         float(temperature), _ptr(seeds), int(offset) & 0xFFFFFFFFFFFFFFFF,
         _ptr(sample_index), _ptr(sample_logsumexp), _ptr(sample_key), _ptr(top_value), _ptr(top_index),
         _ptr(top_key), _ptr(ws), ws.numel(), _stream(hidden.device))
-    _check(status, "gsp_row_sparse_sample")
+    _check(status, "gsp_sample")
 
 
 def merge_logsumexp(lse_parts, out) -> None:

@@ -499,7 +499,7 @@ class SampleResult(NamedTuple):
 
 def grammar_sample(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torch.Tensor, *,
                    seeds: torch.Tensor, step: int, temperature: float = 1.0,
-                   return_logits: bool = False) -> SampleResult:
+                   return_logits: bool = False, route: str = "row-sparse") -> SampleResult:
     """Grammar-conditioned fused sampler: one launch projects the legal rows
     and draws each request's next token from softmax(logits / temperature)
     over its legal tokens, without writing vocabulary-shaped logits unless
@@ -511,8 +511,13 @@ def grammar_sample(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torc
     (token id, step): the same (seeds, step) reproduce the same tokens, on any
     route decomposition; use a new step per decode step. logsumexp gives the
     sampled token's log-probability, logit / temperature - logsumexp. The
-    greedy top-1 comes with it. Shapes are [B, ...] always.
+    greedy top-1 comes with it. Shapes are [B, ...] always. route picks the
+    projection: "row-sparse" (legal rows only), "block-sparse" (tensor-core
+    tiles holding a legal token) or "dense-mask" (every tile); each draws from
+    the same contract, noise computed for legal tokens only.
     """
+    if route not in ROUTES:
+        raise ValueError(f"unknown route {route!r}")
     hidden_2d, mask_2d, _, batch, vocab = _sparse_inputs(hidden, weight, bitmask_gpu)
     _half_only(hidden.dtype, "grammar_sample")
     if seeds.device.type != "cuda" or seeds.dtype != torch.int64 or seeds.numel() != batch:
@@ -526,7 +531,8 @@ def grammar_sample(hidden: torch.Tensor, weight: torch.Tensor, bitmask_gpu: torc
     top_value = torch.empty(batch, device=dev, dtype=torch.float32)
     top_index = torch.empty(batch, device=dev, dtype=torch.int64)
     _native.row_sparse_sample(hidden_2d, weight, mask_2d, seeds.contiguous(), step, temperature, token_ids,
-                              sample_logsumexp=lse, logits=logits, top_value=top_value, top_index=top_index)
+                              sample_logsumexp=lse, logits=logits, top_value=top_value, top_index=top_index,
+                              route=route)
     return SampleResult(token_ids, lse, top_value, top_index, logits)
 
 

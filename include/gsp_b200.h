@@ -250,6 +250,28 @@ int32_t gsp_row_sparse_sample(const void* hidden, int64_t hidden_row_stride,
                               int64_t* top_key, void* workspace, size_t workspace_bytes,
                               void* stream);
 
+/*
+ * The same fused sampler on any route (GSP_ROUTE_*): row-sparse runs
+ * gsp_row_sparse_sample; block-sparse and dense-mask run the tensor-core
+ * projection with the sampler in its epilogue (Gumbel noise only for the legal
+ * entries of the tiles it computes, per-request winning keys and (max, sum of
+ * exp) partials merged by the last CTA). Same arguments and contract as
+ * gsp_row_sparse_sample, so the same (seeds, offset) give the same tokens on
+ * every route up to the last-bit differences of the routes' fp32 summation
+ * order (a draw whose two best perturbed scores lie that close may differ).
+ * No counterpart in the reference (paper/draft.md section 6.4).
+ */
+int32_t gsp_sample(int32_t route, const void* hidden, int64_t hidden_row_stride,
+                   const void* weight, int64_t weight_row_stride,
+                   const int32_t* bitmask, int64_t bitmask_row_stride,
+                   int32_t batch, int32_t vocab, int32_t hidden_dim,
+                   int32_t dtype, int64_t vocab_offset, void* logits,
+                   int64_t logits_row_stride, float temperature,
+                   const uint64_t* seeds, uint64_t offset, int64_t* sample_index,
+                   float* sample_logsumexp, int64_t* sample_key,
+                   float* top_value, int64_t* top_index, int64_t* top_key,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* out[b] = log sum over r < parts of exp(lse[r * batch + b]) (-inf when every
  * part is -inf): merges per-shard log-sum-exps of a vocabulary-parallel
  * sampler step (device arrays). No counterpart in the reference. */

@@ -193,3 +193,63 @@ def test_sharded_sampling_equals_whole_vocabulary(cuda_device, shards):
         ti = torch.empty(batch, dtype=torch.int64, device=dev)
         _native.top1_from_keys(torch.stack(tkeys).max(dim=0).values, tv, ti)
         assert torch.equal(ti, full.top_index) and torch.equal(tv, full.top_value)
+
+
+@pytest.mark.parametrize("route", ["block-sparse", "dense-mask"])
+@pytest.mark.parametrize("case", [
+    # vocab, hidden, batch, dtype, temperature, clustered
+    (50000, 256, 8, torch.float16, 1.0, True),      # narrow epilogue (batch pads to 32)
+    (20011, 192, 40, torch.bfloat16, 0.7, False),   # wide epilogue, ragged vocabulary and hidden size
+    (3000, 128, 300, torch.float16, 1.3, True),     # two batch chunks (256 + 44)
+])
+def test_tensor_core_sample_matches_oracle(cuda_device, route, case):
+    """The sampler in the tensor-core epilogue (gsp_sample, block-sparse and
+    dense-mask routes) draws under the same contract: the oracle's Gumbel-max
+    pick except within the tie tolerance, its log-sum-exp, the greedy top-1 of
+    the materialised logits, and the same tokens on a repeated call; the
+    workspace is left all zero."""
+    vocab, hidden, batch, dtype, temperature, clustered = case
+    rng = np.random.default_rng(vocab + batch + hidden)
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * 0.3).to(dtype)
+    h = torch.from_numpy(rng.standard_normal((batch, hidden), dtype=np.float32)).to(dtype)
+    ks = [int(x) for x in rng.integers(1, max(2, vocab // 50), size=batch)]
+    ks[0] = 0  # a request with no legal token
+    mask = O.make_batch_mask(rng, batch, vocab, ks, clustered=clustered, max_runs=8)
+    dev = cuda_device
+    hd, wd, md = h.to(dev), w.to(dev), torch.from_numpy(mask).to(dev)
+    seeds = _seeds(dev, batch, base=77)
+    for step in (0, 9):
+        res = tr.grammar_sample(hd, wd, md, seeds=seeds, step=step, temperature=temperature, return_logits=True,
+                                route=route)
+        ref = O.sample_reference(h, w, mask, dtype, temperature, seeds.cpu().numpy(), step)
+        _check_against_oracle(res, ref, temperature, f"{route} {case} step {step}")
+        assert torch.equal(res.top_index, res.logits.argmax(-1))
+        again = tr.grammar_sample(hd, wd, md, seeds=seeds, step=step, temperature=temperature, route=route)
+        assert torch.equal(again.token_ids, res.token_ids)
+        assert torch.allclose(again.logsumexp, res.logsumexp, rtol=1e-5, atol=1e-5, equal_nan=True)
+    torch.cuda.synchronize()
+    assert _native.workspace_error(dev) == 0
+    ws = _native.workspace(dev, batch, vocab)
+    assert int(ws[:4].count_nonzero()) == 0 and int(ws[8:].count_nonzero()) == 0
+
+
+def test_tensor_core_sample_batched_workload(cuda_device):
+    """The batched workload's shape (V=248,320, H=2,048 fp16, batch 32, each
+    request 0.5% legal in <= 16 runs) on the block-sparse route: every draw
+    against the oracle, and the same draws as the row-sparse sampler except
+    within the tie tolerance."""
+    dev = cuda_device
+    vocab, hidden, batch = 248_320, 2048, 32
+    g = torch.Generator(device=dev).manual_seed(7)
+    wd = (torch.randn(vocab, hidden, device=dev, generator=g) * 0.02).half()
+    hd = torch.randn(batch, hidden, device=dev, generator=g).half()
+    rng = np.random.default_rng(32)
+    mask = O.make_batch_mask(rng, batch, vocab, [1242] * batch, clustered=True, max_runs=16)
+    md = torch.from_numpy(mask).to(dev)
+    seeds = _seeds(dev, batch, base=5)
+    res = tr.grammar_sample(hd, wd, md, seeds=seeds, step=3, temperature=0.8, route="block-sparse")
+    ref = O.sample_reference(hd.cpu(), wd.cpu(), mask, torch.float16, 0.8, seeds.cpu().numpy(), 3)
+    _check_against_oracle(res, ref, 0.8, "block-sparse batched")
+    rs = tr.grammar_sample(hd, wd, md, seeds=seeds, step=3, temperature=0.8, route="row-sparse")
+    _check_against_oracle(rs, ref, 0.8, "row-sparse batched")
+    assert _native.workspace_error(dev) == 0

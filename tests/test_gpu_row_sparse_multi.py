@@ -1,4 +1,4 @@
-"""GPU parity of the multi-request row-sparse path: masks of more than 8,192
+"""GPU parity of the multi-request row-sparse path: masks of more than 16,384
 flat (request, word) entries go through the cooperative kernel, which splits
 the mask into one word slice per CTA and balances legal rows across CTAs
 from the published slice counts.
@@ -60,7 +60,7 @@ def test_rows_packed_into_one_request(cuda_device):
 def test_all_legal_several_rounds(cuda_device, dtype):
     """400,000 units: about 2,700 per CTA, more than one list round each."""
     rng = np.random.default_rng(32)
-    vocab, hidden, batch = 100000, 64, 4
+    vocab, hidden, batch = 100000, 64, 6
     w, h = _inputs(rng, vocab, hidden, batch, dtype)
     mask = O.make_batch_mask(rng, batch, vocab, [vocab] * batch)
     logits, _, _ = _run_and_check(cuda_device, h, w, mask, dtype, "all legal")
@@ -69,7 +69,7 @@ def test_all_legal_several_rounds(cuda_device, dtype):
 
 def test_no_legal_token_anywhere(cuda_device):
     rng = np.random.default_rng(33)
-    vocab, hidden, batch = 40000, 64, 8
+    vocab, hidden, batch = 40000, 64, 16
     w, h = _inputs(rng, vocab, hidden, batch, torch.float16)
     mask = np.zeros((batch, O.mask_words(vocab)), dtype=np.int32)
     dev = cuda_device
@@ -97,9 +97,9 @@ def test_slices_longer_than_one_chunk(cuda_device, clustered):
 
 def test_compact_output_and_offsets(cuda_device):
     rng = np.random.default_rng(35)
-    vocab, hidden, batch = 60001, 128, 6
+    vocab, hidden, batch = 60001, 128, 10
     w, h = _inputs(rng, vocab, hidden, batch, torch.bfloat16)
-    ks = [5, 0, 7000, 60001, 1, 300]
+    ks = [5, 0, 7000, 60001, 1, 300, 12, 0, 2500, 60001]
     mask = O.make_batch_mask(rng, batch, vocab, ks, clustered=True, max_runs=8)
     ids, lg, off = tr.bitmask_compact_logits(h.to(cuda_device), w.to(cuda_device), torch.from_numpy(mask).to(cuda_device))
     assert off.tolist() == list(np.concatenate([[0], np.cumsum(ks)]))
@@ -115,7 +115,7 @@ def test_compact_output_and_offsets(cuda_device):
 def test_broadcast_mask_and_ragged_vocab(cuda_device):
     """One mask row for every request (row stride 0), V % 32 != 0."""
     rng = np.random.default_rng(36)
-    vocab, hidden, batch = 40007, 96, 10
+    vocab, hidden, batch = 40007, 96, 14
     w, h = _inputs(rng, vocab, hidden, batch, torch.float16)
     row = O.recipe_mask("c900", rng, 1, vocab)
     mask_full = np.repeat(row, batch, axis=0)
@@ -130,7 +130,7 @@ def test_broadcast_mask_and_ragged_vocab(cuda_device):
 def test_repeated_calls_are_identical(cuda_device):
     """Slice counts, flags and the unit list are re-zeroed by the kernel itself."""
     rng = np.random.default_rng(37)
-    vocab, hidden, batch = 70000, 64, 5
+    vocab, hidden, batch = 70000, 64, 8
     w, h = _inputs(rng, vocab, hidden, batch, torch.float16)
     mask = O.make_batch_mask(rng, batch, vocab, [10, 2000, 0, 70000, 333], clustered=True, max_runs=4)
     first = _run_and_check(cuda_device, h, w, mask, torch.float16, "call 0")

@@ -47,7 +47,7 @@ def _check_against_oracle(res, ref, temperature, dtype_label):
 @pytest.mark.parametrize("case", [
     # vocab, hidden, batch, dtype, temperature, clustered, misaligned  (kernel)
     (50000, 256, 1, torch.float16, 1.0, False, False),     # staged
-    (40000, 128, 8, torch.bfloat16, 0.7, True, False),     # cooperative
+    (40000, 128, 16, torch.bfloat16, 0.7, True, False),    # cooperative (20,000 flat words)
     (3000, 96, 3, torch.float16, 1.5, False, True),        # direct (unaligned hidden)
 ])
 def test_sample_matches_oracle(cuda_device, case):

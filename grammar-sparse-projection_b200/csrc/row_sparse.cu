@@ -58,9 +58,6 @@ constexpr size_t kStagedSmemMax = 200 * 1024;  // list + keys + mask slice + hid
 // (batch 2 at V=248,320, 15,520 words, measured 14.2 us on the staged kernel
 // against 16.1 us on the cooperative one.)
 constexpr int64_t kCoopMinWords = 16384;
-// Greedy calls with masks up to this many flat words take the ranked kernel
-// (every CTA reads the mask from L2) instead of the cooperative one.
-constexpr int64_t kRankedMaxWords = 65536;
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -480,11 +477,11 @@ __device__ __forceinline__ uint32_t code_of_rank(uint32_t r, const uint32_t* s_e
 // Greedy streaming of the CTA's units of rank [rbase, rbase + n) with no unit
 // list: warp w takes units w, w + 16, w + 32, ... two rows at a time, and
 // before every 16 such pairs its 32 lanes resolve those 32 units' codes at
-// once (code_of(r): the unit code of global rank r). No block barrier
-// between the scan and the first row load. With kHSmem the hidden states are
-// in s_h (request b at b * H), else read from global memory.
-template <typename T, bool kHSmem, typename CodeFn>
-__device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uint64_t rbase, int n, CodeFn code_of,
+// once (code_of_rank; without a mask the code follows from the rank). No
+// block barrier between the scan and the first row load.
+template <typename T, int kWpt>
+__device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uint64_t rbase, int n, bool has_mask,
+                                                   const uint32_t* s_excl, const uint32_t* s_words,
                                                    uint32_t code_stride, const void* s_h, bool want_top,
                                                    unsigned long long* s_keys) {
   using Bits = typename DTypeTraits<T>::Bits;
@@ -494,7 +491,16 @@ __device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uin
   RunningSample rs;
   for (int g0 = warp; g0 < n; g0 += 32 * kWarps) {
     const int my_i = g0 + lane * kWarps;
-    const uint32_t my_code = my_i < n ? code_of(rbase + (uint64_t)my_i) : 0u;
+    uint32_t my_code = 0u;
+    if (my_i < n) {
+      const uint64_t r = rbase + (uint64_t)my_i;
+      if (has_mask) {
+        my_code = code_of_rank<kWpt>((uint32_t)r, s_excl, s_words, p.nw, code_stride);
+      } else {
+        const uint32_t b = (uint32_t)(r / (uint64_t)p.vocab);
+        my_code = b * code_stride + (uint32_t)(r - (uint64_t)b * p.vocab);
+      }
+    }
     for (int k = 0; k < 32; k += 2) {
       const int i = g0 + k * kWarps;
       if (i >= n) break;
@@ -506,12 +512,8 @@ __device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uin
       const int bb = (int)(cb / code_stride), vb = (int)(cb - (uint32_t)bb * code_stride);
       const uint4* wa = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)va * p.weight_stride);
       const uint4* wb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)vb * p.weight_stride);
-      const uint4* ha = kHSmem ? reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)ba * H)
-                               : reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) +
-                                                                (int64_t)ba * p.hidden_stride);
-      const uint4* hb = kHSmem ? reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)bb * H)
-                               : reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) +
-                                                                (int64_t)bb * p.hidden_stride);
+      const uint4* ha = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)ba * H);
+      const uint4* hb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)bb * H);
       float acc_a = 0.f, acc_b = 0.f;
       for (int base = 0; base < nvec; base += 32 * kUnroll) {
         uint4 ra[kUnroll], rb[kUnroll];
@@ -525,8 +527,8 @@ __device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uin
         for (int u = 0; u < kUnroll; ++u) {
           const int e = base + u * 32 + lane;
           if (e < nvec) {
-            acc_a = dot_vec<T>(ra[u], kHSmem ? ha[e] : __ldg(ha + e), acc_a);
-            if (has2) acc_b = dot_vec<T>(rb[u], kHSmem ? hb[e] : __ldg(hb + e), acc_b);
+            acc_a = dot_vec<T>(ra[u], ha[e], acc_a);
+            if (has2) acc_b = dot_vec<T>(rb[u], hb[e], acc_b);
           }
         }
       }
@@ -713,12 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   const uint32_t code_stride = (uint32_t)nw * 32u;
   if constexpr (!kSample) {
     // greedy: each warp resolves its own units from the prefixes, no unit list
-    auto code_of = [&](uint64_t r) -> uint32_t {
-      if (has_mask) return code_of_rank<kWpt>((uint32_t)r, s_excl, s_words, nw, code_stride);
-      const uint32_t b = (uint32_t)(r / (uint64_t)V);
-      return b * code_stride + (uint32_t)(r - (uint64_t)b * V);
-    };
-    stream_rows_ranked<T, true>(p, lo, (int)(hi - lo), code_of, code_stride, s_h, want_top, s_keys);
+    stream_rows_ranked<T, kWpt>(p, lo, (int)(hi - lo), has_mask, s_excl, s_words, code_stride, s_h, want_top, s_keys);
     if (want_top) finalize_top1<false>(p, s_keys, s_misc, want_top);
   } else {
   for (uint64_t rbase = lo; rbase < hi; rbase += kListCap) {
@@ -778,198 +775,6 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   // ---- 7. top-1 ------------------------------------------------------------
   finalize_top1<kSample>(p, s_keys, s_misc, want_top);
   }
-}
-
-// ===========================================================================
-// ranked kernel (greedy; masks of 16,385 .. kRankedMaxWords flat words)
-// ===========================================================================
-// Every CTA streams the whole flat mask from L2 in 16-word groups, keeping
-// only each group's popcount in shared memory; one block scan turns the
-// counts into global rank prefixes per group (4 bytes per 16 words). A warp
-// resolves a unit of rank r by a binary search over the group prefixes and
-// one re-read of that group's 16 words (64 bytes, from L2). No CTA waits for
-// another before its rows, at the price of every CTA reading the mask from L2
-// (batch x ceil(V/32) x 4 bytes each), which is why the cooperative kernel
-// takes the larger masks.
-constexpr int kGroupWords = 16;
-constexpr int kGroupBatch = 4;  // groups whose loads one thread keeps in flight
-
-struct RankedLayout {
-  size_t gpre, keys, warp, misc, hidden, total;
-};
-
-__host__ __device__ inline RankedLayout ranked_layout(int batch, int hidden_dim, int elem_bytes, int64_t ngroups,
-                                                      bool hsmem) {
-  RankedLayout l;
-  size_t off = 0;
-  l.gpre = off;
-  off += 4 * (size_t)ngroups;
-  l.keys = align_up(off, 16);
-  off = l.keys + 8 * (size_t)batch;
-  l.warp = align_up(off, 16);
-  off = l.warp + 4 * 32;
-  l.misc = align_up(off, 16);
-  off = l.misc + 16;
-  l.hidden = align_up(off, 16);
-  off = l.hidden + (hsmem ? (size_t)elem_bytes * batch * hidden_dim : 0);
-  l.total = align_up(off, 128);
-  return l;
-}
-
-// Words [16 g, 16 g + 16) of the flat (request, word) mask, bits at or beyond
-// the vocabulary cleared, flat words at or beyond F read as 0. vec: 16-byte
-// loads (nw % 4 == 0 and 16-byte aligned mask rows, so every 4-word vector
-// lies inside one request).
-__device__ __forceinline__ void load_group(const RowSparseParams& p, int64_t g, int64_t F, bool vec,
-                                           uint32_t tail_keep, uint32_t (&w)[kGroupWords]) {
-  const int nw = p.nw;
-  if (vec) {
-#pragma unroll
-    for (int v = 0; v < kGroupWords / 4; ++v) {
-      const int64_t f = g * kGroupWords + 4 * v;
-      uint4 x = make_uint4(0, 0, 0, 0);
-      if (f < F) {
-        const int b = (int)(f / nw), wi = (int)(f - (int64_t)b * nw);
-        x = __ldg(reinterpret_cast<const uint4*>(p.mask + (int64_t)b * p.mask_stride + wi));
-        if (wi == nw - 4) x.w &= tail_keep;
-      }
-      w[4 * v] = x.x;
-      w[4 * v + 1] = x.y;
-      w[4 * v + 2] = x.z;
-      w[4 * v + 3] = x.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < kGroupWords; ++j) {
-      const int64_t f = g * kGroupWords + j;
-      uint32_t x = 0u;
-      if (f < F) {
-        const int b = (int)(f / nw), wi = (int)(f - (int64_t)b * nw);
-        x = __ldg(p.mask + (int64_t)b * p.mask_stride + wi);
-        if (wi == nw - 1) x &= tail_keep;
-      }
-      w[j] = x;
-    }
-  }
-}
-
-template <typename T, bool kHSmem>
-__global__ void __launch_bounds__(kThreads, 1) row_sparse_ranked_kernel(const RowSparseParams p) {
-  // Launched with programmatic dependent launch allowed: nothing is read or
-  // written before the previous kernel in the stream has completed.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  using Bits = typename DTypeTraits<T>::Bits;
-  extern __shared__ __align__(1024) unsigned char smem[];
-  const int B = p.batch, V = p.vocab, H = p.hidden_dim, nw = p.nw;
-  const int64_t F = (int64_t)B * nw;
-  const int64_t NG = (F + kGroupWords - 1) / kGroupWords;
-  const RankedLayout L = ranked_layout(B, H, (int)sizeof(Bits), NG, kHSmem);
-  uint32_t* s_gpre = reinterpret_cast<uint32_t*>(smem + L.gpre);
-  unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
-  uint32_t* s_warp = reinterpret_cast<uint32_t*>(smem + L.warp);
-  int* s_misc = reinterpret_cast<int*>(smem + L.misc);
-  Bits* s_h = reinterpret_cast<Bits*>(smem + L.hidden);
-
-  const int tid = threadIdx.x;
-  const int G = gridDim.x, cta = blockIdx.x;
-  const bool want_top = (p.top_value != nullptr) | (p.top_index != nullptr) | (p.top_key != nullptr);
-  const uint32_t tail_keep = (V & 31) ? ((1u << (V & 31)) - 1u) : 0xffffffffu;
-  const bool vec = ((reinterpret_cast<uintptr_t>(p.mask) & 15) == 0) && (nw % 4 == 0) &&
-                   (B == 1 || p.mask_stride % 4 == 0);
-
-  if constexpr (kHSmem) {
-    const int nvec = H / DTypeTraits<T>::kPerVec;
-    for (int i = tid; i < B * nvec; i += kThreads) {
-      const int b = i / nvec, j = i - b * nvec;
-      reinterpret_cast<uint4*>(s_h)[i] = __ldg(
-          reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
-    }
-  }
-  for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
-
-  // ---- 1. group popcounts of this thread's contiguous groups ----------------
-  const int64_t per = (NG + kThreads - 1) / kThreads;
-  const int64_t g0 = min((int64_t)tid * per, NG), g1 = min(g0 + per, NG);
-  uint32_t cnt = 0;
-  for (int64_t gb = g0; gb < g1; gb += kGroupBatch) {
-    uint32_t w[kGroupBatch][kGroupWords];
-#pragma unroll
-    for (int k = 0; k < kGroupBatch; ++k) {  // every load of the batch in flight at once
-      if (gb + k < g1) {
-        load_group(p, gb + k, F, vec, tail_keep, w[k]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < kGroupWords; ++j) w[k][j] = 0u;
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < kGroupBatch; ++k) {
-      uint32_t c = 0;
-#pragma unroll
-      for (int j = 0; j < kGroupWords; ++j) c += (uint32_t)__popc(w[k][j]);
-      if (gb + k < g1) s_gpre[gb + k] = c;
-      cnt += c;
-    }
-  }
-
-  // ---- 2. group counts -> global rank prefixes --------------------------------
-  uint32_t tot;
-  uint32_t run = block_exclusive_scan(cnt, s_warp, &tot);  // contains __syncthreads
-  for (int64_t g = g0; g < g1; ++g) {
-    const uint32_t c = s_gpre[g];
-    s_gpre[g] = run;
-    run += c;
-  }
-  __syncthreads();
-  const uint64_t total = (uint64_t)tot;
-  const uint64_t lo = total * (uint64_t)cta / (uint64_t)G;
-  const uint64_t hi = total * (uint64_t)(cta + 1) / (uint64_t)G;
-  const uint32_t code_stride = (uint32_t)nw * 32u;
-
-  // ---- 3. rows: unit of rank r from the group prefixes ---------------------
-  auto code_of = [&](uint64_t r64) -> uint32_t {
-    const uint32_t r = (uint32_t)r64;
-    int64_t lo_g = 0, hi_g = NG - 1;  // largest g with s_gpre[g] <= r (s_gpre[0] == 0)
-    while (lo_g < hi_g) {
-      const int64_t mid = (lo_g + hi_g + 1) >> 1;
-      if (s_gpre[mid] <= r) lo_g = mid; else hi_g = mid - 1;
-    }
-    uint32_t w[kGroupWords];
-    load_group(p, lo_g, F, vec, tail_keep, w);
-    uint32_t local = r - s_gpre[lo_g];
-    uint32_t word = 0u;
-    int q = 0;
-    bool found = false;
-#pragma unroll
-    for (int j = 0; j < kGroupWords; ++j) {
-      const uint32_t pc = (uint32_t)__popc(w[j]);
-      if (!found) {
-        if (local < pc) {
-          found = true;
-          word = w[j];
-          q = j;
-        } else {
-          local -= pc;
-        }
-      }
-    }
-    const int64_t f = lo_g * kGroupWords + q;
-    const int b = (int)(f / nw), wi = (int)(f - (int64_t)b * nw);
-    return (uint32_t)b * code_stride + (uint32_t)(wi * 32 + (int)__fns(word, 0u, (int)local + 1));
-  };
-  auto fill = [&]() {  // -inf over the illegal entries of this CTA's slice of words
-    if (p.logits) {
-      const int64_t w_lo = F * cta / G, w_hi = F * (cta + 1) / G;
-      fill_illegal<T>(p, w_lo, w_hi, [&](int64_t, int b, int w) {
-        return tail_clip(__ldg(p.mask + (int64_t)b * p.mask_stride + w), w, V);
-      });
-    }
-  };
-  fill();
-  stream_rows_ranked<T, kHSmem>(p, lo, (int)(hi - lo), code_of, code_stride, s_h, want_top, s_keys);
-
-  // ---- 4. top-1 --------------------------------------------------------------
-  if (want_top) finalize_top1<false>(p, s_keys, s_misc, want_top);
 }
 
 // ===========================================================================
@@ -1518,32 +1323,6 @@ cudaError_t launch_typed(const RowSparseParams& p, cudaStream_t stream) {
                    (p.weight_stride % kPV == 0) && ((reinterpret_cast<uintptr_t>(p.hidden) & 15) == 0) &&
                    (p.batch == 1 || p.hidden_stride % kPV == 0);
   const int64_t F64 = p.mask ? (int64_t)p.batch * p.nw : 0;
-  if constexpr (!kSample) {
-    // greedy, no compact output, mask of 16,385 .. kRankedMaxWords words: the ranked kernel
-    const bool want_top = p.top_value || p.top_index || p.top_key;
-    if (vec && F64 > kCoopMinWords && F64 <= kRankedMaxWords && p.compact == nullptr && p.offsets == nullptr &&
-        (!want_top || (p.keys != nullptr && p.ticket != nullptr))) {
-      const int64_t ng = (F64 + kGroupWords - 1) / kGroupWords;
-      const size_t elem = sizeof(typename DTypeTraits<T>::Bits);
-      const bool hsmem = (size_t)p.batch * p.hidden_dim * elem <= (size_t)kHStageBytes;
-      const RankedLayout L = ranked_layout(p.batch, p.hidden_dim, (int)elem, ng, hsmem);
-      if (L.total <= kStagedSmemMax) {
-        auto k = hsmem ? row_sparse_ranked_kernel<T, true> : row_sparse_ranked_kernel<T, false>;
-        if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), L.total, dev)) != cudaSuccess) return err;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)grid);
-        cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = L.total;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, k, p);
-      }
-    }
-  }
   if (vec && F64 > kCoopMinWords && p.slice_counts != nullptr && p.published != nullptr && p.slice_ready != nullptr &&
       F64 * 32 < (int64_t)1 << 32) {
     const CoopLayout L = coop_layout(p.batch);

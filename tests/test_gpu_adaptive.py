@@ -19,9 +19,9 @@ pytestmark = pytest.mark.gpu
 
 # Small head with the cost model steered so that all three routes occur:
 # sparse uniform masks -> row-sparse (the multi-request cooperative kernel at
-# 72 x 1,024 mask words, launched cooperatively inside a conditional node's
-# body), one shared 10% run -> block-sparse, 95% uniform -> dense-mask.
-V, H, B = 32768, 512, 72
+# 24 x 1,024 mask words), one shared 10% run -> block-sparse, 95% uniform ->
+# dense-mask.
+V, H, B = 32768, 512, 24
 COST = {"row_sparse_fixed_us": 0.5, "block_floor_us": 0.0, "block_fixed_us": 1.0, "dense_fixed_us": 0.0}
 EXPECTED = {"sparse": "row-sparse", "shared": "block-sparse", "wide": "dense-mask"}
 DIRECT = {"row-sparse": _native.row_sparse, "block-sparse": _native.block_gemm, "dense-mask": _native.dense_masked}

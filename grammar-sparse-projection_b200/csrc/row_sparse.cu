@@ -285,6 +285,86 @@ __device__ __forceinline__ void finalize_top1(const RowSparseParams& p, unsigned
   }
 }
 
+// ---------------------------------------------------------------------------
+// Polled cross-CTA top-1 merge (greedy kernels, small batches).
+//
+// The ticket merge above costs three dependent L2 round trips on the last
+// CTA's path (atomicMax + fence, ticket, key read). Here every CTA but the
+// decoder (the last block index) stores its per-request keys as self-tagged
+// 8-byte words into its own slots, [batch][grid] in the workspace's unit-list
+// region, and leaves: no fence, no ticket. Bits 24..31 of a key are always set
+// while every global token id is below 2^24 - 1 (the low word is
+// 0xffffffff - id), so they carry a fixed non-zero tag; the empty key travels
+// as the tag alone. The decoder, after its own rows, polls the slots until
+// each carries the tag, folds them into its shared-memory keys, re-zeroes
+// them and writes the top-1. Only the decoder waits, and only on CTAs that
+// never wait, so the merge needs no co-residency guarantee; the wait is still
+// bounded (error word 4 and no token reported when it runs out, after which
+// the caller re-zeroes the workspace).
+// ---------------------------------------------------------------------------
+constexpr int kPolledMaxBatch = 8;
+constexpr uint32_t kSlotTag = 0x5Au;
+constexpr int64_t kSlotWaitNs = 200000000;  // 0.2 s
+constexpr uint32_t kSlotPollLimit = 1u << 22;
+
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Whether this launch merges its top-1 keys by polled slots (uniform across
+// the grid; the host's workspace carve gives unit_list/list_cap).
+__device__ __forceinline__ bool polled_merge_ok(const RowSparseParams& p) {
+  return p.unit_list != nullptr && p.batch <= kPolledMaxBatch &&
+         (uint64_t)p.vocab_offset + (uint64_t)p.vocab < (1ull << 24) - 1 &&
+         8ull * gridDim.x * (uint64_t)p.batch <= 4ull * (uint64_t)p.list_cap;
+}
+
+// All threads of every CTA call it after their units; s_keys[0, batch) holds
+// the CTA's keys. s_word: one word of shared memory.
+__device__ __forceinline__ void finalize_top1_polled(const RowSparseParams& p, unsigned long long* s_keys,
+                                                     uint32_t* s_word) {
+  const int tid = threadIdx.x, G = gridDim.x, B = p.batch;
+  unsigned long long* slots = reinterpret_cast<unsigned long long*>(p.unit_list);
+  __syncthreads();  // every warp's running key is in s_keys
+  if ((int)blockIdx.x != G - 1) {
+    for (int b = tid; b < B; b += blockDim.x) st_relaxed_gpu_u64(slots + (size_t)b * G + blockIdx.x, tag_key(s_keys[b], kSlotTag));
+    return;
+  }
+  bool late = false;
+  const uint64_t t0 = globaltimer_ns();
+  for (int i = tid; i < B * (G - 1); i += blockDim.x) {
+    const int b = i / (G - 1), c = i - b * (G - 1);
+    unsigned long long* s = slots + (size_t)b * G + c;
+    bool ok = false;
+    unsigned long long w = 0ull;
+    for (uint32_t it = 0; it < kSlotPollLimit; ++it) {
+      w = ld_relaxed_gpu_u64(s);
+      if (tag_is(w, kSlotTag)) {
+        ok = true;
+        break;
+      }
+      if ((int64_t)(globaltimer_ns() - t0) > kSlotWaitNs) break;
+    }
+    if (ok) {
+      const unsigned long long k = untag_key(w);
+      if (k != 0ull) atomicMax(&s_keys[b], k);
+      *s = 0ull;
+    } else {
+      late = true;
+    }
+  }
+  const bool failed = __syncthreads_or(late);
+  if (failed && tid == 0 && p.error) atomicExch(p.error, 4);
+  bool ok = !failed;
+  if (p.peers.world > 1) ok = peer_exchange_keys(p.peers, s_keys, B, s_word, p.error) && ok;
+  for (int b = tid; b < B; b += blockDim.x) store_top1(p.top_value, p.top_index, p.top_key, b, s_keys[b], ok);
+}
+
 // -inf over the illegal entries of flat words [w_lo, w_hi). word_of(f, b, w)
 // returns the word with bits at or beyond `vocab` already cleared or not; rows
 // beyond `vocab` are never written either way.
@@ -716,7 +796,12 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   if constexpr (!kSample) {
     // greedy: each warp resolves its own units from the prefixes, no unit list
     stream_rows_ranked<T, kWpt>(p, lo, (int)(hi - lo), has_mask, s_excl, s_words, code_stride, s_h, want_top, s_keys);
-    if (want_top) finalize_top1<false>(p, s_keys, s_misc, want_top);
+    if (want_top) {
+      if (polled_merge_ok(p))
+        finalize_top1_polled(p, s_keys, reinterpret_cast<uint32_t*>(s_misc + 1));
+      else
+        finalize_top1<false>(p, s_keys, s_misc, want_top);
+    }
   } else {
   for (uint64_t rbase = lo; rbase < hi; rbase += kListCap) {
     const uint64_t rend = min(hi, rbase + (uint64_t)kListCap);

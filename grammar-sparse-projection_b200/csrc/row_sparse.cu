@@ -369,20 +369,18 @@ __device__ __forceinline__ void finalize_top1_polled(const RowSparseParams& p, u
 // returns the word with bits at or beyond `vocab` already cleared or not; rows
 // beyond `vocab` are never written either way.
 // Threads [t0, t0 + nt) of the CTA take part (default: all of them).
-template <typename T, typename WordFn>
-__device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w_lo, int64_t w_hi, WordFn word_of,
-                                             int t0 = 0, int nt = 0) {
+// I: the index type of the loop (32-bit whenever the byte count allows).
+template <typename T, typename I, typename WordFn>
+__device__ __forceinline__ void fill_illegal_range(const RowSparseParams& p, I w_lo, I w_hi, WordFn word_of, int me,
+                                                   int nt) {
   const int V = p.vocab, nw = p.nw;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.logits) & 15) == 0) && (p.logits_stride % 8 == 0);
   using Bits = typename DTypeTraits<T>::Bits;
   const Bits ninf = DTypeTraits<T>::kNegInfBits;
-  if (nt == 0) nt = blockDim.x;
-  const int me = (int)threadIdx.x - t0;
-  if (me < 0 || me >= nt) return;
-  for (int64_t g = w_lo * 4 + me; g < w_hi * 4; g += nt) {
-    const int64_t f = g >> 2;
+  for (I g = w_lo * 4 + me; g < w_hi * 4; g += nt) {
+    const I f = g >> 2;
     const int q = (int)(g & 3);
-    const int b = (int)(f / nw), w = (int)(f - (int64_t)b * nw);
+    const int b = p.batch == 1 ? 0 : (int)(f / nw), w = (int)(f - (I)b * nw);
     const uint32_t byte = (word_of(f, b, w) >> (q * 8)) & 0xffu;
     const int row0 = w * 32 + q * 8;
     if (row0 >= V || byte == 0xffu) continue;
@@ -401,6 +399,18 @@ __device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w
         if (!((byte >> e) & 1u) && row0 + e < V) dst[e] = ninf;
     }
   }
+}
+
+template <typename T, typename WordFn>
+__device__ __forceinline__ void fill_illegal(const RowSparseParams& p, int64_t w_lo, int64_t w_hi, WordFn word_of,
+                                             int t0 = 0, int nt = 0) {
+  if (nt == 0) nt = blockDim.x;
+  const int me = (int)threadIdx.x - t0;
+  if (me < 0 || me >= nt) return;
+  if (w_hi * 4 + nt < (int64_t)INT32_MAX)
+    fill_illegal_range<T, int>(p, (int)w_lo, (int)w_hi, word_of, me, nt);
+  else
+    fill_illegal_range<T, int64_t>(p, w_lo, w_hi, word_of, me, nt);
 }
 
 // Streams units s_list[0, n) (two rows per warp in flight) and emits them.
@@ -695,44 +705,63 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   const uint32_t tail_keep = (V & 31) ? ((1u << (V & 31)) - 1u) : 0xffffffffu;
   const int f0 = tid * kWpt;  // this thread's words: flat [f0, f0 + kWpt)
 
-  // ---- 1. loads: this thread's mask words (registers), hidden states (smem) --
+  // ---- 1. loads: this thread's mask words (registers), hidden states (smem).
+  //         Every load of the phase is issued before any result is used, so
+  //         the phase costs one round trip, not one per load. -----------------
+  const int hvec = B * nvec;
+  uint4 hx = make_uint4(0, 0, 0, 0);
+  if (tid < hvec) {
+    const int b = tid / nvec, j = tid - b * nvec;
+    hx = __ldg(reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);
+  }
   uint32_t wd[kWpt];
   if (has_mask) {
     const bool vec = ((reinterpret_cast<uintptr_t>(p.mask) & 15) == 0) && (nw % 4 == 0) &&
                      (B == 1 || p.mask_stride % 4 == 0);
     if (vec) {
+      uint4 x[kV];
+      bool tail[kV];
 #pragma unroll
       for (int v = 0; v < kV; ++v) {
         const int f = f0 + 4 * v;
-        uint4 x = make_uint4(0, 0, 0, 0);
+        x[v] = make_uint4(0, 0, 0, 0);
+        tail[v] = false;
         if (f < F) {
-          const int b = f / nw, w = f - b * nw;  // w % 4 == 0
-          x = __ldg(reinterpret_cast<const uint4*>(p.mask + (int64_t)b * p.mask_stride + w));
-          if (w == nw - 4) x.w &= tail_keep;
+          const int b = B == 1 ? 0 : f / nw, w = f - b * nw;  // w % 4 == 0
+          tail[v] = (w == nw - 4);
+          x[v] = __ldg(reinterpret_cast<const uint4*>(p.mask + (int64_t)b * p.mask_stride + w));
         }
-        wd[4 * v] = x.x;
-        wd[4 * v + 1] = x.y;
-        wd[4 * v + 2] = x.z;
-        wd[4 * v + 3] = x.w;
+      }
+#pragma unroll
+      for (int v = 0; v < kV; ++v) {
+        wd[4 * v] = x[v].x;
+        wd[4 * v + 1] = x[v].y;
+        wd[4 * v + 2] = x[v].z;
+        wd[4 * v + 3] = tail[v] ? (x[v].w & tail_keep) : x[v].w;
       }
     } else {
+      bool tail[kWpt];
 #pragma unroll
       for (int j = 0; j < kWpt; ++j) {
         const int f = f0 + j;
-        uint32_t x = 0u;
+        wd[j] = 0u;
+        tail[j] = false;
         if (f < F) {
-          const int b = f / nw, w = f - b * nw;
-          x = __ldg(p.mask + (int64_t)b * p.mask_stride + w);
-          if (w == nw - 1) x &= tail_keep;
+          const int b = B == 1 ? 0 : f / nw, w = f - b * nw;
+          tail[j] = (w == nw - 1);
+          wd[j] = __ldg(p.mask + (int64_t)b * p.mask_stride + w);
         }
-        wd[j] = x;
       }
+#pragma unroll
+      for (int j = 0; j < kWpt; ++j)
+        if (tail[j]) wd[j] &= tail_keep;
     }
   } else {
 #pragma unroll
     for (int j = 0; j < kWpt; ++j) wd[j] = 0u;
   }
-  for (int i = tid; i < B * nvec; i += kThreads) {
+  if (tid < hvec) reinterpret_cast<uint4*>(s_h)[tid] = hx;
+  for (int i = tid + kThreads; i < hvec; i += kThreads) {
     const int b = i / nvec, j = i - b * nvec;
     reinterpret_cast<uint4*>(s_h)[i] = __ldg(
         reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.hidden) + (int64_t)b * p.hidden_stride) + j);

@@ -20,14 +20,17 @@
 //   3. one block-wide scan of per-thread popcounts gives every thread the
 //      rank of its first legal unit; words and per-word rank prefixes are
 //      staged in shared memory with 16-byte stores;
-//   4. the threads holding the CTA's first and last rank publish its word
-//      range, and every thread emits the units of one word of it;
-//   5. each warp streams two whole rows at a time with L1-bypassing 16-byte
+//   4. -inf is written over the illegal entries of the CTA's slice of the
+//      output;
+//   5. the two threads holding the CTA's first and last rank publish
+//      themselves (a test on their own rank range, no per-word search), and
+//      every thread lists the units of one word of theirs in shared memory;
+//   6. each warp streams two whole rows at a time with L1-bypassing 16-byte
 //      loads, dots them against h in shared memory and reduces with shuffles;
-//   6. -inf is written over the illegal entries of the CTA's slice of the output;
-//   7. greedy top-1 keys (rounded value, inverted index) are kept per warp,
-//      merged in shared memory and then with one global atomicMax per request;
-//      the last CTA to arrive decodes them and re-zeroes the workspace.
+//   7. greedy top-1 keys (rounded value, inverted index) are kept per warp and
+//      merged in shared memory; small batches then use the polled merge
+//      (self-tagged per-CTA slots read by the last CTA), others one global
+//      atomicMax per request and an arrival ticket whose last holder decodes.
 //
 // row_sparse_direct_kernel (generic path: any alignment, H % 8 != 0, masks too
 // large for shared memory): the same decomposition, reading the mask and the
@@ -524,54 +527,87 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
   return incl - v + (warp > 0 ? s_warp[warp - 1] : 0u);
 }
 
-// Unit code (request * code_stride + row) of rank r, found from the per-thread
-// exclusive rank prefixes s_excl[kThreads] (non-decreasing, s_excl[0] == 0)
-// and the staged mask words (kWpt words per thread, transposed layout): the
-// thread holding rank r is the largest t with s_excl[t] <= r (nine dependent
-// shared-memory reads), then the word inside its kWpt words, then the bit.
-// r must be below the block total.
+// Slot of flat word f in the transposed staging layout (kWpt words per thread,
+// 16-byte vector v of thread t at vector index v * kThreads + t).
 template <int kWpt>
-__device__ __forceinline__ uint32_t code_of_rank(uint32_t r, const uint32_t* s_excl, const uint32_t* s_words, int nw,
-                                                 uint32_t code_stride) {
-  int t = 0;
+__device__ __forceinline__ int staged_index(int f) {
+  const int t = f / kWpt, r = f - t * kWpt;
+  return ((r >> 2) * kThreads + t) * 4 + (r & 3);
+}
+
+// Unit code (request * code_stride + row) of rank r, resolved by the 16 lanes
+// of one half-warp at once (both halves call it together, each for its own
+// rank; r below the block total). Four levels, each a shared-memory read per
+// lane and a ballot: the warp of the block scan that holds r (16 inclusive
+// warp prefixes s_wincl), the thread within that warp (its 32 exclusive
+// prefixes s_excl), the word within that thread's kWpt staged words (their
+// exclusive prefixes s_pre), the bit within the word. A single lane searching
+// alone spent about 1,700 cycles in dependent steps; this takes a few
+// ballots.
+template <int kWpt>
+__device__ __forceinline__ uint32_t code_of_rank_halfwarp(uint32_t r, const uint32_t* s_wincl, const uint32_t* s_excl,
+                                                          const uint32_t* s_words, const uint32_t* s_pre, int batch,
+                                                          int nw, uint32_t code_stride) {
+  const int lane = threadIdx.x & 31, hl = lane & 15, sh = lane & 16;
+  // level 1: warps whose inclusive prefix is <= r lie wholly below rank r
+  const unsigned m1 = __ballot_sync(FULL_MASK, s_wincl[hl] <= r);
+  const int W = __popc((m1 >> sh) & 0xffffu);
+  // level 2: threads of warp W whose first rank is <= r; the last one holds r
+  const unsigned m2a = __ballot_sync(FULL_MASK, s_excl[32 * W + hl] <= r);
+  const unsigned m2b = __ballot_sync(FULL_MASK, s_excl[32 * W + 16 + hl] <= r);
+  const int t = 32 * W + __popc((m2a >> sh) & 0xffffu) + __popc((m2b >> sh) & 0xffffu) - 1;
+  // level 3: the last non-empty word of thread t that starts at or below r
+  int q = -1;
+  uint32_t word = 0u, base = 0u;
 #pragma unroll
-  for (int step = kThreads / 2; step > 0; step >>= 1)
-    if (s_excl[t + step] <= r) t += step;
-  uint32_t local = r - s_excl[t];
-  uint32_t word = 0u;
-  int f = t * kWpt;
-  bool found = false;
-#pragma unroll
-  for (int v = 0; v < kWpt / 4; ++v) {
-    const uint4 x = reinterpret_cast<const uint4*>(s_words)[v * kThreads + t];
-    const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t pc = (uint32_t)__popc(w4[q]);
-      if (!found) {
-        if (local < pc) {
-          found = true;
-          word = w4[q];
-          f = t * kWpt + 4 * v + q;
-        } else {
-          local -= pc;
-        }
-      }
+  for (int part = 0; part < kWpt / 16; ++part) {
+    const int si = staged_index<kWpt>(t * kWpt + 16 * part + hl);
+    const uint32_t wd = s_words[si], pre = s_pre[si];
+    const unsigned m3 = (__ballot_sync(FULL_MASK, wd != 0u && pre <= r) >> sh) & 0xffffu;
+    const int src = m3 ? 31 - __clz(m3) : -1;
+    const uint32_t w_src = __shfl_sync(FULL_MASK, wd, sh + (src < 0 ? 0 : src));
+    const uint32_t p_src = __shfl_sync(FULL_MASK, pre, sh + (src < 0 ? 0 : src));
+    if (src >= 0) {
+      q = 16 * part + src;
+      word = w_src;
+      base = p_src;
     }
   }
-  const int bit = (int)__fns(word, 0u, (int)local + 1);
-  const int b = f / nw, w = f - b * nw;
+  // level 4: the set bit of that word whose rank is r (lane hl tests bits hl and hl + 16)
+  const uint32_t below_lo = word & ((1u << hl) - 1u);
+  const uint32_t below_hi = word & ((1u << (hl + 16)) - 1u);
+  const bool is_lo = ((word >> hl) & 1u) && base + (uint32_t)__popc(below_lo) == r;
+  const bool is_hi = ((word >> (hl + 16)) & 1u) && base + (uint32_t)__popc(below_hi) == r;
+  const unsigned m4lo = (__ballot_sync(FULL_MASK, is_lo) >> sh) & 0xffffu;
+  const unsigned m4hi = (__ballot_sync(FULL_MASK, is_hi) >> sh) & 0xffffu;
+  const int bit = m4lo ? __ffs(m4lo) - 1 : 16 + __ffs(m4hi) - 1;
+  const int f = t * kWpt + (q < 0 ? 0 : q);
+  const int b = batch == 1 ? 0 : f / nw, w = f - b * nw;
   return (uint32_t)b * code_stride + (uint32_t)(w * 32 + bit);
 }
 
 // Greedy streaming of the CTA's units of rank [rbase, rbase + n) with no unit
-// list: warp w takes units w, w + 16, w + 32, ... two rows at a time, and
-// before every 16 such pairs its 32 lanes resolve those 32 units' codes at
-// once (code_of_rank; without a mask the code follows from the rank). No
-// block barrier between the scan and the first row load.
+// list: warp w takes the pairs (w + 32k, w + 32k + 16); its two half-warps
+// resolve a pair's two codes (code_of_rank_halfwarp; without a mask the code
+// follows from the rank). The codes of the next pair are resolved while the
+// current pair's row loads are in flight, so only the first pair's search is
+// on the critical path.
+template <int kWpt>
+__device__ __forceinline__ uint32_t pair_code(const RowSparseParams& p, uint64_t rbase, int i, bool has2, bool has_mask,
+                                              const uint32_t* s_wincl, const uint32_t* s_excl,
+                                              const uint32_t* s_words, const uint32_t* s_pre, uint32_t code_stride) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t r = rbase + (uint64_t)((lane >= 16 && has2) ? i + kWarps : i);
+  if (has_mask)
+    return code_of_rank_halfwarp<kWpt>((uint32_t)r, s_wincl, s_excl, s_words, s_pre, p.batch, p.nw, code_stride);
+  const uint32_t b = (uint32_t)(r / (uint64_t)p.vocab);
+  return b * code_stride + (uint32_t)(r - (uint64_t)b * p.vocab);
+}
+
 template <typename T, int kWpt>
 __device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uint64_t rbase, int n, bool has_mask,
-                                                   const uint32_t* s_excl, const uint32_t* s_words,
+                                                   const uint32_t* s_wincl, const uint32_t* s_excl,
+                                                   const uint32_t* s_words, const uint32_t* s_pre,
                                                    uint32_t code_stride, const void* s_h, bool want_top,
                                                    unsigned long long* s_keys) {
   using Bits = typename DTypeTraits<T>::Bits;
@@ -579,57 +615,51 @@ __device__ __forceinline__ void stream_rows_ranked(const RowSparseParams& p, uin
   const int H = p.hidden_dim, nvec = H / DTypeTraits<T>::kPerVec;
   RunningTop top;
   RunningSample rs;
-  for (int g0 = warp; g0 < n; g0 += 32 * kWarps) {
-    const int my_i = g0 + lane * kWarps;
-    uint32_t my_code = 0u;
-    if (my_i < n) {
-      const uint64_t r = rbase + (uint64_t)my_i;
-      if (has_mask) {
-        my_code = code_of_rank<kWpt>((uint32_t)r, s_excl, s_words, p.nw, code_stride);
-      } else {
-        const uint32_t b = (uint32_t)(r / (uint64_t)p.vocab);
-        my_code = b * code_stride + (uint32_t)(r - (uint64_t)b * p.vocab);
+  int i = warp;
+  uint32_t my_code = i < n ? pair_code<kWpt>(p, rbase, i, i + kWarps < n, has_mask, s_wincl, s_excl, s_words, s_pre,
+                                             code_stride)
+                           : 0u;
+  while (i < n) {
+    const int j = i + kWarps;
+    const bool has2 = j < n;
+    const int i_next = i + 2 * kWarps;
+    const uint32_t ca = __shfl_sync(FULL_MASK, my_code, 0);
+    const uint32_t cb = __shfl_sync(FULL_MASK, my_code, 16);
+    const int ba = (int)(ca / code_stride), va = (int)(ca - (uint32_t)ba * code_stride);
+    const int bb = (int)(cb / code_stride), vb = (int)(cb - (uint32_t)bb * code_stride);
+    const uint4* wa = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)va * p.weight_stride);
+    const uint4* wb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)vb * p.weight_stride);
+    const uint4* ha = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)ba * H);
+    const uint4* hb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)bb * H);
+    float acc_a = 0.f, acc_b = 0.f;
+    for (int base = 0; base < nvec; base += 32 * kUnroll) {
+      uint4 ra[kUnroll], rb[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int e = base + u * 32 + lane;
+        ra[u] = e < nvec ? ld_stream_v4(wa + e) : make_uint4(0, 0, 0, 0);
+        rb[u] = (has2 && e < nvec) ? ld_stream_v4(wb + e) : make_uint4(0, 0, 0, 0);
       }
-    }
-    for (int k = 0; k < 32; k += 2) {
-      const int i = g0 + k * kWarps;
-      if (i >= n) break;
-      const int j = i + kWarps;
-      const bool has2 = j < n;
-      const uint32_t ca = __shfl_sync(FULL_MASK, my_code, k);
-      const uint32_t cb = has2 ? __shfl_sync(FULL_MASK, my_code, k + 1) : ca;
-      const int ba = (int)(ca / code_stride), va = (int)(ca - (uint32_t)ba * code_stride);
-      const int bb = (int)(cb / code_stride), vb = (int)(cb - (uint32_t)bb * code_stride);
-      const uint4* wa = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)va * p.weight_stride);
-      const uint4* wb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(p.weight) + (int64_t)vb * p.weight_stride);
-      const uint4* ha = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)ba * H);
-      const uint4* hb = reinterpret_cast<const uint4*>(static_cast<const Bits*>(s_h) + (size_t)bb * H);
-      float acc_a = 0.f, acc_b = 0.f;
-      for (int base = 0; base < nvec; base += 32 * kUnroll) {
-        uint4 ra[kUnroll], rb[kUnroll];
+      if (base == 0 && i_next < n)  // next pair's codes while these loads are in flight
+        my_code = pair_code<kWpt>(p, rbase, i_next, i_next + kWarps < n, has_mask, s_wincl, s_excl, s_words, s_pre,
+                                  code_stride);
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const int e = base + u * 32 + lane;
-          ra[u] = e < nvec ? ld_stream_v4(wa + e) : make_uint4(0, 0, 0, 0);
-          rb[u] = (has2 && e < nvec) ? ld_stream_v4(wb + e) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const int e = base + u * 32 + lane;
-          if (e < nvec) {
-            acc_a = dot_vec<T>(ra[u], ha[e], acc_a);
-            if (has2) acc_b = dot_vec<T>(rb[u], hb[e], acc_b);
-          }
+      for (int u = 0; u < kUnroll; ++u) {
+        const int e = base + u * 32 + lane;
+        if (e < nvec) {
+          acc_a = dot_vec<T>(ra[u], ha[e], acc_a);
+          if (has2) acc_b = dot_vec<T>(rb[u], hb[e], acc_b);
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        acc_a += __shfl_xor_sync(FULL_MASK, acc_a, o);
-        acc_b += __shfl_xor_sync(FULL_MASK, acc_b, o);
-      }
-      if (lane == 0) emit_unit<T, false>(p, ba, va, rbase + (uint64_t)i, acc_a, want_top, top, s_keys, rs, 0);
-      if (lane == 1 && has2) emit_unit<T, false>(p, bb, vb, rbase + (uint64_t)j, acc_b, want_top, top, s_keys, rs, 0);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc_a += __shfl_xor_sync(FULL_MASK, acc_a, o);
+      acc_b += __shfl_xor_sync(FULL_MASK, acc_b, o);
+    }
+    if (lane == 0) emit_unit<T, false>(p, ba, va, rbase + (uint64_t)i, acc_a, want_top, top, s_keys, rs, 0);
+    if (lane == 1 && has2) emit_unit<T, false>(p, bb, vb, rbase + (uint64_t)j, acc_b, want_top, top, s_keys, rs, 0);
+    i = i_next;
   }
   if (lane < 2) top.flush(s_keys);
 }
@@ -665,13 +695,6 @@ __host__ __device__ inline StagedLayout staged_layout(int batch, int hidden_dim,
   return l;
 }
 
-// Slot of flat word f in the transposed staging layout (kWpt words per thread,
-// 16-byte vector v of thread t at vector index v * kThreads + t).
-template <int kWpt>
-__device__ __forceinline__ int staged_index(int f) {
-  const int t = f / kWpt, r = f - t * kWpt;
-  return ((r >> 2) * kThreads + t) * 4 + (r & 3);
-}
 
 // kV 16-byte mask vectors (4 * kV words) per thread: the whole flat
 // (request, word) mask lives in the CTA's registers, kThreads * 4 * kV words.
@@ -796,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
       pr.w = run;
       run += __popc(wd[4 * v + 3]);
       reinterpret_cast<uint4*>(s_words)[v * kThreads + tid] = make_uint4(wd[4 * v], wd[4 * v + 1], wd[4 * v + 2], wd[4 * v + 3]);
-      if constexpr (kSample) reinterpret_cast<uint4*>(s_pre)[v * kThreads + tid] = pr;
+      reinterpret_cast<uint4*>(s_pre)[v * kThreads + tid] = pr;
     }
   }
   if (p.offsets != nullptr && cta == 0) {
@@ -816,54 +839,42 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
 
   // -inf over the illegal entries of this CTA's output slice, issued before
   // the rows so that the stores drain while the row loads are in flight
-  if (!kSample || (p.logits && has_mask)) __syncthreads();  // staged words (and prefixes) complete
+  if (!kSample || (p.logits && has_mask)) __syncthreads();  // staged words and prefixes complete
   if (p.logits && has_mask)
     fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_words[staged_index<kWpt>((int)f)]; });
-  const uint64_t lo = total * (uint64_t)cta / (uint64_t)G;
-  const uint64_t hi = total * (uint64_t)(cta + 1) / (uint64_t)G;
+  // this CTA's ranks [lo, hi) (32-bit arithmetic whenever it cannot overflow)
+  uint64_t lo, hi;
+  if (total <= 0xffffffffull / (uint64_t)G) {
+    lo = (uint32_t)total * (uint32_t)cta / (uint32_t)G;
+    hi = (uint32_t)total * (uint32_t)(cta + 1) / (uint32_t)G;
+  } else {
+    lo = total * (uint64_t)cta / (uint64_t)G;
+    hi = total * (uint64_t)(cta + 1) / (uint64_t)G;
+  }
   const uint32_t code_stride = (uint32_t)nw * 32u;
   if constexpr (!kSample) {
-    // greedy: each warp resolves its own units from the prefixes, no unit list
-    stream_rows_ranked<T, kWpt>(p, lo, (int)(hi - lo), has_mask, s_excl, s_words, code_stride, s_h, want_top, s_keys);
-    if (want_top) {
-      if (polled_merge_ok(p))
-        finalize_top1_polled(p, s_keys, reinterpret_cast<uint32_t*>(s_misc + 1));
-      else
-        finalize_top1<false>(p, s_keys, s_misc, want_top);
-    }
+    // greedy: the half-warps resolve each pair's units from the prefixes, no unit list
+    stream_rows_ranked<T, kWpt>(p, lo, (int)(hi - lo), has_mask, s_warp, s_excl, s_words, s_pre, code_stride, s_h,
+                                want_top, s_keys);
   } else {
   for (uint64_t rbase = lo; rbase < hi; rbase += kListCap) {
     const uint64_t rend = min(hi, rbase + (uint64_t)kListCap);
     const int n = (int)(rend - rbase);
-    // ---- 4. extraction: the owners of ranks rbase and rend - 1 publish the
-    //         word range, then every thread emits the units of one word ------
+    // ---- 4. extraction: the threads holding ranks rbase and rend - 1 publish
+    //         themselves (a register test, no per-word search), then every
+    //         thread takes one word of their words and lists its units ------
     if (has_mask) {
       const uint32_t rb32 = (uint32_t)rbase, re32 = (uint32_t)rend;  // ranks < 2^32
-      if (excl <= rb32 && rb32 < excl + cnt) {
-        uint32_t r = excl;
-#pragma unroll
-        for (int j = 0; j < kWpt; ++j) {
-          const uint32_t pc = __popc(wd[j]);
-          if (r <= rb32 && rb32 < r + pc) s_misc[2] = f0 + j;
-          r += pc;
-        }
-      }
-      if (excl <= re32 - 1 && re32 - 1 < excl + cnt) {
-        uint32_t r = excl;
-#pragma unroll
-        for (int j = 0; j < kWpt; ++j) {
-          const uint32_t pc = __popc(wd[j]);
-          if (r <= re32 - 1 && re32 - 1 < r + pc) s_misc[3] = f0 + j;
-          r += pc;
-        }
-      }
+      if (excl <= rb32 && rb32 < excl + cnt) s_misc[2] = tid;
+      if (excl <= re32 - 1 && re32 - 1 < excl + cnt) s_misc[3] = tid;
       __syncthreads();
-      const int fa = s_misc[2], fb = s_misc[3];
-      for (int f = fa + tid; f <= fb; f += kThreads) {
+      const int fa = s_misc[2] * kWpt, fb = s_misc[3] * kWpt + kWpt;
+      for (int f = fa + tid; f < fb; f += kThreads) {
         const int si = staged_index<kWpt>(f);
         uint32_t word = s_words[si];
         uint32_t r = s_pre[si];
-        const int b = f / nw, w = f - b * nw;
+        if (word == 0u || r >= re32 || r + (uint32_t)__popc(word) <= rb32) continue;
+        const int b = B == 1 ? 0 : f / nw, w = f - b * nw;
         while (word) {
           const int bit = __ffs(word) - 1;
           word &= word - 1;
@@ -885,10 +896,13 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
     round_stats<kSample>(sample_smem(s_keys, B), s_list, n, code_stride);
     __syncthreads();
   }
+  }
 
   // ---- 7. top-1 ------------------------------------------------------------
-  finalize_top1<kSample>(p, s_keys, s_misc, want_top);
-  }
+  if (!kSample && want_top && polled_merge_ok(p))
+    finalize_top1_polled(p, s_keys, reinterpret_cast<uint32_t*>(s_misc + 1));
+  else
+    finalize_top1<kSample>(p, s_keys, s_misc, want_top);
 }
 
 // ===========================================================================

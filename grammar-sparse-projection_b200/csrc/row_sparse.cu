@@ -540,8 +540,9 @@ __device__ __forceinline__ int staged_index(int f) {
 // rank; r below the block total). Four levels, each a shared-memory read per
 // lane and a ballot: the warp of the block scan that holds r (16 inclusive
 // warp prefixes s_wincl), the thread within that warp (its 32 exclusive
-// prefixes s_excl), the word within that thread's kWpt staged words (their
-// exclusive prefixes s_pre), the bit within the word. A single lane searching
+// prefixes s_excl, relative to the warp's first rank), the word within that
+// thread's kWpt staged words (their exclusive prefixes s_pre, also relative
+// to the warp), the bit within the word. A single lane searching
 // alone spent about 1,700 cycles in dependent steps; this takes a few
 // ballots.
 template <int kWpt>
@@ -552,6 +553,7 @@ __device__ __forceinline__ uint32_t code_of_rank_halfwarp(uint32_t r, const uint
   // level 1: warps whose inclusive prefix is <= r lie wholly below rank r
   const unsigned m1 = __ballot_sync(FULL_MASK, s_wincl[hl] <= r);
   const int W = __popc((m1 >> sh) & 0xffffu);
+  r -= W > 0 ? s_wincl[W - 1] : 0u;  // rank within warp W (s_excl and s_pre are warp-relative)
   // level 2: threads of warp W whose first rank is <= r; the last one holds r
   const unsigned m2a = __ballot_sync(FULL_MASK, s_excl[32 * W + hl] <= r);
   const unsigned m2b = __ballot_sync(FULL_MASK, s_excl[32 * W + 16 + hl] <= r);
@@ -792,36 +794,65 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
   for (int b = tid; b < B; b += kThreads) s_keys[b] = 0ull;
   if constexpr (kSample) sample_smem_init(p, s_keys);
 
+  // ---- 2. per-thread counts; words and warp-relative rank prefixes staged ---
+  // The words and their exclusive rank prefixes go to shared memory before
+  // the scan's first barrier, so that extraction and the -inf fill can run one
+  // word per thread without a barrier of their own. The prefixes are relative
+  // to the thread's warp (the warp's base is known only after the scan):
+  // s_excl[t] is thread t's first rank within its warp, s_pre the same per
+  // word; s_warp ends as the inclusive prefix of the warp totals. Layout of
+  // the words: the 16-byte vector v of thread t at vector index
+  // v * kThreads + t (conflict-free stores); staged_index() maps a flat word
+  // index to its slot.
+  uint32_t pc[kWpt];
   uint32_t cnt = 0;
 #pragma unroll
-  for (int j = 0; j < kWpt; ++j) cnt += __popc(wd[j]);
-
-  // ---- 3. one block scan of per-thread counts -----------------------------
-  uint32_t tot;
-  const uint32_t excl = block_exclusive_scan(cnt, s_warp, &tot);  // contains __syncthreads
-  const uint64_t total = has_mask ? (uint64_t)tot : (uint64_t)B * V;
-  // words and their exclusive rank prefixes -> shared memory, so that
-  // extraction and the -inf fill run one word per thread. Layout: the 16-byte
-  // vector v of thread t sits at vector index v * kThreads + t (conflict-free
-  // stores); staged_index() maps a flat word index to its slot.
-  if constexpr (!kSample) s_excl[tid] = excl;
+  for (int j = 0; j < kWpt; ++j) {
+    pc[j] = __popc(wd[j]);
+    cnt += pc[j];
+  }
+  uint32_t incl_w = cnt;  // inclusive scan within the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(FULL_MASK, incl_w, o);
+    if ((tid & 31) >= o) incl_w += t;
+  }
+  const uint32_t excl_w = incl_w - cnt;
+  if ((tid & 31) == 31) s_warp[tid >> 5] = incl_w;
+  s_excl[tid] = excl_w;
   if (has_mask) {
-    uint32_t run = excl;
+    uint32_t run = excl_w;
 #pragma unroll
     for (int v = 0; v < kV; ++v) {
       uint4 pr;
       pr.x = run;
-      run += __popc(wd[4 * v]);
+      run += pc[4 * v];
       pr.y = run;
-      run += __popc(wd[4 * v + 1]);
+      run += pc[4 * v + 1];
       pr.z = run;
-      run += __popc(wd[4 * v + 2]);
+      run += pc[4 * v + 2];
       pr.w = run;
-      run += __popc(wd[4 * v + 3]);
+      run += pc[4 * v + 3];
       reinterpret_cast<uint4*>(s_words)[v * kThreads + tid] = make_uint4(wd[4 * v], wd[4 * v + 1], wd[4 * v + 2], wd[4 * v + 3]);
       reinterpret_cast<uint4*>(s_pre)[v * kThreads + tid] = pr;
     }
   }
+  // ---- 3. scan of the warp totals --------------------------------------------
+  __syncthreads();
+  if (tid < 32) {
+    uint32_t x = tid < kWarps ? s_warp[tid] : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(FULL_MASK, x, o);
+      if (tid >= o) x += t;
+    }
+    if (tid < kWarps) s_warp[tid] = x;
+  }
+  __syncthreads();
+  const uint32_t warp_base = (tid >> 5) > 0 ? s_warp[(tid >> 5) - 1] : 0u;
+  const uint32_t excl = warp_base + excl_w;  // this thread's first rank
+  const uint32_t tot = s_warp[kWarps - 1];
+  const uint64_t total = has_mask ? (uint64_t)tot : (uint64_t)B * V;
   if (p.offsets != nullptr && cta == 0) {
     if (has_mask) {
       uint32_t run = excl;
@@ -839,7 +870,6 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
 
   // -inf over the illegal entries of this CTA's output slice, issued before
   // the rows so that the stores drain while the row loads are in flight
-  if (!kSample || (p.logits && has_mask)) __syncthreads();  // staged words and prefixes complete
   if (p.logits && has_mask)
     fill_illegal<T>(p, w_lo, w_hi, [&](int64_t f, int, int) { return s_words[staged_index<kWpt>((int)f)]; });
   // this CTA's ranks [lo, hi) (32-bit arithmetic whenever it cannot overflow)
@@ -872,7 +902,8 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_staged_kernel(const Ro
       for (int f = fa + tid; f < fb; f += kThreads) {
         const int si = staged_index<kWpt>(f);
         uint32_t word = s_words[si];
-        uint32_t r = s_pre[si];
+        const int fw = (f / kWpt) >> 5;  // warp of the thread holding word f
+        uint32_t r = s_pre[si] + (fw > 0 ? s_warp[fw - 1] : 0u);
         if (word == 0u || r >= re32 || r + (uint32_t)__popc(word) <= rb32) continue;
         const int b = B == 1 ? 0 : f / nw, w = f - b * nw;
         while (word) {

@@ -61,6 +61,9 @@ constexpr size_t kStagedSmemMax = 200 * 1024;  // list + keys + mask slice + hid
 // (batch 2 at V=248,320, 15,520 words, measured 14.2 us on the staged kernel
 // against 16.1 us on the cooperative one.)
 constexpr int64_t kCoopMinWords = 16384;
+// Logits bytes per CTA above which the cooperative kernel writes its -inf
+// fill during the count wait rather than after publishing its units.
+constexpr int64_t kEarlyFillBytes = 64 * 1024;
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -1311,12 +1314,19 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowS
     __threadfence();
     atom_add_release_gpu(p.published, 1u);
   }
-  // While the other counts arrive, warps 1.. (warp 0 holds the poller) write
-  // -inf over the own slice's illegal entries (illegal and legal entries are
-  // disjoint, so the order does not matter). Prefetching the slice's legal
-  // rows into L2 here was measured: it did not shorten the kernel.
+  // While the other counts arrive, warps 1.. (warp 0 holds the poller) could
+  // write -inf over the own slice's illegal entries; in list mode the fence
+  // that publishes the CTA's units then waits for those stores too. So the
+  // fill is issued here only when it is large (more than kEarlyFillBytes of
+  // logits per CTA, where it would delay the rows more than the fence);
+  // otherwise it runs beside the flag waits (list mode) or after the rows.
+  // (Measured, V=248,320: deferred, batch 4 / 8 / 16 gained 0.3-0.5 us and
+  // batch 32 lost 0.4 us.) Prefetching the slice's legal rows into L2 during
+  // the count wait did not shorten the kernel.
   const int pollers = 32;
-  const bool filled_early = p.logits != nullptr && max_slice <= kChunk;
+  const bool filled_early = p.logits != nullptr && max_slice <= kChunk &&
+                            (int64_t)B * p.vocab * (int64_t)sizeof(typename DTypeTraits<T>::Bits) >
+                                (int64_t)kEarlyFillBytes * G;
   if (filled_early && my_hi > my_lo)
     fill_illegal<T>(p, my_lo, my_hi, [&](int64_t f, int, int) { return s_words[f - my_lo]; }, pollers,
                     kThreads - pollers);
@@ -1373,8 +1383,12 @@ __global__ void __launch_bounds__(kThreads, 1) row_sparse_coop_kernel(const RowS
         __threadfence();
         st_release_gpu(p.slice_ready + (size_t)cta * kFlagStride, 1u);
       }
-      if (p.logits != nullptr && !filled_early && my_hi > my_lo)
-        fill_illegal<T>(p, my_lo, my_hi, [&](int64_t f, int, int) { return s_words[f - my_lo]; });
+    }
+    // the -inf fill of the own slice runs beside the flag waits (threads below
+    // the first whole warp past the grid poll flags, the others fill)
+    if (p.logits != nullptr && !filled_early && my_hi > my_lo && !aborted) {
+      const int t0 = (G + 31) / 32 * 32 < kThreads ? (G + 31) / 32 * 32 : 0;
+      fill_illegal<T>(p, my_lo, my_hi, [&](int64_t f, int, int) { return s_words[f - my_lo]; }, t0, kThreads - t0);
     }
     // ---- 4. wait for the slices this CTA's ranks come from; stream ---------
     if (lo < hi) {

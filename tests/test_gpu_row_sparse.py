@@ -260,6 +260,27 @@ def test_full_size_density_sweep(cuda_device, clustered):
         assert ti.item() == logits.argmax(-1).item()
 
 
+@pytest.mark.parametrize("clustered", [False, True])
+def test_batch1_mask_over_8192_words(cuda_device, clustered):
+    """Batch 1 with a vocabulary of more than 262,144 tokens (9,376 mask words,
+    a ragged last word): the staged kernel holds 32 mask words per thread, and
+    the half-warps resolve each unit from two groups of 16 staged words."""
+    vocab, hidden = 300_007, 128
+    rng = np.random.default_rng(4242 + clustered)
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * np.float32(0.05)).half()
+    h = torch.from_numpy(rng.standard_normal((1, hidden), dtype=np.float32)).half()
+    wd, hd = w.to(cuda_device), h.to(cuda_device)
+    for density in (0.01, 0.10):
+        k = int(round(density * vocab))
+        mask = O.make_batch_mask(rng, 1, vocab, [k], clustered=clustered, max_runs=32)
+        mask[0, -1] |= np.int32(-1)  # bits beyond the vocabulary set: the kernel must ignore them
+        logits = torch.empty(1, vocab, device=cuda_device, dtype=torch.float16)
+        tv, ti, _ = _fused(hd, wd, torch.from_numpy(mask).to(cuda_device), logits)
+        exact = O.masked_logits_exact(h, w, mask)
+        _check(exact, logits, torch.float16, f"density={density}")
+        assert ti.item() == logits.argmax(-1).item()
+
+
 def test_no_bounded_wait_gave_up(cuda_device):
     """Every kernel above completed without giving up a bounded wait."""
     assert _native.workspace_error(cuda_device) == 0

@@ -17,14 +17,16 @@
 //      hidden states go to shared memory;
 //   2. (no prefetch: prefetching the CTA's own legal rows into L2 before the
 //      scan was measured slower than not doing it);
-//   3. one block-wide scan of per-thread popcounts gives every thread the
-//      rank of its first legal unit; words and per-word rank prefixes are
-//      staged in shared memory with 16-byte stores;
+//   3. the words and their rank prefixes (relative to the thread's warp) are
+//      staged in shared memory with 16-byte stores before the first barrier;
+//      one scan of the 16 warp totals gives the warps' bases;
 //   4. -inf is written over the illegal entries of the CTA's slice of the
 //      output;
-//   5. the two threads holding the CTA's first and last rank publish
-//      themselves (a test on their own rank range, no per-word search), and
-//      every thread lists the units of one word of theirs in shared memory;
+//   5. greedy: each warp takes pairs of the CTA's units, whose codes its two
+//      half-warps resolve by ballots over the staged prefixes (warp, thread,
+//      word, bit), the next pair's while the current rows load; sampler: the
+//      two threads holding the CTA's first and last rank publish themselves
+//      and every thread lists the units of one word of theirs;
 //   6. each warp streams two whole rows at a time with L1-bypassing 16-byte
 //      loads, dots them against h in shared memory and reduces with shuffles;
 //   7. greedy top-1 keys (rounded value, inverted index) are kept per warp and

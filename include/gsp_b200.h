@@ -28,6 +28,13 @@
  *   - `workspace` must be at least gsp_workspace_bytes(batch, vocab) bytes,
  *     zero-filled once before first use; every call leaves it zero-filled
  *     again. Calls that run concurrently must not share one workspace.
+ *     Exception: bytes 4..7 hold an int32 error word that kernels set (and
+ *     never clear) when a bounded wait ran out instead of hanging: 1 a
+ *     multi-CTA kernel's wait for its CTAs' counts, flags or pipeline stages,
+ *     2 a corrupt unit code found (stale state from an earlier failed call),
+ *     3 the cross-rank top-1 exchange, 4 the single-GPU top-1 slot merge
+ *     (then no token is reported: top_index -1). After a non-zero word the
+ *     caller re-zeroes the whole workspace before its next call.
  *   - Returns GSP_OK or a negative GSP_ERR_* code; no exception or abort
  *     crosses the ABI. gsp_last_error() describes the last failure on the
  *     calling host thread.

@@ -341,8 +341,14 @@ __device__ __forceinline__ void finalize_top1_polled(const RowSparseParams& p, u
   __syncthreads();  // every warp's running key is in s_keys
   if ((int)blockIdx.x != G - 1) {
     for (int b = tid; b < B; b += blockDim.x) st_relaxed_gpu_u64(slots + (size_t)b * G + blockIdx.x, tag_key(s_keys[b], kSlotTag));
+    // This CTA is done: a programmatic dependent of this kernel may be
+    // scheduled once every CTA has got here (or exited). Its
+    // griddepcontrol.wait still waits for this whole grid and its memory.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     return;
   }
+  // the decoder's rows are done too; every other CTA it waits for has run
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   bool late = false;
   const uint64_t t0 = globaltimer_ns();
   for (int i = tid; i < B * (G - 1); i += blockDim.x) {

@@ -281,6 +281,26 @@ def test_batch1_mask_over_8192_words(cuda_device, clustered):
         assert ti.item() == logits.argmax(-1).item()
 
 
+def test_top1_merge_paths_agree(cuda_device):
+    """Global ids below 2^24 - 1 take the polled top-1 merge (self-tagged
+    per-CTA key slots); a vocabulary offset that reaches past it takes the
+    ticket merge. Both report the same token, shifted by the offset."""
+    vocab, hidden = 50_000, 256
+    rng = np.random.default_rng(91)
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * np.float32(0.05)).half().to(cuda_device)
+    h = torch.from_numpy(rng.standard_normal((2, hidden), dtype=np.float32)).half().to(cuda_device)
+    mask = torch.from_numpy(O.make_batch_mask(rng, 2, vocab, [400, 3000], clustered=True, max_runs=8)).to(cuda_device)
+    for b in (1, 2):
+        tv0, ti0, _ = _fused(h[:b], w, mask[:b])
+        for offset in (0, 1_000_000, 1 << 24, (1 << 24) - 40_000):
+            tv = torch.empty(b, device=cuda_device)
+            ti = torch.empty(b, device=cuda_device, dtype=torch.int64)
+            _native.row_sparse(h[:b], w, mask[:b], top_value=tv, top_index=ti, vocab_offset=offset)
+            assert torch.equal(ti, ti0 + offset), (b, offset)
+            assert torch.equal(tv, tv0), (b, offset)
+    assert _native.workspace_error(cuda_device) == 0
+
+
 def test_no_bounded_wait_gave_up(cuda_device):
     """Every kernel above completed without giving up a bounded wait."""
     assert _native.workspace_error(cuda_device) == 0

@@ -31,8 +31,11 @@
 //                  order + row) reduced across the warp's 32 rows with a
 //                  transpose-reduce, widened to 64-bit global keys once per
 //                  request.
-//    Tiles are taken from the compacted list round-robin by CTA. The cross-CTA
-//    top-1 merge is the same last-arrival scheme as the row-sparse kernel.
+//    Tiles are taken from the compacted list round-robin by CTA; at set-up a
+//    CTA copies the whole list into its (still idle) A stages in the same
+//    round trip as the per-builder-block counts and picks its own tiles out
+//    of it. The cross-CTA top-1 merge is the last-arrival ticket scheme of
+//    the row-sparse kernel's batched path.
 //
 // "Swap-AB": the vocabulary is the MMA's M dimension and the (small) batch its N
 // dimension, so a batch of 2..256 requests fills a 128 x N tile.
@@ -63,6 +66,7 @@ constexpr int kMaxNpad = 256;
 constexpr int kMaxAcc = 4;          // TMEM accumulators (4 when npad <= 128, else 2)
 constexpr int kMaxUnits = kMaxNpad / 64;  // 32-column units per epilogue warp
 constexpr int kMaxStages = 8;
+constexpr int kMaxMine = 64;  // tiles per CTA that the set-up can list in shared memory
 constexpr uint32_t kABytes = kTileRows * kTileK * 2;  // 16 KB
 
 struct GemmConfig {
@@ -72,12 +76,13 @@ struct GemmConfig {
   int ntiles;    // ceil(V / 128)
   int nbuild;    // builder blocks (block mode)
   int acc_shift; // log2 of the accumulator count
+  int stage_list; // block mode: the set-up copies the tile list into shared memory
   uint32_t tmem_cols;
   uint32_t idesc;
 };
 
 struct GemmLayout {
-  size_t a, b, bars, tmem, keys, skeys, stats, pref, misc, total;
+  size_t a, b, bars, tmem, keys, skeys, stats, pref, mine, misc, total;
 };
 
 __host__ __device__ inline size_t align_to(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -101,6 +106,8 @@ __host__ __device__ inline GemmLayout gemm_layout(int npad, int stages, int nbui
   off = l.stats + 8 * (size_t)kMaxNpad;
   l.pref = align_to(off, 16);
   off = l.pref + 4 * ((size_t)nbuild + 1);
+  l.mine = align_to(off, 16);  // this CTA's tile ids (block mode, stage_list)
+  off = l.mine + 4 * (size_t)kMaxMine;
   l.misc = align_to(off, 16);
   off = l.misc + 16;
   l.total = align_to(off, 1024);
@@ -117,8 +124,11 @@ __device__ __forceinline__ int list_slot(const GemmConfig& c, const int* s_pref,
   return lo * kBuilderTiles + (pos - s_pref[lo]);
 }
 
-__device__ __forceinline__ int tile_at(const BlockGemmParams& p, const GemmConfig& c, const int* s_pref, int pos) {
-  return p.dense ? pos : p.tile_list[list_slot(c, s_pref, pos)];
+// Tile id of compacted position `pos`, the CTA's i-th tile.
+__device__ __forceinline__ int tile_at(const BlockGemmParams& p, const GemmConfig& c, const int* s_pref,
+                                       const int* s_mine, int pos, int i) {
+  if (p.dense) return pos;
+  return c.stage_list ? s_mine[i] : p.tile_list[list_slot(c, s_pref, pos)];
 }
 
 // -inf over every request's outputs in the inactive 128-row tiles
@@ -308,6 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   unsigned long long* s_skeys = reinterpret_cast<unsigned long long*>(smem + L.skeys);
   unsigned long long* s_stats = reinterpret_cast<unsigned long long*>(smem + L.stats);
   int* s_pref = reinterpret_cast<int*>(smem + L.pref);
+  int* s_mine = reinterpret_cast<int*>(smem + L.mine);
   int* s_misc = reinterpret_cast<int*>(smem + L.misc);  // [0] abort, [1] last-CTA flag
   volatile int* abort_flag = s_misc;
 
@@ -346,20 +357,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Everything above overlaps the tile builder; from here on its outputs (and
   // the inactive-tile -inf fill) are complete and visible.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (!p.dense && warp == 2) {
-    // exclusive prefix of the builder blocks' active-tile counts
-    int carry = 0;
-    for (int j0 = 0; j0 < c.nbuild; j0 += 32) {
-      const int j = j0 + lane;
-      const int v = j < c.nbuild ? p.tile_counts[j] : 0;
-      int incl = v;
+  if (!p.dense && c.stage_list && warp != 2) {
+    // The whole compacted list into shared memory, in the same round trip as
+    // the counts that warp 2 reads (the A stages are idle until the
+    // producer's first copy); the CTA picks its own tiles out of it below.
+    int* s_list = reinterpret_cast<int*>(s_a);
+    const int t = warp < 2 ? tid : tid - 32, nt = kGemmThreads - 32;
+    const int n = c.ntiles;
+    if ((reinterpret_cast<uintptr_t>(p.tile_list) & 15) == 0) {
+      const int4* src = reinterpret_cast<const int4*>(p.tile_list);
+      int4* dst = reinterpret_cast<int4*>(s_list);
+      const int n4 = n / 4;
+      for (int i0 = t; i0 < n4; i0 += 4 * nt) {
+        int4 v[4];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(FULL_MASK, incl, o);
-        if (lane >= o) incl += t;
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * nt < n4) v[u] = src[i0 + u * nt];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * nt < n4) dst[i0 + u * nt] = v[u];
       }
-      if (j < c.nbuild) s_pref[j] = carry + incl - v;
-      carry += __shfl_sync(FULL_MASK, incl, 31);
+      for (int j = n4 * 4 + t; j < n; j += nt) s_list[j] = p.tile_list[j];
+    } else {
+      for (int j = t; j < n; j += nt) s_list[j] = p.tile_list[j];
+    }
+  }
+  if (!p.dense && warp == 2) {
+    // exclusive prefix of the builder blocks' active-tile counts; up to 256
+    // counts are loaded before the first is used (one round trip)
+    constexpr int kPre = 8;
+    int carry = 0;
+    for (int j00 = 0; j00 < c.nbuild; j00 += 32 * kPre) {
+      int v[kPre];
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        const int j = j00 + u * 32 + lane;
+        v[u] = j < c.nbuild ? p.tile_counts[j] : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        const int j = j00 + u * 32 + lane;
+        int incl = v[u];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(FULL_MASK, incl, o);
+          if (lane >= o) incl += t;
+        }
+        if (j < c.nbuild) s_pref[j] = carry + incl - v[u];
+        carry += __shfl_sync(FULL_MASK, incl, 31);
+      }
     }
     if (lane == 0) s_pref[c.nbuild] = carry;
   }
@@ -368,13 +414,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem_base = *s_tmem;
   const int total = p.dense ? c.ntiles : s_pref[c.nbuild];
+  if (!p.dense && c.stage_list) {
+    // this CTA's tiles, compacted positions cta, cta + G, ..., in order
+    const int* s_list = reinterpret_cast<const int*>(s_a);
+    for (int j = tid; j < c.nbuild; j += kGemmThreads) {
+      const int base = s_pref[j], cnt = s_pref[j + 1] - base;
+      int k = (cta - base) % G;
+      if (k < 0) k += G;
+      for (; k < cnt; k += G) s_mine[(base + k) / G] = s_list[j * kBuilderTiles + k];
+    }
+    // order these generic accesses of the A stages before the producer's
+    // first TMA write into them
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+  }
 
   if (warp == 0) {
     // ---- TMA producer -------------------------------------------------------
     if (lane == 0) {
       uint32_t g = 0;
-      for (int pos = cta; pos < total && !*abort_flag; pos += G) {
-        const int tile = tile_at(p, c, s_pref, pos);
+      for (int pos = cta, i = 0; pos < total && !*abort_flag; pos += G, ++i) {
+        const int tile = tile_at(p, c, s_pref, s_mine, pos, i);
         for (int kb = 0; kb < c.kblocks; ++kb, ++g) {
           const int s = (int)(g % (uint32_t)c.stages);
           const uint32_t use = g / (uint32_t)c.stages;
@@ -456,7 +516,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int pos = cta; pos < total; pos += G, ++i) {
       const int acc = i & ((1 << c.acc_shift) - 1);
       const uint32_t ause = (uint32_t)(i >> c.acc_shift);
-      const int tile = tile_at(p, c, s_pref, pos);
+      const int tile = tile_at(p, c, s_pref, s_mine, pos, i);
       const int row0 = tile * kTileRows + q * 32;
       const int word_idx = tile * 4 + q;  // mask word holding this warp's 32 rows
       // mask words first: their loads overlap the wait for the accumulator
@@ -606,7 +666,16 @@ __global__ void __launch_bounds__(kBuilderThreads) tile_builder_kernel(const Blo
     const int groups = kBuilderThreads / kBuilderTiles;
     const int t = t0 + lt;
     uint32_t any = 0u;
-    if (t < ntiles) {
+    if (t < ntiles && t * 4 + 4 <= nw && (reinterpret_cast<uintptr_t>(p.mask) & 15) == 0 && p.mask_stride % 4 == 0) {
+      // the tile's 4 words as one 16-byte load per request: a warp reads 512
+      // contiguous bytes per request
+#pragma unroll 4
+      for (int b = grp; b < B; b += groups) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(p.mask + (int64_t)b * p.mask_stride + t * 4));
+        any |= tail_clip(q.x, t * 4, V) | tail_clip(q.y, t * 4 + 1, V) | tail_clip(q.z, t * 4 + 2, V) |
+               tail_clip(q.w, t * 4 + 3, V);
+      }
+    } else if (t < ntiles) {
 #pragma unroll 4
       for (int b = grp; b < B; b += groups) {
         const uint32_t* row = p.mask + (int64_t)b * p.mask_stride;
@@ -687,11 +756,15 @@ cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream)
   while (cols < ((uint32_t)c.npad << c.acc_shift)) cols <<= 1;
   c.tmem_cols = cols;
   c.idesc = tc_idesc_f16((uint32_t)c.npad, sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value);
+  c.stage_list = 0;
   const size_t stage_bytes = kABytes + (size_t)c.npad * kTileK * 2;
   const size_t fixed = gemm_layout(c.npad, 0, c.nbuild).total + 1024 + 2048;
   c.stages = (int)std::min<size_t>(kMaxStages, ((size_t)smem_optin(dev) - fixed) / stage_bytes);
   if (c.stages < 2) return cudaErrorInvalidConfiguration;
   const GemmLayout L = gemm_layout(c.npad, c.stages, c.nbuild);
+  const int G = num_sms(dev);
+  // the whole list fits the A stages and each CTA's share fits s_mine
+  c.stage_list = (size_t)c.ntiles * 4 <= (size_t)c.stages * kABytes && (c.ntiles + G - 1) / G <= kMaxMine;
 
   const int bf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   CUtensorMap tw, th;
@@ -711,7 +784,7 @@ cudaError_t launch_chunk(const BlockGemmParams& p, int dev, cudaStream_t stream)
   const size_t smem_bytes = L.total + 1024;
   if ((err = raise_smem_limit(reinterpret_cast<const void*>(k), smem_bytes, dev)) != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms(dev));
+  cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;

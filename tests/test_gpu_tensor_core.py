@@ -170,5 +170,29 @@ def test_workspace_reuse_across_batch_sizes(cuda_device):
             assert torch.equal(tv, logits.float().gather(1, ti[:, None])[:, 0]), (batch, fn.__name__)
 
 
+@pytest.mark.parametrize("route", ["block", "dense"])
+def test_top1_with_vocab_offset_tensor_core(cuda_device, route):
+    """The fused top-1 of a vocabulary shard (global ids offset by up to and
+    past 2^24, as the vocabulary-parallel head reports them) at batches 1-33
+    is the argmax of the kernel's own logits, shifted by the offset."""
+    vocab, hidden = 50_000, 256
+    rng = np.random.default_rng(93)
+    w = torch.from_numpy(rng.standard_normal((vocab, hidden), dtype=np.float32) * np.float32(0.05)).half().to(cuda_device)
+    h = torch.from_numpy(rng.standard_normal((33, hidden), dtype=np.float32)).half().to(cuda_device)
+    ks = [int(k) for k in rng.integers(1, 3000, size=33)]
+    mask = torch.from_numpy(O.make_batch_mask(rng, 33, vocab, ks, clustered=True, max_runs=8)).to(cuda_device)
+    fn = _native.block_gemm if route == "block" else _native.dense_masked
+    for b in (1, 2, 8, 32, 33):
+        logits, tv0, ti0 = _run(fn, h[:b], w, mask[:b])
+        assert torch.equal(ti0, logits.argmax(-1)), (route, b)
+        for offset in (1_000_000, 1 << 24, (1 << 24) - 40_000):
+            tv = torch.empty(b, device=cuda_device)
+            ti = torch.empty(b, device=cuda_device, dtype=torch.int64)
+            fn(h[:b], w, mask[:b], top_value=tv, top_index=ti, vocab_offset=offset)
+            assert torch.equal(ti, ti0 + offset), (route, b, offset)
+            assert torch.equal(tv, tv0), (route, b, offset)
+    assert _native.workspace_error(cuda_device) == 0
+
+
 def test_no_bounded_wait_gave_up_tensor_core(cuda_device):
     assert _native.workspace_error(cuda_device) == 0

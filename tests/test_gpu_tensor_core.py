@@ -99,6 +99,7 @@ def test_batched_clustered_workload(cuda_device, batch):
     (3000, 128, 300, torch.float16),     # two batch chunks (256 + 44)
     (1025, 512, 33, torch.bfloat16),     # last tile holds one row
     (777, 12, 2, torch.float16),         # H % 8 != 0: row-sparse path
+    (1_300_000, 64, 3, torch.float16),   # over 64 tiles per CTA: tile ids read from the workspace list
 ])
 def test_edge_shapes(cuda_device, vocab, hidden, batch, dtype):
     rng = np.random.default_rng(vocab + batch)

@@ -362,7 +362,9 @@ __device__ __forceinline__ void finalize_top1_polled(const RowSparseParams& p, u
         ok = true;
         break;
       }
-      if ((int64_t)(globaltimer_ns() - t0) > kSlotWaitNs) break;
+      // the timer is read on every 32nd poll only: a read between two polls
+      // delays the next one
+      if ((it & 31u) == 31u && (int64_t)(globaltimer_ns() - t0) > kSlotWaitNs) break;
     }
     if (ok) {
       const unsigned long long k = untag_key(w);
